@@ -1,0 +1,39 @@
+// Launch builders for the non-structured ops of a plan.  Each returns a
+// closure that resolves device pointers from the runtime's buffers and
+// enqueues one kernel.  Defined in runtime.cpp.
+#pragma once
+
+#include <functional>
+#include <vector>
+
+#include "../kernels/kernels.h"
+#include "plan.h"
+
+namespace gawee {
+
+// B-operand packing source: element (b, k, n) of the logical [batch, K, N]
+// operand (see kern::PackBParams).
+struct PackSpec {
+  View src;
+  int64_t batch = 1, K = 0, N = 0;
+  int64_t sn = 0;
+  std::vector<int64_t> k_shape, k_st, k_valid;
+  std::vector<int64_t> batch_shape, batch_st;
+};
+
+namespace launch {
+using Fn = std::function<void(Runtime&, void*)>;
+Fn remap(kern::RemapParams rp, const View& in, const View& out);
+Fn reduce(const View& in, const View& out, const std::vector<bool>& red, bool mean, float count);
+Fn generic_reduce(const View& in, const View& out, const std::vector<bool>& red, const EProgram& body);
+Fn pool(kern::PoolParams pp, const View& in, const View& out);
+Fn softmax(const View& in, const View& out, int axis);
+Fn gather(const View& data, const View& idx, const View& out, int64_t pre, int64_t axis_len, int64_t nidx,
+          int64_t post);
+Fn gather_elements(const View& data, const View& idx, const View& out, int axis);
+Fn range(kern::RangeParams rp, const View& out);
+Fn topk(const View& in, const View& vals, const View& idxs, const View& used, int64_t k);
+Fn pack(const PackSpec& ps, int64_t ldk, int hi, int lo);
+}  // namespace launch
+
+}  // namespace gawee

@@ -1,0 +1,941 @@
+// libgawee_cuda runtime: device memory, launches, CUDA-graph replay and the
+// C ABI declared in include/gawee_cuda.h.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <array>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <sstream>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../../include/gawee_cuda.h"
+#include "../kernels/kernels.h"
+#include "ir.h"
+#include "launch.h"
+#include "plan.h"
+
+namespace gawee {
+
+struct CudaError : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+struct StatusError : std::runtime_error {
+  gawee_status code;
+  StatusError(gawee_status c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+#define GCHECK(expr)                                                                            \
+  do {                                                                                          \
+    cudaError_t e_ = (expr);                                                                    \
+    if (e_ != cudaSuccess) throw ::gawee::CudaError(std::string(#expr) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+struct alignas(64) TMap {
+  unsigned char b[128];
+};
+
+// ---------------------------------------------------------------------------
+// NCCL, loaded on first use so that the library itself has no NCCL dependency.
+// ---------------------------------------------------------------------------
+struct NcclApi {
+  ncclResult_t (*getUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*commInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*groupStart)() = nullptr;
+  ncclResult_t (*groupEnd)() = nullptr;
+  const char* (*errorString)(ncclResult_t) = nullptr;
+  bool ok = false;
+};
+
+static NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    api.getUniqueId = (decltype(api.getUniqueId))dlsym(h, "ncclGetUniqueId");
+    api.commInitRank = (decltype(api.commInitRank))dlsym(h, "ncclCommInitRank");
+    api.commDestroy = (decltype(api.commDestroy))dlsym(h, "ncclCommDestroy");
+    api.send = (decltype(api.send))dlsym(h, "ncclSend");
+    api.recv = (decltype(api.recv))dlsym(h, "ncclRecv");
+    api.groupStart = (decltype(api.groupStart))dlsym(h, "ncclGroupStart");
+    api.groupEnd = (decltype(api.groupEnd))dlsym(h, "ncclGroupEnd");
+    api.errorString = (decltype(api.errorString))dlsym(h, "ncclGetErrorString");
+    api.ok = api.getUniqueId && api.commInitRank && api.commDestroy && api.send && api.recv && api.groupStart &&
+             api.groupEnd && api.errorString;
+  });
+  return api;
+}
+
+static void nccl_check(ncclResult_t r, const char* what) {
+  if (r != ncclSuccess) throw StatusError(GAWEE_ERR_NCCL, std::string(what) + ": " + nccl().errorString(r));
+}
+
+// ---------------------------------------------------------------------------
+// Runtime state
+// ---------------------------------------------------------------------------
+struct Runtime {
+  std::unique_ptr<Plan> plan;
+  int device = 0;
+  cudaStream_t own_stream = nullptr;
+  void* persist = nullptr;
+  void* arena = nullptr;
+  int* d_status = nullptr;
+  std::vector<char> dirty;       // per argument
+  std::vector<char> pack_done;   // per op
+  bool prologue_done = false;
+  bool graph_mode = true;
+  int forwards = 0;
+  cudaGraphExec_t gexec = nullptr;
+  cudaGraph_t graph = nullptr;
+  std::vector<std::array<TMap, 2>> tmaps;  // per op (TC only)
+  ncclComm_t comm = nullptr;
+  int world = 1, rank = 0;
+
+  char* ptr(const View& v) const {
+    const Buf& b = plan->bufs[v.buf];
+    if (!b.ptr) throw std::runtime_error("internal: buffer without storage");
+    return static_cast<char*>(b.ptr) + v.off * (int64_t)dtype_size(v.dt);
+  }
+  int* status() const { return d_status; }
+
+  ~Runtime() {
+    if (gexec) cudaGraphExecDestroy(gexec);
+    if (graph) cudaGraphDestroy(graph);
+    if (comm && nccl().ok) nccl().commDestroy(comm);
+    if (persist) cudaFree(persist);
+    if (arena) cudaFree(arena);
+    if (d_status) cudaFree(d_status);
+    if (own_stream) cudaStreamDestroy(own_stream);
+  }
+
+  void allocate();
+  void build_tensor_maps();
+  void run_op(int o, cudaStream_t s);
+  void run_list(const std::vector<int>& ops, cudaStream_t s, bool check);
+  void forward(cudaStream_t s);
+};
+
+static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+void Runtime::allocate() {
+  Plan& P = *plan;
+  auto& bufs = P.bufs;
+  size_t poff = P.persist_bytes, arena_bytes = P.arena_bytes;
+  if (poff) {
+    if (cudaMalloc(&persist, poff) != cudaSuccess)
+      throw StatusError(GAWEE_ERR_OOM, "cudaMalloc of " + std::to_string(poff) + " persistent bytes failed");
+  }
+  if (arena_bytes) {
+    if (cudaMalloc(&arena, arena_bytes) != cudaSuccess)
+      throw StatusError(GAWEE_ERR_OOM, "cudaMalloc of " + std::to_string(arena_bytes) + " arena bytes failed");
+  }
+  GCHECK(cudaMalloc(&d_status, sizeof(int)));
+  GCHECK(cudaMemset(d_status, 0, sizeof(int)));
+  for (auto& B : bufs) {
+    if (!B.live) continue;
+    B.ptr = static_cast<char*>(B.kind == BufKind::ARENA ? arena : persist) + B.offset;
+  }
+  // constants
+  for (auto& B : bufs) {
+    if (B.kind != BufKind::CONST || !B.ptr) continue;
+    if (B.const_value >= 0) {
+      const Value& v = P.g.values[B.const_value];
+      GCHECK(cudaMemcpy(B.ptr, v.data.data(), v.data.size(), cudaMemcpyHostToDevice));
+    } else if (!B.host_init.empty()) {
+      GCHECK(cudaMemcpy(B.ptr, B.host_init.data(), B.host_init.size(), cudaMemcpyHostToDevice));
+    }
+  }
+  dirty.assign(P.g.args.size(), 1);
+  pack_done.assign(P.ops.size(), 0);
+}
+
+void Runtime::build_tensor_maps() {
+  Plan& P = *plan;
+  tmaps.assign(P.ops.size(), {});
+  for (size_t o = 0; o < P.ops.size(); ++o) {
+    const Op& op = P.ops[o];
+    if (op.dead || op.kind != OpKind::TC) continue;
+    const auto& t = op.tc;
+    const float* hi = static_cast<const float*>(P.bufs[t.hi].ptr);
+    const float* lo = static_cast<const float*>(P.bufs[t.lo].ptr);
+    if (!kern::make_b_tensor_maps(hi, lo, t.b_batch, t.N, t.ldk, t.block_n, tmaps[o][0].b, tmaps[o][1].b))
+      throw std::runtime_error("cuTensorMapEncodeTiled failed for op " + op.name);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Structured launches
+// ---------------------------------------------------------------------------
+static kern::DProgram to_device(const EProgram& p) {
+  if ((int)p.code.size() > kern::kMaxInstr || (int)p.reg_types.size() > kern::kMaxRegs)
+    throw std::runtime_error("scalar program too large for the device interpreter");
+  kern::DProgram d{};
+  d.n_code = (int)p.code.size();
+  d.n_args = p.n_args;
+  d.result = p.result;
+  for (size_t k = 0; k < p.code.size(); ++k) {
+    const EInstr& in = p.code[k];
+    auto& o = d.code[k];
+    o.op = (uint8_t)in.op;
+    o.ty = (uint8_t)in.ty;
+    o.rty = (uint8_t)in.rty;
+    o.pred = in.pred;
+    o.dst = (int8_t)in.dst;
+    o.a = (int8_t)in.a;
+    o.b = (int8_t)in.b;
+    o.c = (int8_t)in.c;
+    o.fimm = in.fimm;
+    o.iimm = in.iimm;
+  }
+  return d;
+}
+
+static void launch_ew(Runtime& rt, const Op& op, cudaStream_t s) {
+  const View& out = op.out;
+  int r = out.rank();
+  // iteration dims: drop size-1 dims, order by output stride (outermost first), merge contiguous
+  std::vector<int> dims;
+  for (int d = 0; d < r; ++d)
+    if (out.shape[d] != 1) dims.push_back(d);
+  std::stable_sort(dims.begin(), dims.end(), [&](int a, int b) { return out.st[a] > out.st[b]; });
+  std::vector<int64_t> shape;
+  std::vector<std::vector<int64_t>> st(op.ins.size() + 1);
+  for (int d : dims) {
+    shape.push_back(out.shape[d]);
+    st[0].push_back(out.st[d]);
+    for (size_t k = 0; k < op.ins.size(); ++k) st[k + 1].push_back(op.ins[k].st[d]);
+  }
+  // merge dim i into i-1 when every operand is contiguous across them
+  for (int i = (int)shape.size() - 1; i > 0; --i) {
+    bool ok = true;
+    for (auto& s2 : st)
+      if (s2[i - 1] != s2[i] * shape[i]) ok = false;
+    if (!ok) continue;
+    shape[i - 1] *= shape[i];
+    shape.erase(shape.begin() + i);
+    for (auto& s2 : st) {
+      s2[i - 1] = s2[i];
+      s2.erase(s2.begin() + i);
+    }
+  }
+  if (shape.empty()) {
+    shape.push_back(1);
+    for (auto& s2 : st) s2.push_back(0);
+  }
+  if ((int)shape.size() > kern::kMaxRank) throw std::runtime_error("elementwise iteration rank too large");
+  if ((int)op.ins.size() > kern::kMaxIn) throw std::runtime_error("too many elementwise operands");
+  kern::EwParams p{};
+  p.rank = (int)shape.size();
+  p.n_in = (int)op.ins.size();
+  p.numel = 1;
+  for (size_t d = 0; d < shape.size(); ++d) {
+    p.shape[d] = shape[d];
+    p.numel *= shape[d];
+    p.out.st[d] = st[0][d];
+    for (size_t k = 0; k < op.ins.size(); ++k) p.in[k].st[d] = st[k + 1][d];
+  }
+  p.out.ptr = rt.ptr(out);
+  p.out.dt = (int8_t)out.dt;
+  for (size_t k = 0; k < op.ins.size(); ++k) {
+    p.in[k].ptr = rt.ptr(op.ins[k]);
+    p.in[k].dt = (int8_t)op.ins[k].dt;
+  }
+  p.prog = to_device(op.prog);
+  p.status = rt.status();
+  kern::launch_elementwise(p, s);
+}
+
+static void launch_tc(Runtime& rt, int o, const Op& op, cudaStream_t s) {
+  const auto& t = op.tc;
+  kern::ConvGemmParams p{};
+  p.x = reinterpret_cast<const float*>(rt.ptr(t.x));
+  // strides of size-1 dims are never stepped; zero them so alignment checks see only real strides
+  if (t.conv) {
+    p.x_sn = t.x.shape[0] > 1 ? t.x.st[0] : 0;
+    p.x_sh = t.x.st[2];
+    p.x_sw = t.x.st[3];
+  } else {
+    int r = t.x.rank();
+    p.x_sn = 0;
+    p.x_sh = t.M > 1 ? t.x.st[r - 2] : 0;
+    p.x_sw = 0;
+  }
+  p.H = t.H; p.W = t.W; p.C = t.C; p.P = t.P; p.Q = t.Q;
+  p.R = t.R; p.S = t.S; p.sh = t.sh; p.sw = t.sw; p.ph = t.ph; p.pw = t.pw; p.dh = t.dh; p.dw = t.dw;
+  p.M = t.M; p.N = t.N; p.K = t.K;
+  p.nb = 1;
+  p.batch_rank = t.batch_rank;
+  for (int d = 0; d < t.batch_rank; ++d) {
+    p.batch_shape[d] = t.batch_shape[d];
+    p.a_bst[d] = t.a_bst[d];
+    p.b_bst[d] = t.b_bst[d];
+    p.c_bst[d] = t.out.st[d];
+    p.nb *= (int)t.batch_shape[d];
+  }
+  p.out = reinterpret_cast<float*>(rt.ptr(t.out));
+  if (t.conv) {
+    p.ldc = t.out.st[3];
+    p.ldc_n = t.out.st[1];
+  } else {
+    int r = t.out.rank();
+    p.ldc = t.out.st[r - 2];
+    p.ldc_n = t.out.st[r - 1];
+  }
+  p.epi = t.epi;
+  p.bias = t.bias.buf >= 0 ? reinterpret_cast<const float*>(rt.ptr(t.bias)) : nullptr;
+  p.res = t.res.buf >= 0 ? reinterpret_cast<const float*>(rt.ptr(t.res)) : nullptr;
+  p.n_aux = (int)t.aux.size();
+  for (size_t a = 0; a < t.aux.size(); ++a) {
+    const View& v = t.aux[a];
+    int r = v.rank();
+    p.aux[a] = reinterpret_cast<const float*>(rt.ptr(v));
+    p.aux_sm[a] = v.st[r - 2];
+    p.aux_sn[a] = v.st[r - 1];
+    for (int d = 0; d < t.batch_rank; ++d) p.aux_sb[a][d] = v.st[d];
+  }
+  if (t.epi == kern::EPI_PROGRAM) p.prog = to_device(t.prog);
+  p.status = rt.status();
+  if (!kern::launch_conv_gemm_tc(p, rt.tmaps[o][0].b, rt.tmaps[o][1].b, t.block_n, s))
+    throw StatusError(GAWEE_ERR_UNSUPPORTED, "tensor-core launch rejected the shape of op " + op.name);
+}
+
+void Runtime::run_op(int o, cudaStream_t s) {
+  const Op& op = plan->ops[o];
+  if (op.kind == OpKind::EW) launch_ew(*this, op, s);
+  else if (op.kind == OpKind::TC) launch_tc(*this, o, op, s);
+  else op.launch(*this, s);
+}
+
+void Runtime::run_list(const std::vector<int>& ops, cudaStream_t s, bool check) {
+  for (int o : ops) {
+    run_op(o, s);
+    if (check) {
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) throw CudaError("launch of " + plan->ops[o].name + ": " + cudaGetErrorString(e));
+    }
+  }
+}
+
+void Runtime::forward(cudaStream_t s) {
+  if (!prologue_done) {
+    run_list(plan->prologue, s, true);
+    prologue_done = true;
+  }
+  for (int o : plan->pack) {
+    const Op& op = plan->ops[o];
+    bool need = !pack_done[o];
+    for (int a : op.dep_args) need = need || dirty[a];
+    if (need) {
+      run_op(o, s);
+      GCHECK(cudaGetLastError());
+      pack_done[o] = 1;
+    }
+  }
+  // First forward runs eagerly (it also sets kernel attributes); later ones
+  // replay a CUDA graph of the main sequence.
+  if (graph_mode && forwards > 0 && s != nullptr) {
+    if (!gexec) {
+      GCHECK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+      try {
+        run_list(plan->main, s, false);
+      } catch (...) {
+        cudaGraph_t g;
+        cudaStreamEndCapture(s, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+      }
+      GCHECK(cudaStreamEndCapture(s, &graph));
+      GCHECK(cudaGraphInstantiate(&gexec, graph, 0));
+    }
+    GCHECK(cudaGraphLaunch(gexec, s));
+  } else {
+    run_list(plan->main, s, true);
+  }
+  std::fill(dirty.begin(), dirty.end(), 0);
+  ++forwards;
+}
+
+// ---------------------------------------------------------------------------
+// Launch builders (launch.h)
+// ---------------------------------------------------------------------------
+namespace launch {
+
+Fn remap(kern::RemapParams rp, const View& in, const View& out) {
+  return [rp, in, out](Runtime& rt, void* s) mutable {
+    rp.in = rt.ptr(in);
+    rp.out = rt.ptr(out);
+    kern::launch_remap(rp, static_cast<cudaStream_t>(s));
+  };
+}
+
+static void split_dims(const View& in, const std::vector<bool>& red, kern::ReduceParams* rp,
+                       kern::GenericReduceParams* gp, const View& out) {
+  std::vector<int64_t> ks, kst, rs, rst;
+  for (int d = 0; d < in.rank(); ++d) {
+    if (red[d]) { rs.push_back(in.shape[d]); rst.push_back(in.st[d]); }
+    else { ks.push_back(in.shape[d]); kst.push_back(in.st[d]); }
+  }
+  // output strides over kept dims: the output is dense row-major over its own
+  // shape, which equals the kept dims with unit dims inserted (keepdims)
+  std::vector<int64_t> ost;
+  {
+    int k = 0;
+    for (int d = 0; d < in.rank(); ++d) {
+      if (red[d]) continue;
+      (void)k;
+      ost.push_back(0);
+    }
+    // strides over kept dims in row-major order of the kept shape
+    int64_t acc = 1;
+    for (int i = (int)ks.size() - 1; i >= 0; --i) {
+      ost[i] = acc;
+      acc *= ks[i];
+    }
+  }
+  if (ks.size() > (size_t)kern::kMaxRank || rs.size() > (size_t)kern::kMaxRank)
+    throw std::runtime_error("reduction rank too large");
+  auto fill = [&](auto* p) {
+    p->kept_rank = (int)ks.size();
+    p->red_rank = (int)rs.size();
+    p->rows = 1;
+    p->cols = 1;
+    for (size_t i = 0; i < ks.size(); ++i) {
+      p->kept_shape[i] = ks[i];
+      p->kept_st[i] = kst[i];
+      p->out_st[i] = ost[i];
+      p->rows *= ks[i];
+    }
+    for (size_t i = 0; i < rs.size(); ++i) {
+      p->red_shape[i] = rs[i];
+      p->red_st[i] = rst[i];
+      p->cols *= rs[i];
+    }
+  };
+  if (rp) fill(rp);
+  if (gp) fill(gp);
+  (void)out;
+}
+
+Fn reduce(const View& in, const View& out, const std::vector<bool>& red, bool mean, float count) {
+  if (!out.dense_rowmajor()) throw std::runtime_error("reduce output must be dense");
+  kern::ReduceParams rp{};
+  split_dims(in, red, &rp, nullptr, out);
+  rp.mode = mean ? 1 : 0;
+  rp.count = count;
+  return [rp, in, out](Runtime& rt, void* s) mutable {
+    rp.in = reinterpret_cast<const float*>(rt.ptr(in));
+    rp.out = reinterpret_cast<float*>(rt.ptr(out));
+    kern::launch_reduce_f32(rp, static_cast<cudaStream_t>(s));
+  };
+}
+
+Fn generic_reduce(const View& in, const View& out, const std::vector<bool>& red, const EProgram& body) {
+  kern::GenericReduceParams gp{};
+  split_dims(in, red, nullptr, &gp, out);
+  gp.in_dt = (int8_t)in.dt;
+  gp.out_dt = (int8_t)out.dt;
+  gp.prog = to_device(body);
+  return [gp, in, out](Runtime& rt, void* s) mutable {
+    gp.in = rt.ptr(in);
+    gp.out = rt.ptr(out);
+    gp.status = rt.status();
+    kern::launch_generic_reduce(gp, static_cast<cudaStream_t>(s));
+  };
+}
+
+Fn pool(kern::PoolParams pp, const View& in, const View& out) {
+  return [pp, in, out](Runtime& rt, void* s) mutable {
+    pp.in = reinterpret_cast<const float*>(rt.ptr(in));
+    pp.out = reinterpret_cast<float*>(rt.ptr(out));
+    kern::launch_pool(pp, static_cast<cudaStream_t>(s));
+  };
+}
+
+Fn softmax(const View& in, const View& out, int axis) {
+  kern::SoftmaxParams sp{};
+  sp.len = in.shape[axis];
+  sp.in_axis_st = in.st[axis];
+  sp.out_axis_st = out.st[axis];
+  sp.rows = 1;
+  int k = 0;
+  for (int d = 0; d < in.rank(); ++d) {
+    if (d == axis) continue;
+    sp.row_shape[k] = in.shape[d];
+    sp.in_row_st[k] = in.st[d];
+    sp.out_row_st[k] = out.st[d];
+    sp.rows *= in.shape[d];
+    ++k;
+  }
+  sp.rank = k;
+  return [sp, in, out](Runtime& rt, void* s) mutable {
+    sp.in = reinterpret_cast<const float*>(rt.ptr(in));
+    sp.out = reinterpret_cast<float*>(rt.ptr(out));
+    kern::launch_softmax(sp, static_cast<cudaStream_t>(s));
+  };
+}
+
+Fn gather(const View& data, const View& idx, const View& out, int64_t pre, int64_t axis_len, int64_t nidx,
+          int64_t post) {
+  kern::GatherParams gp{};
+  gp.idx_dt = (int8_t)idx.dt;
+  gp.elem_bytes = (int)dtype_size(data.dt);
+  gp.pre = pre;
+  gp.axis_len = axis_len;
+  gp.nidx = nidx;
+  gp.post = post;
+  return [gp, data, idx, out](Runtime& rt, void* s) mutable {
+    gp.data = rt.ptr(data);
+    gp.idx = rt.ptr(idx);
+    gp.out = rt.ptr(out);
+    gp.status = rt.status();
+    kern::launch_gather(gp, static_cast<cudaStream_t>(s));
+  };
+}
+
+Fn gather_elements(const View& data, const View& idx, const View& out, int axis) {
+  kern::GatherElementsParams gp{};
+  gp.idx_dt = (int8_t)idx.dt;
+  gp.elem_bytes = (int)dtype_size(data.dt);
+  gp.rank = idx.rank();
+  gp.axis = axis;
+  gp.numel = idx.numel();
+  for (int d = 0; d < idx.rank(); ++d) {
+    gp.shape[d] = idx.shape[d];
+    gp.data_st[d] = data.st[d];
+  }
+  gp.data_axis_len = data.shape[axis];
+  return [gp, data, idx, out](Runtime& rt, void* s) mutable {
+    gp.data = rt.ptr(data);
+    gp.idx = rt.ptr(idx);
+    gp.out = rt.ptr(out);
+    gp.status = rt.status();
+    kern::launch_gather_elements(gp, static_cast<cudaStream_t>(s));
+  };
+}
+
+Fn range(kern::RangeParams rp, const View& out) {
+  return [rp, out](Runtime& rt, void* s) mutable {
+    rp.out = rt.ptr(out);
+    kern::launch_range(rp, static_cast<cudaStream_t>(s));
+  };
+}
+
+Fn topk(const View& in, const View& vals, const View& idxs, const View& used, int64_t k) {
+  kern::TopKParams tp{};
+  tp.rows = in.shape[0];
+  tp.len = in.shape[1];
+  tp.k = k;
+  return [tp, in, vals, idxs, used](Runtime& rt, void* s) mutable {
+    tp.in = reinterpret_cast<const float*>(rt.ptr(in));
+    tp.vals = reinterpret_cast<float*>(rt.ptr(vals));
+    tp.idxs = reinterpret_cast<int64_t*>(rt.ptr(idxs));
+    tp.used = reinterpret_cast<unsigned char*>(rt.ptr(used));
+    kern::launch_topk(tp, static_cast<cudaStream_t>(s));
+  };
+}
+
+Fn pack(const PackSpec& ps, int64_t ldk, int hi, int lo) {
+  kern::PackBParams pp{};
+  pp.batch = ps.batch;
+  pp.K = ps.K;
+  pp.N = ps.N;
+  pp.ldk = ldk;
+  pp.sn = ps.sn;
+  pp.k_rank = (int)ps.k_shape.size();
+  for (int d = 0; d < pp.k_rank; ++d) {
+    pp.k_shape[d] = ps.k_shape[d];
+    pp.k_st[d] = ps.k_st[d];
+    pp.k_valid[d] = ps.k_valid[d];
+  }
+  pp.batch_rank = (int)ps.batch_shape.size();
+  for (int d = 0; d < pp.batch_rank; ++d) {
+    pp.batch_shape[d] = ps.batch_shape[d];
+    pp.batch_st[d] = ps.batch_st[d];
+  }
+  View src = ps.src;
+  return [pp, src, hi, lo](Runtime& rt, void* s) mutable {
+    pp.src = reinterpret_cast<const float*>(rt.ptr(src));
+    pp.hi = static_cast<float*>(rt.plan->bufs[hi].ptr);
+    pp.lo = static_cast<float*>(rt.plan->bufs[lo].ptr);
+    kern::launch_pack_b(pp, static_cast<cudaStream_t>(s));
+  };
+}
+
+}  // namespace launch
+}  // namespace gawee
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+struct gawee_ctx {
+  gawee::Runtime rt;
+  std::string err;
+};
+
+namespace {
+
+template <class F>
+gawee_status guard(gawee_ctx* ctx, F&& f) {
+  try {
+    if (ctx) cudaSetDevice(ctx->rt.device);
+    f();
+    return GAWEE_OK;
+  } catch (const gawee::StatusError& e) {
+    if (ctx) ctx->err = e.what();
+    return e.code;
+  } catch (const gawee::ParseError& e) {
+    if (ctx) ctx->err = e.what();
+    return GAWEE_ERR_PARSE;
+  } catch (const gawee::CudaError& e) {
+    if (ctx) ctx->err = e.what();
+    return GAWEE_ERR_CUDA;
+  } catch (const std::exception& e) {
+    if (ctx) ctx->err = e.what();
+    std::string m = e.what();
+    return m.rfind("unsupported", 0) == 0 || m.find(": unsupported") != std::string::npos ? GAWEE_ERR_UNSUPPORTED
+                                                                                          : GAWEE_ERR_INVALID;
+  } catch (...) {
+    if (ctx) ctx->err = "unknown error";
+    return GAWEE_ERR_INVALID;
+  }
+}
+
+cudaStream_t stream_of(gawee_ctx* ctx, void* s) {
+  return s ? static_cast<cudaStream_t>(s) : ctx->rt.own_stream;
+}
+
+thread_local std::string g_create_error;
+
+gawee_status create_impl(const std::string& text, const char* entry, int device, gawee_ctx** out) {
+  if (!out) return GAWEE_ERR_INVALID;
+  *out = nullptr;
+  auto* ctx = new gawee_ctx();
+  ctx->rt.device = device;
+  gawee_status st = guard(ctx, [&] {
+    int n = 0;
+    GCHECK(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n) throw gawee::StatusError(GAWEE_ERR_INVALID, "invalid device index");
+    GCHECK(cudaSetDevice(device));
+    gawee::Graph g = gawee::parse_mlir(text, entry ? entry : "forward");
+    ctx->rt.plan = gawee::build_plan(std::move(g));
+    GCHECK(cudaStreamCreateWithFlags(&ctx->rt.own_stream, cudaStreamNonBlocking));
+    ctx->rt.allocate();
+    ctx->rt.build_tensor_maps();
+  });
+  if (st != GAWEE_OK) {
+    g_create_error = ctx->err;
+    delete ctx;
+    return st;
+  }
+  *out = ctx;
+  return GAWEE_OK;
+}
+
+int value_info(const gawee::Value& v, int* dtype, int* rank, int64_t* shape) {
+  if (dtype) *dtype = (int)v.type.dtype;
+  if (rank) *rank = v.type.rank();
+  if (shape)
+    for (int d = 0; d < v.type.rank(); ++d) shape[d] = v.type.shape[d];
+  return GAWEE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+gawee_status gawee_create(const char* mlir_text, const char* entry, int device, gawee_ctx** out) {
+  if (!mlir_text) return GAWEE_ERR_INVALID;
+  return create_impl(mlir_text, entry, device, out);
+}
+
+gawee_status gawee_create_from_file(const char* path, const char* entry, int device, gawee_ctx** out) {
+  if (!path) return GAWEE_ERR_INVALID;
+  std::string text;
+  try {
+    text = gawee::read_text_file(path);
+  } catch (const std::exception& e) {
+    g_create_error = e.what();
+    return GAWEE_ERR_INVALID;
+  }
+  return create_impl(text, entry, device, out);
+}
+
+void gawee_destroy(gawee_ctx* ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->rt.device);
+  if (ctx->rt.own_stream) cudaStreamSynchronize(ctx->rt.own_stream);
+  delete ctx;
+}
+
+gawee_status gawee_last_error(const gawee_ctx* ctx, char* buf, size_t n) {
+  if (!buf || n == 0) return GAWEE_ERR_INVALID;
+  const std::string& m = ctx ? ctx->err : g_create_error;
+  std::strncpy(buf, m.c_str(), n - 1);
+  buf[n - 1] = 0;
+  return GAWEE_OK;
+}
+
+int gawee_num_args(const gawee_ctx* ctx) { return ctx ? (int)ctx->rt.plan->g.args.size() : -1; }
+int gawee_num_outputs(const gawee_ctx* ctx) { return ctx ? (int)ctx->rt.plan->g.results.size() : -1; }
+
+gawee_status gawee_arg_info(const gawee_ctx* ctx, int i, int* dtype, int* rank, int64_t* shape) {
+  if (!ctx || i < 0 || i >= gawee_num_args(ctx)) return GAWEE_ERR_INVALID;
+  const auto& g = ctx->rt.plan->g;
+  return value_info(g.values[g.args[i]], dtype, rank, shape);
+}
+
+gawee_status gawee_output_info(const gawee_ctx* ctx, int i, int* dtype, int* rank, int64_t* shape) {
+  if (!ctx || i < 0 || i >= gawee_num_outputs(ctx)) return GAWEE_ERR_INVALID;
+  const auto& g = ctx->rt.plan->g;
+  return value_info(g.values[g.results[i]], dtype, rank, shape);
+}
+
+static gawee_status set_arg_impl(gawee_ctx* ctx, int i, const void* src, size_t bytes, void* stream,
+                                 cudaMemcpyKind kind) {
+  if (!ctx) return GAWEE_ERR_INVALID;
+  return guard(ctx, [&] {
+    auto& rt = ctx->rt;
+    if (i < 0 || i >= (int)rt.plan->arg_buf.size()) throw gawee::StatusError(GAWEE_ERR_INVALID, "argument index out of range");
+    const gawee::Buf& b = rt.plan->bufs[rt.plan->arg_buf[i]];
+    if (bytes != b.bytes() || !src)
+      throw gawee::StatusError(GAWEE_ERR_INVALID, "argument " + std::to_string(i) + " expects " +
+                                                      std::to_string(b.bytes()) + " bytes, got " + std::to_string(bytes));
+    if (!b.ptr) return;  // argument never read by the graph
+    GCHECK(cudaMemcpyAsync(b.ptr, src, bytes, kind, stream_of(ctx, stream)));
+    rt.dirty[i] = 1;
+  });
+}
+
+gawee_status gawee_set_arg(gawee_ctx* ctx, int i, const void* host, size_t bytes, void* stream) {
+  return set_arg_impl(ctx, i, host, bytes, stream, cudaMemcpyHostToDevice);
+}
+
+gawee_status gawee_set_arg_device(gawee_ctx* ctx, int i, const void* dev, size_t bytes, void* stream) {
+  return set_arg_impl(ctx, i, dev, bytes, stream, cudaMemcpyDeviceToDevice);
+}
+
+gawee_status gawee_forward(gawee_ctx* ctx, void* stream) {
+  if (!ctx) return GAWEE_ERR_INVALID;
+  return guard(ctx, [&] { ctx->rt.forward(stream_of(ctx, stream)); });
+}
+
+gawee_status gawee_get_output(gawee_ctx* ctx, int i, void* host, size_t bytes, void* stream) {
+  if (!ctx) return GAWEE_ERR_INVALID;
+  return guard(ctx, [&] {
+    auto& rt = ctx->rt;
+    if (i < 0 || i >= (int)rt.plan->result_view.size()) throw gawee::StatusError(GAWEE_ERR_INVALID, "output index out of range");
+    const gawee::View& v = rt.plan->result_view[i];
+    size_t nb = (size_t)v.numel() * gawee::dtype_size(v.dt);
+    if (bytes != nb || !host)
+      throw gawee::StatusError(GAWEE_ERR_INVALID, "output " + std::to_string(i) + " has " + std::to_string(nb) + " bytes");
+    GCHECK(cudaMemcpyAsync(host, rt.ptr(v), nb, cudaMemcpyDeviceToHost, stream_of(ctx, stream)));
+  });
+}
+
+gawee_status gawee_output_device_ptr(gawee_ctx* ctx, int i, void** ptr) {
+  if (!ctx || !ptr) return GAWEE_ERR_INVALID;
+  return guard(ctx, [&] {
+    auto& rt = ctx->rt;
+    if (i < 0 || i >= (int)rt.plan->result_view.size()) throw gawee::StatusError(GAWEE_ERR_INVALID, "output index out of range");
+    *ptr = rt.ptr(rt.plan->result_view[i]);
+  });
+}
+
+gawee_status gawee_synchronize(gawee_ctx* ctx, void* stream) {
+  if (!ctx) return GAWEE_ERR_INVALID;
+  return guard(ctx, [&] {
+    GCHECK(cudaStreamSynchronize(stream_of(ctx, stream)));
+    int st = 0;
+    GCHECK(cudaMemcpy(&st, ctx->rt.d_status, sizeof(int), cudaMemcpyDeviceToHost));
+    if (st) {
+      GCHECK(cudaMemset(ctx->rt.d_status, 0, sizeof(int)));
+      static const char* names[] = {"ok", "gather index out of range", "tensor-core barrier wait timed out",
+                                    "invalid scalar program", "integer division by zero", "slice out of bounds"};
+      throw gawee::StatusError(GAWEE_ERR_DEVICE, std::string("device reported: ") + (st >= 0 && st < 6 ? names[st] : "error"));
+    }
+  });
+}
+
+gawee_status gawee_set_graph_mode(gawee_ctx* ctx, int enabled) {
+  if (!ctx) return GAWEE_ERR_INVALID;
+  ctx->rt.graph_mode = enabled != 0;
+  return GAWEE_OK;
+}
+
+int gawee_num_kernels(const gawee_ctx* ctx) { return ctx ? (int)ctx->rt.plan->main.size() : -1; }
+
+gawee_status gawee_plan_summary(const gawee_ctx* ctx, char* buf, size_t n) {
+  if (!ctx || !buf || n == 0) return GAWEE_ERR_INVALID;
+  std::string s = ctx->rt.plan->summary();
+  std::strncpy(buf, s.c_str(), n - 1);
+  buf[n - 1] = 0;
+  return GAWEE_OK;
+}
+
+gawee_status gawee_op_info(const gawee_ctx* ctx, int i, char* name, size_t n, int* is_tc, double* flops) {
+  if (!ctx || i < 0 || i >= (int)ctx->rt.plan->main.size()) return GAWEE_ERR_INVALID;
+  const gawee::Op& op = ctx->rt.plan->ops[ctx->rt.plan->main[i]];
+  if (name && n) {
+    std::strncpy(name, op.name.c_str(), n - 1);
+    name[n - 1] = 0;
+  }
+  if (is_tc) *is_tc = op.kind == gawee::OpKind::TC;
+  if (flops) *flops = op.kind == gawee::OpKind::TC ? op.tc.flops : 0.0;
+  return GAWEE_OK;
+}
+
+gawee_status gawee_profile_forward(gawee_ctx* ctx, void* stream, float* ms, int n) {
+  if (!ctx || !ms || n < (int)ctx->rt.plan->main.size()) return GAWEE_ERR_INVALID;
+  return guard(ctx, [&] {
+    auto& rt = ctx->rt;
+    cudaStream_t s = stream_of(ctx, stream);
+    rt.forward(s);  // prologue / packing as needed, then one regular forward
+    const auto& main = rt.plan->main;
+    std::vector<cudaEvent_t> ev(main.size() + 1);
+    for (auto& e : ev) GCHECK(cudaEventCreate(&e));
+    GCHECK(cudaEventRecord(ev[0], s));
+    for (size_t k = 0; k < main.size(); ++k) {
+      rt.run_op(main[k], s);
+      GCHECK(cudaGetLastError());
+      GCHECK(cudaEventRecord(ev[k + 1], s));
+    }
+    GCHECK(cudaStreamSynchronize(s));
+    for (size_t k = 0; k < main.size(); ++k) GCHECK(cudaEventElapsedTime(&ms[k], ev[k], ev[k + 1]));
+    for (auto& e : ev) cudaEventDestroy(e);
+  });
+}
+
+gawee_status gawee_plan_text(const char* mlir_text, const char* entry, char* buf, size_t n) {
+  if (!mlir_text || !buf || n == 0) return GAWEE_ERR_INVALID;
+  gawee_status st = GAWEE_OK;
+  std::string out;
+  try {
+    auto plan = gawee::build_plan(gawee::parse_mlir(mlir_text, entry ? entry : "forward"));
+    out = plan->summary();
+  } catch (const gawee::ParseError& e) {
+    out = e.what();
+    st = GAWEE_ERR_PARSE;
+  } catch (const std::exception& e) {
+    out = e.what();
+    std::string m = out;
+    st = m.find("unsupported") != std::string::npos ? GAWEE_ERR_UNSUPPORTED : GAWEE_ERR_INVALID;
+  }
+  std::strncpy(buf, out.c_str(), n - 1);
+  buf[n - 1] = 0;
+  g_create_error = st == GAWEE_OK ? "" : out;
+  return st;
+}
+
+gawee_status gawee_ciface_forward(gawee_ctx* ctx, void* result_desc, void* const* arg_descs, int nargs) {
+  if (!ctx) return GAWEE_ERR_INVALID;
+  return guard(ctx, [&] {
+    auto& rt = ctx->rt;
+    const auto& g = rt.plan->g;
+    if (nargs != (int)g.args.size()) throw gawee::StatusError(GAWEE_ERR_INVALID, "wrong number of memref arguments");
+    if (g.results.size() != 1) throw gawee::StatusError(GAWEE_ERR_UNSUPPORTED, "the ciface entry supports one result");
+    cudaStream_t s = rt.own_stream;
+    for (int a = 0; a < nargs; ++a) {
+      const auto& t = g.values[g.args[a]].type;
+      const char* d = static_cast<const char*>(arg_descs[a]);
+      const char* aligned;
+      int64_t offset;
+      std::memcpy(&aligned, d + sizeof(void*), sizeof(void*));
+      std::memcpy(&offset, d + 2 * sizeof(void*), 8);
+      const int64_t* sizes = reinterpret_cast<const int64_t*>(d + 2 * sizeof(void*) + 8);
+      const int64_t* strides = sizes + t.rank();
+      int64_t expect = 1;
+      for (int k = t.rank() - 1; k >= 0; --k) {
+        if (sizes[k] != t.shape[k]) throw gawee::StatusError(GAWEE_ERR_INVALID, "memref size mismatch on arg " + std::to_string(a));
+        if (t.shape[k] != 1 && strides[k] != expect)
+          throw gawee::StatusError(GAWEE_ERR_INVALID, "memref arg " + std::to_string(a) + " is not dense row-major");
+        expect *= t.shape[k];
+      }
+      const gawee::Buf& b = rt.plan->bufs[rt.plan->arg_buf[a]];
+      if (b.ptr)
+        GCHECK(cudaMemcpyAsync(b.ptr, aligned + offset * (int64_t)gawee::dtype_size(t.dtype), b.bytes(),
+                               cudaMemcpyHostToDevice, s));
+      rt.dirty[a] = 1;
+    }
+    rt.forward(s);
+    const gawee::View& v = rt.plan->result_view[0];
+    size_t nb = (size_t)v.numel() * gawee::dtype_size(v.dt);
+    void* host = std::malloc(nb ? nb : 1);  // owned by the caller, as in the reference ABI
+    if (!host) throw gawee::StatusError(GAWEE_ERR_OOM, "malloc of the result failed");
+    GCHECK(cudaMemcpyAsync(host, rt.ptr(v), nb, cudaMemcpyDeviceToHost, s));
+    GCHECK(cudaStreamSynchronize(s));
+    char* r = static_cast<char*>(result_desc);
+    const auto& rtype = g.values[g.results[0]].type;
+    int64_t zero = 0;
+    std::memcpy(r, &host, sizeof(void*));
+    std::memcpy(r + sizeof(void*), &host, sizeof(void*));
+    std::memcpy(r + 2 * sizeof(void*), &zero, 8);
+    int64_t* sizes = reinterpret_cast<int64_t*>(r + 2 * sizeof(void*) + 8);
+    int64_t* strides = sizes + rtype.rank();
+    int64_t acc = 1;
+    for (int k = rtype.rank() - 1; k >= 0; --k) {
+      sizes[k] = rtype.shape[k];
+      strides[k] = acc;
+      acc *= rtype.shape[k];
+    }
+  });
+}
+
+gawee_status gawee_dp_unique_id(void* id) {
+  if (!id) return GAWEE_ERR_INVALID;
+  if (!gawee::nccl().ok) return GAWEE_ERR_NCCL;
+  ncclUniqueId u;
+  if (gawee::nccl().getUniqueId(&u) != ncclSuccess) return GAWEE_ERR_NCCL;
+  static_assert(sizeof(ncclUniqueId) == GAWEE_NCCL_ID_BYTES, "nccl id size");
+  std::memcpy(id, &u, sizeof(u));
+  return GAWEE_OK;
+}
+
+gawee_status gawee_dp_init(gawee_ctx* ctx, int world, int rank, const void* id) {
+  if (!ctx || !id || world < 1 || rank < 0 || rank >= world) return GAWEE_ERR_INVALID;
+  return guard(ctx, [&] {
+    if (!gawee::nccl().ok) throw gawee::StatusError(GAWEE_ERR_NCCL, "libnccl.so.2 could not be loaded");
+    ncclUniqueId u;
+    std::memcpy(&u, id, sizeof(u));
+    gawee::nccl_check(gawee::nccl().commInitRank(&ctx->rt.comm, world, u, rank), "ncclCommInitRank");
+    ctx->rt.world = world;
+    ctx->rt.rank = rank;
+  });
+}
+
+gawee_status gawee_dp_gather_output(gawee_ctx* ctx, int i, void* dst, void* stream) {
+  if (!ctx) return GAWEE_ERR_INVALID;
+  return guard(ctx, [&] {
+    auto& rt = ctx->rt;
+    if (!rt.comm) throw gawee::StatusError(GAWEE_ERR_INVALID, "gawee_dp_init was not called");
+    if (i < 0 || i >= (int)rt.plan->result_view.size()) throw gawee::StatusError(GAWEE_ERR_INVALID, "output index out of range");
+    const gawee::View& v = rt.plan->result_view[i];
+    size_t nb = (size_t)v.numel() * gawee::dtype_size(v.dt);
+    cudaStream_t s = stream_of(ctx, stream);
+    auto& api = gawee::nccl();
+    if (rt.rank == 0) {
+      if (!dst) throw gawee::StatusError(GAWEE_ERR_INVALID, "rank 0 needs a destination buffer");
+      GCHECK(cudaMemcpyAsync(dst, rt.ptr(v), nb, cudaMemcpyDeviceToDevice, s));
+      gawee::nccl_check(api.groupStart(), "ncclGroupStart");
+      for (int r = 1; r < rt.world; ++r)
+        gawee::nccl_check(api.recv(static_cast<char*>(dst) + (size_t)r * nb, nb, ncclInt8, r, rt.comm, s), "ncclRecv");
+      gawee::nccl_check(api.groupEnd(), "ncclGroupEnd");
+    } else {
+      gawee::nccl_check(api.send(rt.ptr(v), nb, ncclInt8, 0, rt.comm, s), "ncclSend");
+    }
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,545 @@
+// Tensor-core implicit-GEMM convolution and (batched) GEMM for sm_100a.
+//
+// One CTA computes a 128 x BN tile of C = A . B^T with fp32 accuracy from
+// TF32 tensor cores: three tcgen05.mma per k-step (hi*hi + hi*lo + lo*hi; see
+// Ootomo & Yokota, "Recovering single precision accuracy from Tensor Cores
+// while surpassing the FP32 theoretical peak performance", 2022).
+//
+// The tensor core's fp32 accumulation truncates (Fasi et al., "Numerical
+// behavior of NVIDIA tensor cores", 2021), so over thousands of k-steps its
+// error grows linearly with K.  Each 32-wide k-block is therefore accumulated
+// alone in one of two tensor-memory buffers, and four accumulator warps add
+// the block sums into fp32 registers with IEEE round-to-nearest while the next
+// block is multiplied into the other buffer.
+//
+// Warp roles (320 threads):
+//   warps 0-3  gather the A tile (im2col rows of the NHWC input, zero padding,
+//              K tails) with 16-byte loads, split each value into an exact
+//              TF32 high part and an fp32 remainder in registers, and store
+//              both into 128B-swizzled K-major shared-memory tiles
+//   warp 4     issues the TMA loads of the pre-split B planes; owns the TMEM
+//              allocation
+//   warp 5     one elected thread issues tcgen05.mma and tcgen05.commit
+//   warps 6-9  accumulate block sums from TMEM and run the epilogue
+// Stage hand-off uses mbarriers; every wait is bounded in time and on expiry
+// records ST_BARRIER_TIMEOUT in the status word and lets the CTA finish.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <mutex>
+
+#include "kernels.h"
+#include "program.cuh"
+
+namespace gawee {
+namespace kern {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 32;               // fp32 elements per k-block (one 128-byte swizzle row)
+constexpr int kThreadsTC = 320;
+constexpr unsigned long long kWaitNs = 4000000000ull;  // 4 s per barrier wait
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: returns false if the CTA is aborting or the wait timed out.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status) {
+  if (mbar_try(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  while (true) {
+    if (mbar_try(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_ns() - t0 > kWaitNs) {
+      *abort_flag = 1;
+      if (status) atomicCAS(status, 0, (int)ST_BARRIER_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr & 0x3FFFFu) >> 4);  // start address
+  d |= (uint64_t)1 << 16;                   // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;         // stride byte offset
+  d |= (uint64_t)1 << 46;                   // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                   // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: kind::tf32, fp32 accumulate, K-major A and B, M = 128.
+template <int BN>
+__device__ __forceinline__ uint32_t umma_idesc_tf32() {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+      "[%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
+
+template <int BN, int STAGES>
+struct Smem {
+  static constexpr int kATile = kBM * kBK * 4;  // 16 KB
+  static constexpr int kBTile = BN * kBK * 4;
+  static constexpr int kStage = 2 * kATile + 2 * kBTile;
+  static constexpr int kBarOff = STAGES * kStage;
+  static constexpr int kNumBars = 3 * STAGES + 5;  // full_a, full_b, empty per stage; tfull[2], tempty[2], done
+  static constexpr int kBytes = kBarOff + 8 * kNumBars + 16 + 1024;  // + alignment slack
+  static constexpr int kTmemCols = 2 * BN;         // two k-block accumulators
+};
+
+}  // namespace
+
+template <int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(kThreadsTC, 1)
+    conv_gemm_tc_kernel(const __grid_constant__ ConvGemmParams p, const __grid_constant__ CUtensorMap tm_hi,
+                        const __grid_constant__ CUtensorMap tm_lo) {
+  using L = Smem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* full_a = bars;
+  uint64_t* full_b = bars + STAGES;
+  uint64_t* empty = bars + 2 * STAGES;
+  uint64_t* tfull = bars + 3 * STAGES;      // [2] block sum ready in TMEM buffer b
+  uint64_t* tempty = bars + 3 * STAGES + 2; // [2] TMEM buffer b drained by the accumulator warps
+  uint64_t* done = bars + 3 * STAGES + 4;   // every MMA issued by this CTA completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t m0 = (int64_t)blockIdx.x * kBM;
+  const int n0 = blockIdx.y * BN;
+  const int z = blockIdx.z;
+  const int num_kb = (int)((p.K + kBK - 1) / kBK);
+
+  // batch offsets
+  int64_t a_off = 0, c_off = 0;
+  int b_plane = 0;
+  {
+    int64_t rem = z;
+    for (int d = p.batch_rank - 1; d >= 0; --d) {
+      const int64_t c = rem % p.batch_shape[d];
+      rem /= p.batch_shape[d];
+      a_off += c * p.a_bst[d];
+      c_off += c * p.c_bst[d];
+      b_plane += (int)(c * p.b_bst[d]);
+    }
+  }
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full_a[s]), 4);
+      mbar_init(smem_u32(&full_b[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&tfull[b]), 1);
+      mbar_init(smem_u32(&tempty[b]), 4);
+    }
+    mbar_init(smem_u32(done), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 4) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"((uint32_t)L::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp < 4) {
+    // ------------------------------------------------------------------ A producer
+    const int chunk = lane & 7;
+    const int rsub = lane >> 3;
+    int64_t rbase[8];
+    int ih0[8], iw0[8];
+    const int64_t PQ = p.P * p.Q;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t m = m0 + warp * 32 + i * 4 + rsub;
+      if (m < p.M) {
+        const int64_t img = m / PQ, pq = m % PQ;
+        const int64_t pp = pq / p.Q, qq = pq % p.Q;
+        rbase[i] = a_off + img * p.x_sn;
+        ih0[i] = (int)(pp * p.sh - p.ph);
+        iw0[i] = (int)(qq * p.sw - p.pw);
+      } else {
+        rbase[i] = -1;
+        ih0[i] = 0;
+        iw0[i] = 0;
+      }
+    }
+    auto load_kb = [&](int kb, float4 (&v)[8]) {
+      const int64_t k0 = (int64_t)kb * kBK + chunk * 4;
+      int r = 0, s = 0;
+      int64_t c = 0;
+      const bool kin = k0 < p.K;
+      if (kin) {
+        const int64_t rs = k0 / p.C;
+        c = k0 - rs * p.C;
+        r = (int)(rs / p.S);
+        s = (int)(rs - (int64_t)r * p.S);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int ih = ih0[i] + r * p.dh, iw = iw0[i] + s * p.dw;
+        if (kin && rbase[i] >= 0 && ih >= 0 && ih < p.H && iw >= 0 && iw < p.W) {
+          v[i] = __ldg(reinterpret_cast<const float4*>(p.x + rbase[i] + ih * p.x_sh + iw * p.x_sw + c));
+        } else {
+          v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+    };
+    float4 cur[8], nxt[8];
+    if (num_kb > 0) load_kb(0, cur);
+    for (int kb = 0; kb < num_kb; ++kb) {
+      const int st = kb % STAGES;
+      const uint32_t ph = (kb / STAGES) & 1;
+      if (kb + 1 < num_kb) load_kb(kb + 1, nxt);
+      if (!mbar_wait(smem_u32(&empty[st]), ph ^ 1, abort_flag, p.status)) break;
+      uint8_t* a_hi = smem + st * L::kStage;
+      uint8_t* a_lo = a_hi + L::kATile;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int row = warp * 32 + i * 4 + rsub;
+        const int off = row * 128 + ((chunk ^ (row & 7)) << 4);
+        const float4 x = cur[i];
+        const float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
+        const float4 l = make_float4(__fsub_rn(x.x, h.x), __fsub_rn(x.y, h.y), __fsub_rn(x.z, h.z), __fsub_rn(x.w, h.w));
+        *reinterpret_cast<float4*>(a_hi + off) = h;
+        *reinterpret_cast<float4*>(a_lo + off) = l;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&full_a[st]));
+#pragma unroll
+      for (int i = 0; i < 8; ++i) cur[i] = nxt[i];
+    }
+  } else if (warp == 4) {
+    // ------------------------------------------------------------------ B producer (TMA)
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_hi)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_lo)) : "memory");
+      int issued = 0;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int st = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        if (!mbar_wait(smem_u32(&empty[st]), ph ^ 1, abort_flag, p.status)) break;
+        uint8_t* b_hi = smem + st * L::kStage + 2 * L::kATile;
+        uint8_t* b_lo = b_hi + L::kBTile;
+        const uint32_t bar = smem_u32(&full_b[st]);
+        mbar_arrive_tx(bar, 2 * L::kBTile);
+        tma_load_3d(smem_u32(b_hi), &tm_hi, bar, kb * kBK, n0, b_plane);
+        tma_load_3d(smem_u32(b_lo), &tm_lo, bar, kb * kBK, n0, b_plane);
+        issued = kb + 1;
+      }
+      if (*abort_flag) {
+        // let copies already in flight land before the CTA retires
+        for (int kb = issued - STAGES < 0 ? 0 : issued - STAGES; kb < issued; ++kb) {
+          volatile int never = 0;
+          mbar_wait(smem_u32(&full_b[kb % STAGES]), (kb / STAGES) & 1, &never, nullptr);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_tf32<BN>();
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int st = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        const int buf = kb & 1;
+        const uint32_t use = (uint32_t)(kb >> 1) & 1;
+        if (!mbar_wait(smem_u32(&full_a[st]), ph, abort_flag, p.status)) break;
+        if (!mbar_wait(smem_u32(&full_b[st]), ph, abort_flag, p.status)) break;
+        if (!mbar_wait(smem_u32(&tempty[buf]), use ^ 1, abort_flag, p.status)) break;
+        tc_fence_after();
+        const uint32_t a_hi = smem_u32(smem + st * L::kStage);
+        const uint32_t a_lo = a_hi + L::kATile;
+        const uint32_t b_hi = a_hi + 2 * L::kATile;
+        const uint32_t b_lo = b_hi + L::kBTile;
+        const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BN);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 8; ++kk) {
+          const uint32_t koff = kk * 32;  // 8 tf32 = 32 bytes along the swizzled row
+          const uint64_t dah = umma_desc_sw128(a_hi + koff), dal = umma_desc_sw128(a_lo + koff);
+          const uint64_t dbh = umma_desc_sw128(b_hi + koff), dbl = umma_desc_sw128(b_lo + koff);
+          umma_tf32(tmem_d, dal, dbh, idesc, kk != 0);
+          umma_tf32(tmem_d, dah, dbl, idesc, 1);
+          umma_tf32(tmem_d, dah, dbh, idesc, 1);
+        }
+        umma_commit(smem_u32(&empty[st]));
+        umma_commit(smem_u32(&tfull[buf]));
+      }
+      umma_commit(smem_u32(done));
+    }
+  } else {
+    // ------------------------------------------------------------------ accumulate + epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
+    float acc[BN];
+#pragma unroll
+    for (int j = 0; j < BN; ++j) acc[j] = 0.0f;
+    bool ok = true;
+    for (int kb = 0; kb < num_kb; ++kb) {
+      const int buf = kb & 1;
+      const uint32_t use = (uint32_t)(kb >> 1) & 1;
+      if (!mbar_wait(smem_u32(&tfull[buf]), use, abort_flag, p.status)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(lane_base + (uint32_t)(buf * BN + c0), r);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[c0 + j] = __fadd_rn(acc[c0 + j], __uint_as_float(r[j]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&tempty[buf]));
+    }
+    ok = ok && !*abort_flag;
+    const int64_t m = m0 + row;
+    if (ok && m < p.M) {
+      float* crow = p.out + c_off + m * p.ldc;
+      if (EPI == EPI_PROGRAM) {
+        Reg regs[kMaxRegs];
+        int err = 0;
+#pragma unroll
+        for (int j = 0; j < BN; ++j) {
+          const int64_t n = n0 + j;
+          if (n < p.N) {
+            regs[0].f = p.bias ? __fadd_rn(acc[j], p.bias[n]) : acc[j];
+            for (int a = 0; a < p.n_aux; ++a) {
+              int64_t ao = m * p.aux_sm[a] + n * p.aux_sn[a];
+              int64_t rem = z;
+              for (int d = p.batch_rank - 1; d >= 0; --d) {
+                ao += (rem % p.batch_shape[d]) * p.aux_sb[a][d];
+                rem /= p.batch_shape[d];
+              }
+              regs[1 + a].f = p.aux[a][ao];
+            }
+            crow[n * p.ldc_n] = run_program(p.prog, regs, &err).f;
+          }
+        }
+        if (err && p.status) atomicCAS(p.status, 0, err);
+      } else {
+#pragma unroll
+        for (int j = 0; j < BN; ++j) {
+          const int64_t n = n0 + j;
+          float x = acc[j];
+          if (EPI >= EPI_BIAS) x = __fadd_rn(x, n < p.N ? p.bias[n] : 0.f);
+          if (EPI == EPI_BIAS_ADD_RELU) x = __fadd_rn(x, n < p.N ? p.res[c_off + m * p.ldc + n * p.ldc_n] : 0.f);
+          if (EPI == EPI_BIAS_RELU || EPI == EPI_BIAS_ADD_RELU) x = maximumf_(x, 0.0f);
+          acc[j] = x;
+        }
+        const bool vec = p.ldc_n == 1 && n0 + BN <= p.N && ((reinterpret_cast<uintptr_t>(crow + n0) & 15) == 0);
+        if (vec) {
+#pragma unroll
+          for (int j = 0; j < BN; j += 4)
+            *reinterpret_cast<float4*>(crow + n0 + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN; ++j)
+            if (n0 + j < p.N) crow[(int64_t)(n0 + j) * p.ldc_n] = acc[j];
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    // every MMA must have completed before the accumulator memory is released
+    volatile int never = 0;
+    if (lane == 0) mbar_wait(smem_u32(done), 0, &never, p.status);
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"((uint32_t)L::kTmemCols)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+template <int BN, int STAGES, int EPI>
+bool launch_t(const ConvGemmParams& p, const void* tmh, const void* tml, cudaStream_t s) {
+  auto kern = conv_gemm_tc_kernel<BN, STAGES, EPI>;
+  constexpr int smem = Smem<BN, STAGES>::kBytes;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return false;
+    attr = true;
+  }
+  dim3 grid((unsigned)((p.M + kBM - 1) / kBM), (unsigned)((p.N + BN - 1) / BN), (unsigned)p.nb);
+  kern<<<grid, kThreadsTC, smem, s>>>(p, *static_cast<const CUtensorMap*>(tmh), *static_cast<const CUtensorMap*>(tml));
+  return true;
+}
+
+template <int BN, int STAGES>
+bool launch_epi(const ConvGemmParams& p, const void* tmh, const void* tml, cudaStream_t s) {
+  switch (p.epi) {
+    case EPI_NONE: return launch_t<BN, STAGES, EPI_NONE>(p, tmh, tml, s);
+    case EPI_BIAS: return launch_t<BN, STAGES, EPI_BIAS>(p, tmh, tml, s);
+    case EPI_BIAS_RELU: return launch_t<BN, STAGES, EPI_BIAS_RELU>(p, tmh, tml, s);
+    case EPI_BIAS_ADD_RELU: return launch_t<BN, STAGES, EPI_BIAS_ADD_RELU>(p, tmh, tml, s);
+    case EPI_PROGRAM: return launch_t<BN, STAGES, EPI_PROGRAM>(p, tmh, tml, s);
+    default: return false;
+  }
+}
+
+}  // namespace
+
+int conv_gemm_smem_bytes(int block_n) {
+  return block_n == 64 ? Smem<64, 4>::kBytes : Smem<128, 3>::kBytes;
+}
+
+bool make_b_tensor_maps(const float* hi, const float* lo, int64_t batch, int64_t N, int64_t ldk, int block_n,
+                        void* tmap_hi_out, void* tmap_lo_out) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  if (ldk % 4 != 0 || (reinterpret_cast<uintptr_t>(hi) & 15) || (reinterpret_cast<uintptr_t>(lo) & 15)) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)ldk, (cuuint64_t)N, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(ldk * 4), (cuuint64_t)(N * ldk * 4)};
+  cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)block_n, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  for (int k = 0; k < 2; ++k) {
+    CUtensorMap* m = static_cast<CUtensorMap*>(k == 0 ? tmap_hi_out : tmap_lo_out);
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(k == 0 ? hi : lo), dims, strides, box,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return false;
+  }
+  return true;
+}
+
+bool launch_conv_gemm_tc(const ConvGemmParams& p, const void* tmap_hi, const void* tmap_lo, int block_n,
+                         cudaStream_t s) {
+  if (p.M <= 0 || p.N <= 0 || p.nb <= 0) return true;
+  if (p.K <= 0) return false;  // an empty reduction would leave tensor memory unwritten
+  // 16-byte A gathers need channel counts and strides in whole float4s
+  if (p.C % 4 != 0 || p.x_sh % 4 != 0 || p.x_sw % 4 != 0 || p.x_sn % 4 != 0 ||
+      (reinterpret_cast<uintptr_t>(p.x) & 15))
+    return false;
+  for (int d = 0; d < p.batch_rank; ++d)
+    if (p.a_bst[d] % 4 != 0) return false;
+  if (p.nb > 65535 || (p.N + block_n - 1) / block_n > 65535) return false;
+  if (block_n == 64) return launch_epi<64, 4>(p, tmap_hi, tmap_lo, s);
+  if (block_n == 128) return launch_epi<128, 3>(p, tmap_hi, tmap_lo, s);
+  return false;
+}
+
+}  // namespace kern
+}  // namespace gawee

@@ -1,0 +1,263 @@
+// Launch interfaces of the sm_100a kernels used by the gawee CUDA runtime.
+// Plain structs passed by value as kernel parameters; no torch types.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace gawee {
+namespace kern {
+
+constexpr int kMaxRank = 8;
+constexpr int kMaxIn = 8;
+constexpr int kMaxInstr = 40;
+constexpr int kMaxRegs = 32;
+
+// Device-side dtype codes (same numbering as gawee::DType).
+enum DT : int8_t { DT_F32 = 0, DT_F64 = 1, DT_F16 = 2, DT_I64 = 3, DT_I32 = 4, DT_I1 = 5, DT_INDEX = 6 };
+
+// Error codes written to the per-context device status word.
+enum Status : int {
+  ST_OK = 0,
+  ST_GATHER_INDEX = 1,     // gather index outside the table
+  ST_BARRIER_TIMEOUT = 2,  // a bounded mbarrier wait in a tensor-core kernel gave up
+  ST_BAD_PROGRAM = 3,      // elementwise program with an unknown opcode
+  ST_INT_DIV_ZERO = 4,
+  ST_SLICE_BOUNDS = 5,
+};
+
+struct DInstr {
+  uint8_t op, ty, rty;
+  int8_t pred;
+  int8_t dst, a, b, c;
+  double fimm;
+  long long iimm;
+};
+
+struct DProgram {
+  int n_code;
+  int n_args;
+  int result;
+  DInstr code[kMaxInstr];
+};
+
+// A strided operand over the iteration space of an elementwise launch.
+struct EwOperand {
+  void* ptr;
+  int64_t st[kMaxRank];  // element strides per iteration dim (0 = broadcast)
+  int8_t dt;
+};
+
+struct EwParams {
+  int rank;
+  int n_in;
+  int64_t numel;
+  int64_t shape[kMaxRank];  // iteration space (output shape, dims ordered outer..inner)
+  EwOperand out;
+  EwOperand in[kMaxIn];
+  DProgram prog;
+  int* status;
+};
+
+void launch_elementwise(const EwParams& p, cudaStream_t s);
+
+// Reduction of `cols` elements per output row.  Input offset of (row, col) is
+// unravel(row over kept dims) . kept strides + unravel(col over reduced dims) . red strides.
+struct ReduceParams {
+  const float* in;
+  float* out;              // out[row]; contiguous rows in output order
+  int64_t rows, cols;
+  int kept_rank, red_rank;
+  int64_t kept_shape[kMaxRank], kept_st[kMaxRank];
+  int64_t red_shape[kMaxRank], red_st[kMaxRank];
+  int64_t out_st[kMaxRank];  // output strides over kept dims
+  int mode;                // 0 sum, 1 mean (sum / count)
+  float count;
+};
+void launch_reduce_f32(const ReduceParams& p, cudaStream_t s);
+
+// linalg.reduce with an arbitrary scalar body: one thread per output element,
+// sequential over the reduced elements in input row-major order (the
+// reference loop order).  The output already holds the init values.
+struct GenericReduceParams {
+  const void* in;
+  void* out;
+  int8_t in_dt, out_dt;
+  int64_t rows, cols;
+  int kept_rank, red_rank;
+  int64_t kept_shape[kMaxRank], kept_st[kMaxRank];
+  int64_t red_shape[kMaxRank], red_st[kMaxRank];
+  int64_t out_st[kMaxRank];
+  DProgram prog;  // registers 0 = input element, 1 = accumulator
+  int* status;
+};
+void launch_generic_reduce(const GenericReduceParams& p, cudaStream_t s);
+
+// Softmax along one axis: rows x len, element (row, j) at in + row_off(row) + j * axis_st.
+struct SoftmaxParams {
+  const float* in;
+  float* out;
+  int64_t rows, len;
+  int rank;                       // rank of the row space
+  int64_t row_shape[kMaxRank], in_row_st[kMaxRank], out_row_st[kMaxRank];
+  int64_t in_axis_st, out_axis_st;
+};
+void launch_softmax(const SoftmaxParams& p, cudaStream_t s);
+
+// out[pre, j, post] = data[pre, idx[j], post] with data contiguous [pre, axis, post].
+struct GatherParams {
+  const void* data;
+  const void* idx;     // i64 or i32 index tensor, contiguous
+  void* out;           // contiguous [pre, nidx, post]
+  int8_t idx_dt;
+  int elem_bytes;
+  int64_t pre, axis_len, nidx, post;
+  int* status;
+};
+void launch_gather(const GatherParams& p, cudaStream_t s);
+
+// out[i] = data[i with dim `axis` replaced by idx[i]]; all contiguous.
+struct GatherElementsParams {
+  const void* data;
+  const void* idx;
+  void* out;
+  int8_t idx_dt;
+  int elem_bytes;
+  int rank, axis;
+  int64_t numel;
+  int64_t shape[kMaxRank];       // output/index shape
+  int64_t data_st[kMaxRank];     // data strides (elements)
+  int64_t data_axis_len;
+  int* status;
+};
+void launch_gather_elements(const GatherElementsParams& p, cudaStream_t s);
+
+// Per-dim index remap copy: src coordinate = ((o / div) % mod) - sub; outside
+// [0, src_dim) reads `fill`.  Used for pad, tile and nearest resize.
+struct RemapParams {
+  const void* in;
+  void* out;
+  int elem_bytes;
+  int rank;
+  int64_t numel;
+  int64_t out_shape[kMaxRank], out_st[kMaxRank];
+  int64_t in_shape[kMaxRank], in_st[kMaxRank];
+  int64_t div[kMaxRank], mod[kMaxRank], sub[kMaxRank];
+  uint64_t fill_bits;
+};
+void launch_remap(const RemapParams& p, cudaStream_t s);
+
+// out[i] = start + i * delta
+struct RangeParams {
+  void* out;
+  int8_t dt;
+  int64_t n;
+  double fstart, fdelta;
+  long long istart, idelta;
+};
+void launch_range(const RangeParams& p, cudaStream_t s);
+
+// Max / sum pooling over (n, c, oh, ow) with arbitrary strides on both sides.
+struct PoolParams {
+  const float* in;
+  float* out;
+  int64_t N, C, H, W, OH, OW;
+  int64_t in_st[4], out_st[4];  // n, c, h, w strides
+  int kh, kw, sh, sw, ph, pw, dh, dw;
+  int mode;                      // 0 max (pad -inf), 1 sum / count (pad 0)
+  float count;
+  int64_t iter_perm[4];          // iteration order of output dims, outermost first
+};
+void launch_pool(const PoolParams& p, cudaStream_t s);
+
+// Rank-2 top-k following the reference's selection loop.
+struct TopKParams {
+  const float* in;
+  float* vals;
+  int64_t* idxs;
+  unsigned char* used;  // rows x len scratch flags
+  int64_t rows, len, k;
+};
+void launch_topk(const TopKParams& p, cudaStream_t s);
+
+// Pack a B operand for the tensor-core kernels into split-precision planes
+// hi/lo of shape [batch][N][ldk] (row-major, zero for k >= K), where hi = x
+// with the low 13 mantissa bits cleared (an exact TF32 value) and lo = x - hi.
+// Source element (b, k, n) is read at
+//   src + boff(b) + sum_d kc_d * k_st[d] + n * sn
+// where k is unravelled over k_shape (outer..inner) into coordinates kc_d; a
+// coordinate kc_d >= k_valid[d] reads zero (used for channel padding).
+struct PackBParams {
+  const float* src;
+  float* hi;
+  float* lo;
+  int64_t batch, K, N, ldk;
+  int64_t sn;
+  int k_rank;
+  int64_t k_shape[3], k_st[3], k_valid[3];
+  int batch_rank;
+  int64_t batch_shape[4], batch_st[4];
+};
+void launch_pack_b(const PackBParams& p, cudaStream_t s);
+
+// ---------------------------------------------------------------------------
+// Tensor-core contraction: implicit-GEMM convolution / (batched) GEMM.
+// C[z][m][n] = sum_k A[z][m][k] * B[z][n][k]  (+ epilogue)
+// The A operand is gathered: for row m = (img, p, q) and k = (r, s, c):
+//   A = x[img*x_sn + (p*sh - ph + r*dh)*x_sh + (q*sw - pw + s*dw)*x_sw + c]
+// with zero outside the image (implicit zero padding); a plain GEMM is the
+// 1x1 case with P = rows, Q = 1.  The B operand is read from packed TF32
+// hi/lo planes with TMA.  Products use three TF32 tcgen05 MMAs
+// (hi*hi + hi*lo + lo*hi) accumulated in fp32 in tensor memory.
+// ---------------------------------------------------------------------------
+enum Epi : int {
+  EPI_NONE = 0,       // C = acc
+  EPI_BIAS = 1,       // C = acc + bias[n]
+  EPI_BIAS_RELU = 2,  // C = max(acc + bias[n], 0)
+  EPI_BIAS_ADD_RELU = 3,  // C = max((acc + bias[n]) + res[m][n], 0)
+  EPI_PROGRAM = 4,    // C = program(acc, aux...) with aux operands indexed like C
+};
+
+struct ConvGemmParams {
+  // A gather
+  const float* x;
+  int64_t x_sn, x_sh, x_sw;     // c stride is 1
+  int64_t H, W, C;              // input spatial size and channels
+  int64_t P, Q;                 // output spatial size (GEMM: P = M, Q = 1)
+  int R, S, sh, sw, ph, pw, dh, dw;
+  int64_t M, N, K;              // M = imgs*P*Q, N = out channels, K = R*S*C
+  // batching (GEMM only; conv uses nb = 1)
+  int nb;
+  int batch_rank;
+  int64_t batch_shape[4];
+  int64_t a_bst[4];             // A batch strides (elements)
+  int64_t b_bst[4];             // B batch strides (planes)
+  int64_t c_bst[4];             // C batch strides (elements)
+  // output
+  float* out;
+  int64_t ldc;                  // row stride of C
+  int64_t ldc_n;                // column stride of C (1 unless transposed output)
+  int epi;
+  const float* bias;            // [N]
+  const float* res;             // residual, same indexing as C
+  // EPI_PROGRAM operands: register 0 = accumulator, 1.. = aux loads
+  int n_aux;
+  const float* aux[4];
+  int64_t aux_sm[4], aux_sn[4], aux_sb[4][4];
+  DProgram prog;
+  int* status;
+};
+
+// Returns false (and launches nothing) when the shape is not supported.
+bool launch_conv_gemm_tc(const ConvGemmParams& p, const void* tmap_hi, const void* tmap_lo, int block_n,
+                         cudaStream_t s);
+
+// Build the TMA descriptors for packed B planes [batch][N][ldk] (fp32).
+bool make_b_tensor_maps(const float* hi, const float* lo, int64_t batch, int64_t N, int64_t ldk, int block_n,
+                        void* tmap_hi_out, void* tmap_lo_out);
+
+// Shared-memory bytes the tensor-core kernel requests for a given block_n.
+int conv_gemm_smem_bytes(int block_n);
+
+}  // namespace kern
+}  // namespace gawee

@@ -1,0 +1,512 @@
+// Memory-bound kernels of the gawee CUDA runtime: strided elementwise programs,
+// reductions, softmax, gather, index remaps, pooling, top-k and the packing of
+// tensor-core B operands.  Grids are sized as multiples of the SM count and
+// use grid-stride loops.
+#include <cfloat>
+#include <cstdio>
+
+#include "kernels.h"
+#include "program.cuh"
+
+namespace gawee {
+namespace kern {
+
+namespace {
+
+constexpr int kThreads = 256;
+
+int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+unsigned grid_for(int64_t work, int per_block = kThreads, int waves = 8) {
+  int64_t g = (work + per_block - 1) / per_block;
+  int64_t cap = (int64_t)sm_count() * waves;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return (unsigned)g;
+}
+
+__device__ __forceinline__ void set_status(int* st, int code) {
+  if (st) atomicCAS(st, 0, code);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Elementwise: one program run per output element; operands addressed through
+// per-dimension strides over the iteration space (0 = broadcast).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads) elementwise_kernel(const __grid_constant__ EwParams p) {
+  Reg regs[kMaxRegs];
+  int err = 0;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < p.numel; i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rem = i;
+    int64_t off_out = 0;
+    int64_t off_in[kMaxIn];
+#pragma unroll
+    for (int k = 0; k < kMaxIn; ++k) off_in[k] = 0;
+    for (int d = p.rank - 1; d >= 0; --d) {
+      int64_t c = rem % p.shape[d];
+      rem /= p.shape[d];
+      off_out += c * p.out.st[d];
+#pragma unroll
+      for (int k = 0; k < kMaxIn; ++k)
+        if (k < p.n_in) off_in[k] += c * p.in[k].st[d];
+    }
+#pragma unroll
+    for (int k = 0; k < kMaxIn; ++k)
+      if (k < p.n_in) regs[k] = load_dt(p.in[k].ptr, off_in[k], p.in[k].dt);
+    Reg r = run_program(p.prog, regs, &err);
+    store_dt(p.out.ptr, off_out, p.out.dt, r);
+  }
+  if (err) set_status(p.status, err);
+}
+
+// Contiguous float fast path: all operands f32 with identical dense layout or
+// scalar broadcast, processed four elements at a time.
+__global__ void __launch_bounds__(kThreads) elementwise_dense4_kernel(const __grid_constant__ EwParams p,
+                                                                      unsigned scalar_mask) {
+  Reg regs[kMaxRegs];
+  int err = 0;
+  const int64_t n4 = p.numel / 4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 v[kMaxIn];
+#pragma unroll
+    for (int k = 0; k < kMaxIn; ++k) {
+      if (k < p.n_in) {
+        if (scalar_mask & (1u << k)) {
+          float s = static_cast<const float*>(p.in[k].ptr)[0];
+          v[k] = make_float4(s, s, s, s);
+        } else {
+          v[k] = reinterpret_cast<const float4*>(p.in[k].ptr)[i];
+        }
+      }
+    }
+    float4 o;
+    float* op = reinterpret_cast<float*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+#pragma unroll
+      for (int k = 0; k < kMaxIn; ++k)
+        if (k < p.n_in) regs[k].f = reinterpret_cast<float*>(&v[k])[e];
+      op[e] = run_program(p.prog, regs, &err).f;
+    }
+    reinterpret_cast<float4*>(p.out.ptr)[i] = o;
+  }
+  // tail
+  for (int64_t i = n4 * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < p.numel;
+       i += (int64_t)gridDim.x * blockDim.x) {
+#pragma unroll
+    for (int k = 0; k < kMaxIn; ++k)
+      if (k < p.n_in) regs[k].f = static_cast<const float*>(p.in[k].ptr)[(scalar_mask & (1u << k)) ? 0 : i];
+    static_cast<float*>(p.out.ptr)[i] = run_program(p.prog, regs, &err).f;
+  }
+  if (err) set_status(p.status, err);
+}
+
+void launch_elementwise(const EwParams& p, cudaStream_t s) {
+  if (p.numel <= 0) return;
+  // Dense float fast path: rank-1 iteration, unit strides or scalars, 16-byte aligned.
+  bool dense = p.rank == 1 && p.out.dt == DT_F32 && p.out.st[0] == 1 &&
+               (reinterpret_cast<uintptr_t>(p.out.ptr) & 15) == 0;
+  unsigned scalar_mask = 0;
+  for (int k = 0; dense && k < p.n_in; ++k) {
+    if (p.in[k].dt != DT_F32) dense = false;
+    else if (p.in[k].st[0] == 0) scalar_mask |= 1u << k;
+    else if (p.in[k].st[0] != 1 || (reinterpret_cast<uintptr_t>(p.in[k].ptr) & 15) != 0) dense = false;
+  }
+  if (dense) {
+    elementwise_dense4_kernel<<<grid_for(p.numel / 4 + 1), kThreads, 0, s>>>(p, scalar_mask);
+  } else {
+    elementwise_kernel<<<grid_for(p.numel), kThreads, 0, s>>>(p);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Float sum / mean reductions: one warp per output row.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int64_t unravel_off(int64_t idx, int rank, const int64_t* shape, const int64_t* st) {
+  int64_t off = 0;
+  for (int d = rank - 1; d >= 0; --d) {
+    int64_t c = idx % shape[d];
+    idx /= shape[d];
+    off += c * st[d];
+  }
+  return off;
+}
+
+__global__ void __launch_bounds__(kThreads) reduce_f32_kernel(const __grid_constant__ ReduceParams p) {
+  const int warps = blockDim.x / 32;
+  const int lane = threadIdx.x & 31;
+  for (int64_t row = blockIdx.x * (int64_t)warps + threadIdx.x / 32; row < p.rows; row += (int64_t)gridDim.x * warps) {
+    const int64_t base = unravel_off(row, p.kept_rank, p.kept_shape, p.kept_st);
+    float acc = 0.0f;
+    if (p.red_rank == 1 && p.red_st[0] == 1) {
+      const float* rp = p.in + base;
+      for (int64_t c = lane; c < p.cols; c += 32) acc += rp[c];
+    } else {
+      for (int64_t c = lane; c < p.cols; c += 32) acc += p.in[base + unravel_off(c, p.red_rank, p.red_shape, p.red_st)];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) {
+      const int64_t oo = unravel_off(row, p.kept_rank, p.kept_shape, p.out_st);
+      p.out[oo] = p.mode == 1 ? __fdiv_rn(acc, p.count) : acc;
+    }
+  }
+}
+
+void launch_reduce_f32(const ReduceParams& p, cudaStream_t s) {
+  if (p.rows <= 0) return;
+  reduce_f32_kernel<<<grid_for(p.rows, kThreads / 32), kThreads, 0, s>>>(p);
+}
+
+__global__ void __launch_bounds__(kThreads) generic_reduce_kernel(const __grid_constant__ GenericReduceParams p) {
+  Reg regs[kMaxRegs];
+  int err = 0;
+  for (int64_t row = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; row < p.rows; row += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t base = unravel_off(row, p.kept_rank, p.kept_shape, p.kept_st);
+    const int64_t oo = unravel_off(row, p.kept_rank, p.kept_shape, p.out_st);
+    Reg acc = load_dt(p.out, oo, p.out_dt);
+    for (int64_t c = 0; c < p.cols; ++c) {
+      regs[0] = load_dt(p.in, base + unravel_off(c, p.red_rank, p.red_shape, p.red_st), p.in_dt);
+      regs[1] = acc;
+      acc = run_program(p.prog, regs, &err);
+    }
+    store_dt(p.out, oo, p.out_dt, acc);
+  }
+  if (err) set_status(p.status, err);
+}
+
+void launch_generic_reduce(const GenericReduceParams& p, cudaStream_t s) {
+  if (p.rows <= 0) return;
+  generic_reduce_kernel<<<grid_for(p.rows), kThreads, 0, s>>>(p);
+}
+
+// ---------------------------------------------------------------------------
+// Softmax (linalg.softmax decomposition: max from the lowest finite float,
+// exp(x - max), sum, divide).  One warp per row for short rows, a block per
+// row for long ones.
+// ---------------------------------------------------------------------------
+template <int WARPS_PER_ROW>
+__global__ void __launch_bounds__(kThreads) softmax_kernel(const __grid_constant__ SoftmaxParams p) {
+  __shared__ float red[kThreads / 32];
+  constexpr int kRowThreads = 32 * WARPS_PER_ROW;
+  const int rows_per_block = kThreads / kRowThreads;
+  const int t = threadIdx.x % kRowThreads;
+  const int sub = threadIdx.x / kRowThreads;
+  const int lane = threadIdx.x & 31;
+  const int wid = t / 32;
+  for (int64_t rb = blockIdx.x * (int64_t)rows_per_block; rb < p.rows; rb += (int64_t)gridDim.x * rows_per_block) {
+    const int64_t row = rb + sub;
+    const bool active = row < p.rows;
+    const float* x = active ? p.in + unravel_off(row, p.rank, p.row_shape, p.in_row_st) : p.in;
+    float* y = active ? p.out + unravel_off(row, p.rank, p.row_shape, p.out_row_st) : p.out;
+    float m = -FLT_MAX;
+    if (active)
+      for (int64_t j = t; j < p.len; j += kRowThreads) m = fmaxf(m, x[j * p.in_axis_st]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (WARPS_PER_ROW > 1) {
+      if (lane == 0) red[threadIdx.x / 32] = m;
+      __syncthreads();
+      m = -FLT_MAX;
+      for (int w = 0; w < WARPS_PER_ROW; ++w) m = fmaxf(m, red[sub * WARPS_PER_ROW + w]);
+      __syncthreads();
+    }
+    float ssum = 0.0f;
+    if (active)
+      for (int64_t j = t; j < p.len; j += kRowThreads) {
+        float e = expf(__fsub_rn(x[j * p.in_axis_st], m));
+        y[j * p.out_axis_st] = e;
+        ssum += e;
+      }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
+    if (WARPS_PER_ROW > 1) {
+      if (lane == 0) red[threadIdx.x / 32] = ssum;
+      __syncthreads();
+      ssum = 0.0f;
+      for (int w = 0; w < WARPS_PER_ROW; ++w) ssum += red[sub * WARPS_PER_ROW + w];
+      __syncthreads();
+    }
+    (void)wid;
+    if (active)
+      for (int64_t j = t; j < p.len; j += kRowThreads) y[j * p.out_axis_st] = __fdiv_rn(y[j * p.out_axis_st], ssum);
+  }
+}
+
+void launch_softmax(const SoftmaxParams& p, cudaStream_t s) {
+  if (p.rows <= 0) return;
+  if (p.len <= 1024) {
+    softmax_kernel<1><<<grid_for(p.rows, kThreads / 32), kThreads, 0, s>>>(p);
+  } else {
+    softmax_kernel<8><<<grid_for(p.rows, 1), kThreads, 0, s>>>(p);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Gather
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ long long load_index(const void* idx, int64_t j, int dt) {
+  return dt == DT_I32 ? (long long)static_cast<const int*>(idx)[j] : static_cast<const long long*>(idx)[j];
+}
+
+__global__ void __launch_bounds__(kThreads) gather_rows16_kernel(const __grid_constant__ GatherParams p) {
+  // post * elem_bytes is a multiple of 16: copy 16-byte chunks
+  const int64_t chunks = p.post * p.elem_bytes / 16;
+  const int64_t total = p.pre * p.nidx * chunks;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = i % chunks;
+    const int64_t j = (i / chunks) % p.nidx;
+    const int64_t a = i / (chunks * p.nidx);
+    long long v = load_index(p.idx, j, p.idx_dt);
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (v < 0 || v >= p.axis_len) {
+      set_status(p.status, ST_GATHER_INDEX);
+    } else {
+      val = reinterpret_cast<const uint4*>(p.data)[(a * p.axis_len + v) * chunks + c];
+    }
+    reinterpret_cast<uint4*>(p.out)[i] = val;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) gather_elems_kernel(const __grid_constant__ GatherParams p) {
+  const int64_t total = p.pre * p.nidx * p.post;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t q = i % p.post;
+    const int64_t j = (i / p.post) % p.nidx;
+    const int64_t a = i / (p.post * p.nidx);
+    long long v = load_index(p.idx, j, p.idx_dt);
+    const unsigned char* src = static_cast<const unsigned char*>(p.data);
+    unsigned char* dst = static_cast<unsigned char*>(p.out) + i * p.elem_bytes;
+    if (v < 0 || v >= p.axis_len) {
+      set_status(p.status, ST_GATHER_INDEX);
+      for (int b = 0; b < p.elem_bytes; ++b) dst[b] = 0;
+    } else {
+      src += ((a * p.axis_len + v) * p.post + q) * p.elem_bytes;
+      for (int b = 0; b < p.elem_bytes; ++b) dst[b] = src[b];
+    }
+  }
+}
+
+void launch_gather(const GatherParams& p, cudaStream_t s) {
+  const int64_t total = p.pre * p.nidx * p.post;
+  if (total <= 0) return;
+  bool vec = (p.post * p.elem_bytes) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.data) & 15) == 0 &&
+             (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
+  if (vec) gather_rows16_kernel<<<grid_for(total * p.elem_bytes / 16), kThreads, 0, s>>>(p);
+  else gather_elems_kernel<<<grid_for(total), kThreads, 0, s>>>(p);
+}
+
+__global__ void __launch_bounds__(kThreads) gather_elements_kernel(const __grid_constant__ GatherElementsParams p) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < p.numel; i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rem = i, off = 0;
+    long long v = load_index(p.idx, i, p.idx_dt);
+    bool ok = v >= 0 && v < p.data_axis_len;
+    for (int d = p.rank - 1; d >= 0; --d) {
+      int64_t c = rem % p.shape[d];
+      rem /= p.shape[d];
+      off += (d == p.axis ? (ok ? v : 0) : c) * p.data_st[d];
+    }
+    if (!ok) set_status(p.status, ST_GATHER_INDEX);
+    const unsigned char* src = static_cast<const unsigned char*>(p.data) + off * p.elem_bytes;
+    unsigned char* dst = static_cast<unsigned char*>(p.out) + i * p.elem_bytes;
+    for (int b = 0; b < p.elem_bytes; ++b) dst[b] = ok ? src[b] : 0;
+  }
+}
+
+void launch_gather_elements(const GatherElementsParams& p, cudaStream_t s) {
+  if (p.numel <= 0) return;
+  gather_elements_kernel<<<grid_for(p.numel), kThreads, 0, s>>>(p);
+}
+
+// ---------------------------------------------------------------------------
+// Index remap (pad / tile / resize)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads) remap_kernel(const __grid_constant__ RemapParams p) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < p.numel; i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rem = i, src = 0, dst = 0;
+    bool inside = true;
+    for (int d = p.rank - 1; d >= 0; --d) {
+      int64_t o = rem % p.out_shape[d];
+      rem /= p.out_shape[d];
+      dst += o * p.out_st[d];
+      int64_t c = ((o / p.div[d]) % p.mod[d]) - p.sub[d];
+      if (c < 0 || c >= p.in_shape[d]) inside = false;
+      src += c * p.in_st[d];
+    }
+    unsigned char* dp = static_cast<unsigned char*>(p.out) + dst * p.elem_bytes;
+    if (inside) {
+      const unsigned char* sp = static_cast<const unsigned char*>(p.in) + src * p.elem_bytes;
+      for (int b = 0; b < p.elem_bytes; ++b) dp[b] = sp[b];
+    } else {
+      for (int b = 0; b < p.elem_bytes; ++b) dp[b] = (unsigned char)(p.fill_bits >> (8 * b));
+    }
+  }
+}
+
+void launch_remap(const RemapParams& p, cudaStream_t s) {
+  if (p.numel <= 0) return;
+  remap_kernel<<<grid_for(p.numel), kThreads, 0, s>>>(p);
+}
+
+__global__ void range_kernel(const __grid_constant__ RangeParams p) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < p.n; i += (int64_t)gridDim.x * blockDim.x) {
+    Reg r;
+    r.i = 0;
+    if (p.dt == DT_F32) r.f = __fadd_rn((float)p.fstart, __fmul_rn((float)i, (float)p.fdelta));
+    else if (p.dt == DT_F64) r.d = p.fstart + (double)i * p.fdelta;
+    else r.i = wrap_((long long)((unsigned long long)p.istart + (unsigned long long)i * (unsigned long long)p.idelta), p.dt);
+    store_dt(p.out, i, p.dt, r);
+  }
+}
+
+void launch_range(const RangeParams& p, cudaStream_t s) {
+  if (p.n <= 0) return;
+  range_kernel<<<grid_for(p.n), kThreads, 0, s>>>(p);
+}
+
+// ---------------------------------------------------------------------------
+// Pooling: one thread per output element, iterated in the output's physical
+// order so that NHWC tensors are read and written coalesced along channels.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads) pool_kernel(const __grid_constant__ PoolParams p) {
+  const int64_t total = p.N * p.C * p.OH * p.OW;
+  const int64_t dims[4] = {p.N, p.C, p.OH, p.OW};
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rem = i, c4[4];
+    for (int k = 3; k >= 0; --k) {
+      int d = (int)p.iter_perm[k];
+      c4[d] = rem % dims[d];
+      rem /= dims[d];
+    }
+    const int64_t n = c4[0], c = c4[1], oh = c4[2], ow = c4[3];
+    const float* base = p.in + n * p.in_st[0] + c * p.in_st[1];
+    float acc = p.mode == 0 ? -INFINITY : 0.0f;
+    for (int kh = 0; kh < p.kh; ++kh) {
+      const int64_t ih = oh * p.sh + kh * p.dh - p.ph;
+      for (int kw = 0; kw < p.kw; ++kw) {
+        const int64_t iw = ow * p.sw + kw * p.dw - p.pw;
+        const bool in = ih >= 0 && ih < p.H && iw >= 0 && iw < p.W;
+        if (p.mode == 0) {
+          const float v = in ? base[ih * p.in_st[2] + iw * p.in_st[3]] : -INFINITY;
+          acc = maximumf_(acc, v);
+        } else {
+          const float v = in ? base[ih * p.in_st[2] + iw * p.in_st[3]] : 0.0f;
+          acc = __fadd_rn(acc, v);
+        }
+      }
+    }
+    if (p.mode == 1) acc = __fdiv_rn(acc, p.count);
+    p.out[n * p.out_st[0] + c * p.out_st[1] + oh * p.out_st[2] + ow * p.out_st[3]] = acc;
+  }
+}
+
+void launch_pool(const PoolParams& p, cudaStream_t s) {
+  const int64_t total = p.N * p.C * p.OH * p.OW;
+  if (total <= 0) return;
+  pool_kernel<<<grid_for(total), kThreads, 0, s>>>(p);
+}
+
+// ---------------------------------------------------------------------------
+// Top-k: one block per row; each round is a block-wide first-strict-max scan
+// over unused positions, as in the reference's selection loop.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads) topk_kernel(const __grid_constant__ TopKParams p) {
+  __shared__ float sv[kThreads];
+  __shared__ long long si[kThreads];
+  for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+    const float* x = p.in + row * p.len;
+    unsigned char* used = p.used + row * p.len;
+    for (int64_t j = threadIdx.x; j < p.len; j += blockDim.x) used[j] = 0;
+    __syncthreads();
+    for (int64_t ki = 0; ki < p.k; ++ki) {
+      float bv = -INFINITY;
+      long long bi = 0;
+      bool found = false;
+      for (int64_t j = threadIdx.x; j < p.len; j += blockDim.x) {
+        float v = x[j];
+        if (!used[j] && v > bv) { bv = v; bi = j; found = true; }
+      }
+      sv[threadIdx.x] = bv;
+      si[threadIdx.x] = found ? bi : (long long)p.len;  // "none" sorts last
+      __syncthreads();
+      for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+        if (threadIdx.x < o) {
+          float v2 = sv[threadIdx.x + o];
+          long long i2 = si[threadIdx.x + o];
+          float v1 = sv[threadIdx.x];
+          long long i1 = si[threadIdx.x];
+          // earliest index with the strictly largest value wins; ties keep the first
+          bool take = (i2 < p.len) && ((i1 >= p.len) || v2 > v1 || (v2 == v1 && i2 < i1));
+          if (take) { sv[threadIdx.x] = v2; si[threadIdx.x] = i2; }
+        }
+        __syncthreads();
+      }
+      if (threadIdx.x == 0) {
+        long long w = si[0];
+        float wv = sv[0];
+        if (w >= p.len) { w = 0; wv = -INFINITY; }
+        p.vals[row * p.k + ki] = wv;
+        p.idxs[row * p.k + ki] = w;
+        used[w] = 1;
+      }
+      __syncthreads();
+    }
+  }
+}
+
+void launch_topk(const TopKParams& p, cudaStream_t s) {
+  if (p.rows <= 0) return;
+  topk_kernel<<<grid_for(p.rows, 1, 4), kThreads, 0, s>>>(p);
+}
+
+// ---------------------------------------------------------------------------
+// B-operand packing into TF32 hi/lo planes [batch][N][ldk].
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads) pack_b_kernel(const __grid_constant__ PackBParams p) {
+  const int64_t total = p.batch * p.N * p.ldk;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t k = i % p.ldk;
+    const int64_t n = (i / p.ldk) % p.N;
+    const int64_t b = i / (p.ldk * p.N);
+    float x = 0.0f;
+    if (k < p.K) {
+      int64_t off = n * p.sn, rem = b;
+      for (int d = p.batch_rank - 1; d >= 0; --d) {
+        off += (rem % p.batch_shape[d]) * p.batch_st[d];
+        rem /= p.batch_shape[d];
+      }
+      bool valid = true;
+      rem = k;
+      for (int d = p.k_rank - 1; d >= 0; --d) {
+        const int64_t c = rem % p.k_shape[d];
+        rem /= p.k_shape[d];
+        if (c >= p.k_valid[d]) valid = false;
+        off += c * p.k_st[d];
+      }
+      if (valid) x = p.src[off];
+    }
+    const float hi = __uint_as_float(__float_as_uint(x) & 0xffffe000u);
+    p.hi[i] = hi;
+    p.lo[i] = __fsub_rn(x, hi);
+  }
+}
+
+void launch_pack_b(const PackBParams& p, cudaStream_t s) {
+  const int64_t total = p.batch * p.N * p.ldk;
+  if (total <= 0) return;
+  pack_b_kernel<<<grid_for(total), kThreads, 0, s>>>(p);
+}
+
+}  // namespace kern
+}  // namespace gawee

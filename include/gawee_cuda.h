@@ -1,0 +1,164 @@
+/*
+ * libgawee_cuda — B200 (sm_100a) backend for compiled inference of a
+ * gawee-dialect `forward` function.
+ *
+ * It replaces the CPU code generation of `gawee-opt --gawee-to-llvm`
+ * (middle/mlir/tools/gawee-opt.cpp:120-184) and the AOT launcher/runtime
+ * (back/gawee_aot.cpp:174-291, back/runtime_support.h) for the same graph:
+ * the graph text that `gawee-onnx-translate` prints is planned into a static
+ * sequence of CUDA kernels, weights stay resident on the GPU, and each
+ * forward replays the sequence.
+ *
+ * Conventions
+ *   - Arguments are the `forward` arguments in order: graph inputs, then the
+ *     float initializers (middle/mlir/lib/Emit/ONNXMLIREmitter.cpp:2932-2975).
+ *   - Host buffers are dense C-order arrays of the argument's static shape;
+ *     the caller owns them.  Boolean (i1) tensors use one byte per element.
+ *   - No exception crosses this interface; every call returns a gawee_status.
+ *     gawee_last_error() returns the message of the last failure on a context.
+ *   - One context per device.  Calls on one context must be serialised by
+ *     the caller; contexts on different devices may be used from different
+ *     host threads.
+ *   - `stream` arguments are cudaStream_t values passed as void* (NULL means
+ *     the context's own stream).
+ */
+#ifndef GAWEE_CUDA_H
+#define GAWEE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int gawee_status;
+enum {
+  GAWEE_OK = 0,
+  GAWEE_ERR_INVALID = 1,      /* bad argument, index, size or state */
+  GAWEE_ERR_PARSE = 2,        /* the MLIR text could not be parsed */
+  GAWEE_ERR_UNSUPPORTED = 3,  /* an op or shape the backend does not implement */
+  GAWEE_ERR_CUDA = 4,         /* a CUDA runtime error */
+  GAWEE_ERR_OOM = 5,          /* device allocation failed */
+  GAWEE_ERR_DEVICE = 6,       /* a kernel reported an error (e.g. gather index out of range) */
+  GAWEE_ERR_NCCL = 7          /* a NCCL call failed */
+};
+
+/* Element types (numbering shared with the planner). */
+enum {
+  GAWEE_F32 = 0,
+  GAWEE_F64 = 1,
+  GAWEE_F16 = 2,
+  GAWEE_I64 = 3,
+  GAWEE_I32 = 4,
+  GAWEE_I1 = 5
+};
+
+typedef struct gawee_ctx gawee_ctx;
+
+/* Plan the function `entry` (NULL = "forward") of MLIR module text for
+ * `device`.  Replaces `gawee-opt --gawee-to-llvm` + `gawee-aot build`
+ * (back/gawee_aot.cpp:325-366): parsing, fusion, memory planning and device
+ * allocation happen here, once. */
+gawee_status gawee_create(const char* mlir_text, const char* entry, int device, gawee_ctx** out);
+
+/* Same, reading the MLIR text from a file. */
+gawee_status gawee_create_from_file(const char* mlir_path, const char* entry, int device, gawee_ctx** out);
+
+void gawee_destroy(gawee_ctx* ctx);
+
+/* Copies the last error message (NUL-terminated, truncated to n). */
+gawee_status gawee_last_error(const gawee_ctx* ctx, char* buf, size_t n);
+
+/* Signature of `forward`: counts, dtypes and static shapes (shape needs room
+ * for `rank` values; rank <= 8).  Mirrors parseFuncSignature
+ * (back/gawee_aot.cpp:104-144). */
+int gawee_num_args(const gawee_ctx* ctx);
+int gawee_num_outputs(const gawee_ctx* ctx);
+gawee_status gawee_arg_info(const gawee_ctx* ctx, int i, int* dtype, int* rank, int64_t* shape);
+gawee_status gawee_output_info(const gawee_ctx* ctx, int i, int* dtype, int* rank, int64_t* shape);
+
+/* Stage argument i from host memory (asynchronous on `stream`; pinned host
+ * memory gives true overlap).  Replaces loadNpy + makeDescriptor per argument
+ * (back/gawee_aot.cpp:241-249).  Weights that are re-staged are re-packed on
+ * the next forward; otherwise packed weights stay resident. */
+gawee_status gawee_set_arg(gawee_ctx* ctx, int i, const void* host, size_t bytes, void* stream);
+
+/* Stage argument i from device memory on the context's device. */
+gawee_status gawee_set_arg_device(gawee_ctx* ctx, int i, const void* dev, size_t bytes, void* stream);
+
+/* Enqueue one forward on `stream`.  Replaces the call of
+ * _mlir_ciface_forward (back/gawee_aot.cpp:263-274).  Asynchronous. */
+gawee_status gawee_forward(gawee_ctx* ctx, void* stream);
+
+/* Copy output i to host memory (asynchronous on `stream`).  Replaces
+ * saveReturnedMemRef (back/runtime_support.h:272-277). */
+gawee_status gawee_get_output(gawee_ctx* ctx, int i, void* host, size_t bytes, void* stream);
+
+/* Device pointer of output i (valid until the next forward). */
+gawee_status gawee_output_device_ptr(gawee_ctx* ctx, int i, void** ptr);
+
+/* Wait for `stream` and check the device status word: returns
+ * GAWEE_ERR_DEVICE if a kernel flagged an error since the last check. */
+gawee_status gawee_synchronize(gawee_ctx* ctx, void* stream);
+
+/* Capture the forward sequence into a CUDA graph on the next forward
+ * (enabled = 1, the default) or launch kernels one by one (0). */
+gawee_status gawee_set_graph_mode(gawee_ctx* ctx, int enabled);
+
+/* Kernel i of the per-forward sequence: name (fused ops joined by '+'),
+ * whether it is a tensor-core contraction, and its algorithmic FLOPs
+ * (2*M*N*K with the unpadded K; 0 for other kernels). */
+gawee_status gawee_op_info(const gawee_ctx* ctx, int i, char* name, size_t n, int* is_tc, double* flops);
+
+/* Run one forward eagerly with a CUDA event between every kernel and write
+ * each kernel's device time in milliseconds to ms[0..gawee_num_kernels-1].
+ * Synchronous. */
+gawee_status gawee_profile_forward(gawee_ctx* ctx, void* stream, float* ms, int n);
+
+/* Plan without a device: parse and plan `entry` of MLIR text and write the
+ * plan summary (or the error message) into buf.  No CUDA call is made. */
+gawee_status gawee_plan_text(const char* mlir_text, const char* entry, char* buf, size_t n);
+
+/* Kernels launched by one forward (planned main-sequence steps) and a
+ * human-readable plan summary. */
+int gawee_num_kernels(const gawee_ctx* ctx);
+gawee_status gawee_plan_summary(const gawee_ctx* ctx, char* buf, size_t n);
+
+/* ---------------------------------------------------------------------------
+ * _mlir_ciface_forward compatibility.
+ *
+ * The reference launcher calls
+ *   void _mlir_ciface_forward(MemRefDescriptor<T,R>* result, MemRefDescriptor<Ti,Ri>* arg0, ...)
+ * (back/gawee_aot.cpp:174-195, struct at back/runtime_support.h:21-28).
+ * gawee_ciface_forward takes the same descriptors as an array: it stages every
+ * argument, runs one forward, waits, and writes the single result into a
+ * malloc'ed buffer described by `result` (the callee allocates, as the
+ * reference's lowered code does).  A memref descriptor is
+ *   { T* allocated; T* aligned; int64_t offset; int64_t sizes[R]; int64_t strides[R]; }
+ * and must describe a dense C-order array.
+ * ------------------------------------------------------------------------- */
+gawee_status gawee_ciface_forward(gawee_ctx* ctx, void* result_desc, void* const* arg_descs, int nargs);
+
+/* ---------------------------------------------------------------------------
+ * Data parallelism: batch sharding with replicated weights (one process or
+ * thread per GPU).  The only collective is the gather of each rank's output
+ * rows to rank 0 over NCCL.
+ * ------------------------------------------------------------------------- */
+#define GAWEE_NCCL_ID_BYTES 128
+
+/* Fill `id` (GAWEE_NCCL_ID_BYTES) on rank 0; share it with the other ranks. */
+gawee_status gawee_dp_unique_id(void* id);
+
+/* Join a communicator of `world` ranks on the context's device. */
+gawee_status gawee_dp_init(gawee_ctx* ctx, int world, int rank, const void* id);
+
+/* Gather output i of every rank (rows of equal size) into `dst` on rank 0
+ * (a device buffer of world * output-size bytes; ignored on other ranks). */
+gawee_status gawee_dp_gather_output(gawee_ctx* ctx, int i, void* dst, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GAWEE_CUDA_H */

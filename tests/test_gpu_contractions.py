@@ -1,0 +1,122 @@
+"""Tensor-core contractions (3xTF32 tcgen05) against the oracle's sequential fp32 sums."""
+import numpy as np
+import pytest
+
+from tests.helpers import _arr, build, compare, parity, rand_input
+
+pytestmark = pytest.mark.gpu
+
+F = "f32"
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 4, 1), (7, 12, 5), (128, 32, 64), (129, 33 * 4, 130), (300, 1000, 257),
+                                   (64, 4608, 512), (1000, 64, 3)])
+def test_matmul_2d(m, k, n):
+    def g_(g):
+        a = rand_input(g, (m, k), 1)
+        b = rand_input(g, (k, n), 2)
+        return [g.matmul(a, b)]
+    # fp32-level error: a few ulps of the sum of |a*b| terms
+    parity(*build(g_), atol=1e-4 * max(1.0, np.sqrt(k) / 8), rtol=1e-4)
+
+
+def _scaled_parity(mlir, args, rel=2e-5):
+    """fp32 sums in a different order agree to a few ulps of the output scale:
+    compare with an absolute tolerance proportional to max|output|."""
+    import oracle
+    from gawee_b200.runtime import Model
+    want = oracle.run(mlir, args)
+    m = Model(mlir)
+    try:
+        got = m.run(args)
+    finally:
+        m.close()
+    for k, (a, b) in enumerate(zip(got, want)):
+        compare(a, b, rel * float(np.max(np.abs(b))), 0.0, f"output{k}")
+
+
+def test_matmul_batched_broadcast():
+    def g_(g):
+        a = rand_input(g, (2, 3, 70, 48), 3)
+        b = rand_input(g, (3, 48, 90), 4)        # batch broadcast over the leading dim
+        c = rand_input(g, (1, 3, 90, 20), 5)     # size-1 batch dim broadcast
+        d = rand_input(g, (20, 33), 6)           # 2-D rhs, batched lhs
+        ab = g.matmul(a, b)
+        return [ab, g.matmul(ab, c), g.matmul(g.matmul(ab, c), d)]
+    _scaled_parity(*build(g_))
+
+
+def test_matmul_transposed_operands():
+    def g_(g):
+        q = rand_input(g, (2, 50, 4, 16), 7)     # [b, s, h, d]
+        k = rand_input(g, (2, 50, 4, 16), 8)
+        qt = g.transpose(q, [0, 2, 1, 3])
+        kt = g.transpose(k, [0, 2, 3, 1])
+        s = g.matmul(qt, kt)                     # [b, h, s, s]
+        return [s, g.matmul(s, g.transpose(k, [0, 2, 1, 3]))]
+    parity(*build(g_), atol=2e-4, rtol=1e-4)
+
+
+def test_linear_bias_and_epilogue():
+    def g_(g):
+        x = rand_input(g, (37, 96), 9)
+        w = rand_input(g, (70, 96), 10)
+        b = rand_input(g, (70,), 11)
+        y = g.linear(x, w, b)
+        return [g.relu(y), g.linear(g.relu(y), rand_input(g, (5, 70), 12), rand_input(g, (5,), 13))]
+    parity(*build(g_), atol=2e-4, rtol=1e-4)
+
+
+def test_matmul_fused_epilogues():
+    def g_(g):
+        x = rand_input(g, (3, 40, 64), 14)
+        w = rand_input(g, (64, 96), 15)
+        bias = rand_input(g, (96,), 16)
+        y = g.add(g.matmul(x, w), bias)
+        gl = g.mul(g.mul(y, g.add(g.erf(g.div(y, g.const(1.4142135381698608, F))), g.const(1.0, F))),
+                   g.const(0.5, F))
+        gate = g.matmul(x, rand_input(g, (64, 96), 17))
+        up = g.matmul(x, rand_input(g, (64, 96), 18))
+        sw = g.mul(g.mul(gate, g.sigmoid(gate)), up)
+        return [gl, sw]
+    parity(*build(g_), atol=2e-4, rtol=1e-4)
+
+
+CONVS = [
+    # (N, C, H, W, F, k, stride, pad, dil)
+    (1, 3, 33, 31, 16, 7, 2, 3, 1),     # stem-like, C=3 -> padded to 4 channels
+    (2, 16, 14, 14, 32, 3, 1, 1, 1),
+    (1, 32, 15, 13, 64, 3, 2, 1, 1),
+    (2, 64, 7, 7, 128, 3, 1, 1, 1),
+    (2, 24, 9, 9, 40, 1, 2, 0, 1),
+    (1, 8, 20, 20, 24, 3, 1, 2, 2),     # dilation 2
+    (1, 12, 6, 5, 200, 3, 1, 0, 1),     # N tail beyond one 128 tile, no padding
+]
+
+
+@pytest.mark.parametrize("n,c,h,w,f,k,s,p,d", CONVS)
+def test_conv(n, c, h, w, f, k, s, p, d):
+    ho = (h + 2 * p - d * (k - 1) - 1) // s + 1
+    wo = (w + 2 * p - d * (k - 1) - 1) // s + 1
+
+    def g_(g):
+        x = rand_input(g, (n, c, h, w), 21)
+        wt = rand_input(g, (f, c, k, k), 22, scale=float(np.sqrt(2.0 / (c * k * k))))
+        b = rand_input(g, (f,), 23, scale=0.1)
+        y = g.op("conv", [x, wt, b], {"strides": _arr([s, s]), "padding": _arr([p, p]), "dilation": _arr([d, d])},
+                 F, (n, f, ho, wo))
+        return [y, g.relu(y)]
+    parity(*build(g_), atol=1e-4, rtol=1e-4)
+
+
+def test_conv_residual_block():
+    def g_(g):
+        x = g.relu(rand_input(g, (2, 32, 10, 10), 31))
+        w1 = rand_input(g, (32, 32, 3, 3), 32, scale=0.08)
+        w2 = rand_input(g, (32, 32, 3, 3), 33, scale=0.08)
+        b1, b2 = rand_input(g, (32,), 34, scale=0.01), rand_input(g, (32,), 35, scale=0.01)
+        att = {"strides": _arr([1, 1]), "padding": _arr([1, 1]), "dilation": _arr([1, 1])}
+        y = g.relu(g.op("conv", [x, w1, b1], att, F, (2, 32, 10, 10)))
+        y = g.op("conv", [y, w2, b2], att, F, (2, 32, 10, 10))
+        return [g.relu(g.add(y, x))]
+    parity(*build(g_), atol=1e-4, rtol=1e-4)

@@ -1,0 +1,181 @@
+"""Per-op parity of the CUDA backend against the CPU oracle (small and odd shapes)."""
+import math
+
+import numpy as np
+import pytest
+
+from tests.helpers import _arr, build, parity, rand_input
+
+pytestmark = pytest.mark.gpu
+
+F = "f32"
+
+
+def test_binary_broadcast_and_ints():
+    def g_(g):
+        a = rand_input(g, (2, 3, 5, 7), 1)
+        b = rand_input(g, (3, 1, 7), 2)
+        c = rand_input(g, (1,), 3)
+        i = rand_input(g, (4, 5), 4, dtype="i64", lo=-50, hi=50)
+        j = rand_input(g, (5,), 5, dtype="i64", lo=1, hi=9)
+        return [g.add(a, b), g.sub(b, a), g.mul(a, c), g.div(a, g.add(g.mul(b, b), c)),
+                g.add(i, j), g.op("div", [i, j], None, "i64", (4, 5)), g.op("mul", [i, j], None, "i64", (4, 5))]
+    parity(*build(g_))
+
+
+def test_unary_activations():
+    def g_(g):
+        x = rand_input(g, (3, 37, 11), 7, scale=3.0)
+        outs = [g.relu(x), g.sigmoid(x), g.erf(x), g.op("tanh", [x], None, F, x.shape),
+                g.op("gelu", [x], None, F, x.shape), g.sqrt(g.mul(x, x)),
+                g.op("hard_sigmoid", [x], {"alpha": "2.000000e-01 : f64", "beta": "5.000000e-01 : f64"}, F, x.shape),
+                g.op("hard_swish", [x], None, F, x.shape),
+                g.op("leaky_relu", [x], {"alpha": "0.0099999997764825821 : f64"}, F, x.shape)]
+        return outs
+    parity(*build(g_), atol=2e-6, rtol=2e-6)
+
+
+def test_relu_nan_and_signed_zero():
+    def g_(g):
+        x = g.input(F, (8,), lambda: np.array([-0.0, 0.0, -1.0, 2.0, np.nan, -np.inf, np.inf, -3.5], np.float32))
+        return [g.relu(x)]
+    got, want = parity(*build(g_))
+    assert np.array_equal(np.signbit(got[0]), np.signbit(want[0]))
+
+
+def test_compare_where_cast_maxmin():
+    def g_(g):
+        a = rand_input(g, (4, 6), 11)
+        b = rand_input(g, (6,), 12)
+        i = rand_input(g, (4, 6), 13, dtype="i64", lo=-3, hi=3)
+        eq = g.op("equal", [i, g.const(0, "i64")], None, "i1", (4, 6))
+        w = g.where(eq, a, g.mul(b, g.const(2.0, F)))
+        c1 = g.cast(eq, 1, F)
+        c2 = g.cast(g.mul(a, g.const(7.5, F)), 7, "i64")
+        c3 = g.cast(i, 1, F)
+        mx = g.op("max", [a, b, g.const(0.25, F)], None, F, (4, 6))
+        mn = g.op("min", [a, b], None, F, (4, 6))
+        return [w, c1, c2, c3, mx, mn, eq]
+    parity(*build(g_))
+
+
+@pytest.mark.parametrize("axes,keep", [([-1], True), ([1], False), ([0, 2], True), ([0, 1, 2], False)])
+def test_reduce_mean_sum(axes, keep):
+    def g_(g):
+        x = rand_input(g, (5, 33, 130), 21)
+        m = g.reduce_mean(x, axes, keep)
+        shape = list(m.shape)
+        s = g.op("reduce_sum", [x], {"axes": _arr(axes), "keepDims": "true" if keep else "false"}, F, tuple(shape))
+        return [m, s]
+    # sums of up to 21450 terms: fp32 summation order differs (tree vs sequential)
+    parity(*build(g_), atol=1e-4, rtol=1e-5)
+
+
+@pytest.mark.parametrize("shape,axis", [((3, 5, 17), -1), ((2, 3, 4, 1500), -1), ((3, 9, 4), 1)])
+def test_softmax(shape, axis):
+    def g_(g):
+        x = rand_input(g, shape, 31, scale=4.0)
+        return [g.softmax(x, axis)]
+    parity(*build(g_), atol=1e-6, rtol=1e-5)
+
+
+def test_gather_and_gather_elements():
+    def g_(g):
+        tab = rand_input(g, (50, 12), 41)
+        ids = rand_input(g, (2, 7), 42, dtype="i64", lo=0, hi=50)
+        x = rand_input(g, (4, 9, 3), 43)
+        idx1 = g.const(np.array([8, 0, 3], np.int64), "i64")
+        ge_idx = rand_input(g, (4, 5, 3), 44, dtype="i64", lo=0, hi=9)
+        return [g.gather(tab, ids, 0), g.gather(x, idx1, 1),
+                g.op("gather_elements", [x, ge_idx], {"axis": "1 : i64"}, F, (4, 5, 3))]
+    parity(*build(g_))
+
+
+def test_layout_views_and_copies():
+    def g_(g):
+        x = rand_input(g, (2, 6, 5, 4), 51)
+        t = g.transpose(x, [0, 2, 3, 1])
+        r = g.reshape(t, (2, 20, 6))            # needs a copy (transposed source)
+        s = g.slice(x, [-5, 1], [6, 5], [1, 2], [2, 2])
+        u = g.unsqueeze(s, [0])
+        c = g.cat([x, g.mul(x, g.const(3.0, F))], 1)
+        e = g.expand(rand_input(g, (1, 6, 1, 4), 52), (2, 6, 5, 4))
+        sp = g.op_multi("split", [x], {"axis": "1 : i64", "splitSizes": _arr([2, 4])},
+                        [(F, (2, 2, 5, 4)), (F, (2, 4, 5, 4))])
+        sq = g.op("squeeze", [u], {"axes": _arr([0])}, F, s.shape)
+        return [r, u, c, e, sp[0], sp[1], sq, g.add(t, g.const(1.0, F))]
+    parity(*build(g_))
+
+
+def test_tile_pad_resize():
+    def g_(g):
+        x = rand_input(g, (2, 3, 4), 61)
+        reps = g.const([2, 1, 3], "i64")
+        t = g.op("tile", [x, reps], None, F, (4, 3, 12))
+        pads = g.const([0, 1, 2, 1, 0, 3], "i64")
+        cv = g.const(-2.5, F)
+        p = g.op("pad", [x, pads, cv], {"mode": '"constant"'}, F, (3, 4, 9))
+        x4 = rand_input(g, (1, 2, 3, 5), 62)
+        sc = g.const([1.0, 1.0, 2.0, 3.0], F)
+        rz = g.op("resize", [x4, sc], {"mode": '"nearest"', "coordinateTransformationMode": '"asymmetric"',
+                                       "nearestMode": '"floor"'}, F, (1, 2, 6, 15))
+        return [t, p, rz]
+    parity(*build(g_))
+
+
+def test_pools():
+    def g_(g):
+        x = rand_input(g, (2, 5, 13, 11), 71)
+        mp = g.op("max_pool", [x], {"kernelSize": _arr([3, 3]), "strides": _arr([2, 2]), "padding": _arr([1, 1]),
+                                    "dilation": _arr([1, 1]), "ceilMode": "false"}, F, (2, 5, 7, 6))
+        ap = g.op("average_pool", [x], {"kernelSize": _arr([2, 3]), "strides": _arr([2, 1]), "padding": _arr([0, 0]),
+                                        "ceilMode": "false", "countIncludePad": "false"}, F, (2, 5, 6, 9))
+        gp = g.op("global_average_pool", [x], None, F, (2, 5, 1, 1))
+        ad = g.op("ad_avg_pool", [x], {"outputSize": _arr([1, 1])}, F, (2, 5, 1, 1))
+        return [mp, ap, gp, ad]
+    parity(*build(g_), atol=1e-6, rtol=1e-6)
+
+
+def test_range_shape_topk():
+    def g_(g):
+        r1 = g.range_(3, 40, 4)
+        rf = g.op("range", [g.const(0.5, F), g.const(9.0, F), g.const(0.75, F)], None, F, (12,))
+        x = g.input(F, (3, 10), lambda: np.array([[1, 5, 5, 2, 9, 9, 0, -1, 3, 9]] * 3, np.float32)
+                    + np.arange(3, dtype=np.float32)[:, None])
+        v, i = g.op_multi("topk", [x], {"k": "4 : i64", "axis": "1 : i64"}, [(F, (3, 4)), ("i64", (3, 4))])
+        sh = g.op("shape", [x], {"start": "0 : i64", "end": "2 : i64"}, "i64", (2,))
+        return [r1, rf, v, i, sh]
+    parity(*build(g_))
+
+
+def test_linalg_forms_from_emitter():
+    def g_(g):
+        x = rand_input(g, (3, 17), 81)
+        p = g.pow(x, g.const(2.0, F))
+        p3 = g.pow(g.relu(x), g.const(1.5, F))
+        s, c = g.sin(g.mul(x, g.const(40.0, F))), g.cos(x)
+        n = g.neg(x)
+        r = g.range_(0, 17, 1)
+        le = g.less_equal(g.unsqueeze(r, [0]), g.unsqueeze(r, [1]))
+        return [p, p3, s, c, n, le]
+    parity(*build(g_), atol=2e-6, rtol=2e-6)
+
+
+def test_linalg_reduce_max():
+    mlir = """
+module {
+  func.func @forward(%arg0: tensor<4x9xf32>) -> tensor<4xf32> {
+    %cst = arith.constant 0xFF800000 : f32
+    %0 = tensor.empty() : tensor<4xf32>
+    %1 = linalg.fill ins(%cst : f32) outs(%0 : tensor<4xf32>) -> tensor<4xf32>
+    %reduced = linalg.reduce ins(%arg0 : tensor<4x9xf32>) outs(%1 : tensor<4xf32>) dimensions = [1]
+      (%in: f32, %init: f32) {
+        %2 = arith.maximumf %in, %init : f32
+        linalg.yield %2 : f32
+      }
+    return %reduced : tensor<4xf32>
+  }
+}
+"""
+    x = np.random.default_rng(3).standard_normal((4, 9)).astype(np.float32)
+    parity(mlir, [x])

@@ -1,0 +1,231 @@
+"""Host-side logic that runs without a GPU: MLIR parsing, planning, the C ABI
+surface, the synthetic graphs, the runner file contract and data parallelism."""
+import ctypes
+import os
+import re
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+from gawee_b200 import synth
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF_TESTS = "/root/reference/middle/mlir/test"  # read only when present (CPU container)
+
+
+# ---- parser -------------------------------------------------------------------------------
+
+def test_parser_attribute_forms_and_payloads(oracle_mod):
+    # properties <{...}> and attribute dicts {...}; hex and nested dense payloads; multi-results
+    mlir = """
+#map = affine_map<(d0, d1) -> (d0, d1)>
+#map1 = affine_map<(d0, d1) -> (0, d1)>
+module attributes {test.attr = 1 : i64} {
+  // comment line
+  func.func private @other(%a: tensor<2xf32>) -> tensor<2xf32> { return %a : tensor<2xf32> }
+  func.func @forward(%arg0: tensor<2x3xf32>, %arg1: tensor<1x3xf32>) -> (tensor<2x3xf32>, tensor<2x3xf32>, tensor<3xi64>) attributes {gawee.onnx_source = "x.onnx"} {
+    %cst = arith.constant dense<"0x010000000000000002000000000000000300000000000000"> : tensor<3xi64>
+    %cst_0 = arith.constant dense<[[1.000000e+00, -2.5, 0x7F800000]]> : tensor<1x3xf32>
+    %0 = "gawee.add"(%arg0, %arg1) {} : (tensor<2x3xf32>, tensor<1x3xf32>) -> tensor<2x3xf32>
+    %1:2 = "gawee.split"(%0) <{axis = 0 : i64, splitSizes = array<i64: 1, 1>}> : (tensor<2x3xf32>) -> (tensor<1x3xf32>, tensor<1x3xf32>)
+    %2 = tensor.empty() : tensor<2x3xf32>
+    %3 = linalg.generic {indexing_maps = [#map, #map1, #map], iterator_types = [#linalg.iterator_type<parallel>, #linalg.iterator_type<parallel>]} ins(%0, %cst_0 : tensor<2x3xf32>, tensor<1x3xf32>) outs(%2 : tensor<2x3xf32>) {
+    ^bb0(%in: f32, %in_1: f32, %out: f32):
+      %c2 = arith.constant 2.000000e+00 : f32
+      %4 = arith.mulf %in, %c2 fastmath<contract> : f32
+      %5 = arith.minimumf %4, %in_1 : f32
+      linalg.yield %5 : f32
+    } -> tensor<2x3xf32>
+    %6 = "gawee.cat"(%1#1, %1#0) {axis = 0 : i64} : (tensor<1x3xf32>, tensor<1x3xf32>) -> tensor<2x3xf32>
+    return %3, %6, %cst : tensor<2x3xf32>, tensor<2x3xf32>, tensor<3xi64>
+  }
+}
+"""
+    a = np.arange(6, dtype=np.float32).reshape(2, 3)
+    b = np.array([[1, -1, 0.5]], np.float32)
+    o3, o6, c = oracle_mod.run(mlir, [a, b])
+    s = a + b
+    assert np.array_equal(o3, np.minimum(s * 2, np.array([[1, -2.5, np.inf]], np.float32)))
+    assert np.array_equal(o6, np.concatenate([s[1:], s[:1]]))
+    assert np.array_equal(c, np.array([1, 2, 3], np.int64))
+
+
+@pytest.mark.parametrize("text,msg", [
+    ("module { func.func @forward(%a: tensor<?x3xf32>) -> tensor<?x3xf32> { return %a : tensor<?x3xf32> } }",
+     "dynamic"),
+    ("module { func.func @forward(%a: tensor<3xf32>) -> tensor<3xf32> { return %b : tensor<3xf32> } }",
+     "undefined"),
+    ("module { func.func @main(%a: tensor<3xf32>) -> tensor<3xf32> { return %a : tensor<3xf32> } }",
+     "not found"),
+])
+def test_parser_errors(oracle_mod, text, msg):
+    with pytest.raises(oracle_mod.OracleError, match=msg):
+        oracle_mod.Oracle(text)
+
+
+@pytest.mark.skipif(not os.path.isdir(REF_TESTS), reason="reference test inputs are only in the CPU container")
+def test_parser_reads_reference_test_inputs(oracle_mod):
+    # the reference's own hand-written inputs (no RUN lines there); matmul_test has two functions
+    text = open(os.path.join(REF_TESTS, "matmul_test.mlir")).read()
+    for entry, shapes in [("test_matmul_2d", [(2, 4), (4, 3)]), ("test_matmul_batched", [(1, 2, 3, 4), (1, 2, 4, 5)])]:
+        o = oracle_mod.Oracle(text, entry)
+        assert [s for _, s in o.arg_specs()] == shapes
+    text = open(os.path.join(REF_TESTS, "simple_test.mlir")).read()
+    o = oracle_mod.Oracle(text, "test_add")
+    a = np.ones((2, 3), np.float32)
+    assert np.array_equal(o.run([a, a])[0], a + a)
+
+
+# ---- planner (no device) -------------------------------------------------------------------
+
+def _plan(mlir):
+    from gawee_b200 import runtime
+    return runtime.plan_text(mlir)
+
+
+@pytest.mark.parametrize("name", list(synth.CONFIGS))
+def test_plan_all_configs(name):
+    g = synth.CONFIGS[name]()
+    s = _plan(g.mlir)
+    head = s.splitlines()[0]
+    kv = dict(x.split("=") for x in head.split())
+    assert int(kv["main"]) > 0
+    if name.startswith("resnet"):
+        # every conv's bias/relu/residual is fused into its epilogue
+        assert s.count("conv+add+relu") == 8 and s.count("conv+relu") == 9
+        assert "relu\n" not in s.replace("conv+relu", "").replace("conv+add+relu", "")
+    else:
+        # attention scores: matmul with the scale and mask fused; embeddings gathered
+        assert "matmul+div+add" in s and "gather" in s
+    if name.startswith("llama") or name.startswith("decoder"):
+        assert int(kv["prologue"]) >= 6  # RoPE tables and causal mask computed once
+
+
+def test_plan_memory_reuse():
+    g = synth.resnet18(256)
+    s = _plan(g.mlir)
+    kv = dict(x.split("=") for x in s.splitlines()[0].split())
+    # largest activation: 256x64x112x112 fp32 = 822 MB; liveness keeps the arena to a few of them
+    assert int(kv["arena_bytes"]) < 4 * 256 * 64 * 112 * 112 * 4
+
+
+def test_plan_rejects_unsupported():
+    from gawee_b200 import runtime
+    bad = """module { func.func @forward(%a: tensor<2x3xf32>) -> tensor<2x3xf32> {
+      %0 = "gawee.mystery"(%a) : (tensor<2x3xf32>) -> tensor<2x3xf32>
+      return %0 : tensor<2x3xf32> } }"""
+    with pytest.raises(runtime.GaweeError, match="unsupported"):
+        runtime.plan_text(bad)
+
+
+# ---- C ABI -----------------------------------------------------------------------------------
+
+def test_library_exports_every_declared_symbol():
+    from gawee_b200 import runtime
+    lib = runtime.load_library()
+    header = open(os.path.join(ROOT, "include", "gawee_cuda.h")).read()
+    names = set(re.findall(r"^\s*(?:gawee_status|int|void)\s+(gawee_\w+)\s*\(", header, re.M))
+    assert len(names) >= 20
+    for n in names:
+        assert hasattr(lib, n), n
+
+
+def test_create_without_gpu_fails_cleanly():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    from gawee_b200 import runtime
+    with pytest.raises(runtime.GaweeError):
+        runtime.Model(synth.resnet18(1, image=32).mlir)
+
+
+# ---- synthetic graphs -------------------------------------------------------------------------
+
+def test_synthetic_flops_match_cost_model():
+    # per-unit algorithmic FLOPs of the benchmark configurations
+    assert synth.resnet18(1).flop == 3_628_146_688
+    assert synth.bert_tiny().flop == 117_440_512
+    assert synth.llama15m().flop == 8_229_224_448
+    d = synth.smollm135m()
+    assert abs(d.flop - 9.973e12) / 9.973e12 < 1e-3
+    assert d.out_shapes == [(64, 512, 49152)]
+
+
+def test_emitter_argument_order():
+    g = synth.bert_tiny()
+    kinds = [a.kind for a in g.args]
+    # graph inputs first, then float initializers (ONNXMLIREmitter.cpp:2932-2975)
+    assert kinds[:3] == ["input"] * 3 and set(kinds[3:]) == {"weight"}
+    assert all(a.dtype == "f32" for a in g.args[3:])
+
+
+def test_runner_file_contract(tmp_path, oracle_mod):
+    """oracle CLI: argN.npy in, outputN.npy out, headers byte-compatible with np.load."""
+    g = synth.bert_tiny(seq=16, vocab=64, max_pos=32)
+    args = g.make_args()
+    (tmp_path / "in").mkdir()
+    for i, a in enumerate(args):
+        np.save(tmp_path / "in" / f"arg{i}.npy", a)
+    mlir = tmp_path / "m.mlir"
+    mlir.write_text(g.mlir)
+    r = subprocess.run([oracle_mod.CLI_PATH, str(mlir), str(tmp_path / "in"), str(tmp_path / "out")],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    out = np.load(tmp_path / "out" / "output0.npy")
+    assert np.array_equal(out, oracle_mod.run(g.mlir, args)[0])
+    with open(tmp_path / "out" / "output0.npy", "rb") as f:
+        head = f.read(128)
+    hl = int.from_bytes(head[8:10], "little")
+    assert (10 + hl) % 16 == 0 and b"'descr': '<f4'" in head
+
+
+# ---- data parallelism (gloo ranks on CPU) ---------------------------------------------------------
+
+def _dp_worker(rank, world, port, result_path):
+    import torch.distributed as dist
+    sys.path.insert(0, ROOT)
+    import oracle
+    from gawee_b200 import dp, synth as sy
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        full = sy.resnet18(4, image=32, widths=(8, 8, 16, 16), classes=10)
+        args = full.make_args()
+        local_batch = dp.shard_range(4, world, rank)
+        shard = sy.resnet18(local_batch[1] - local_batch[0], image=32, widths=(8, 8, 16, 16), classes=10)
+        local_args = dp.shard_args(args, [True] + [False] * (len(args) - 1), world, rank)
+        out = oracle.run(shard.mlir, local_args)[0]
+        uid = dp.share_nccl_id(bytes(range(128)) if rank == 0 else bytes(128), rank)
+        assert uid == bytes(range(128))
+        gathered = dp.gather_rows_host(out, rank, world)
+        if rank == 0:
+            want = oracle.run(full.mlir, args)[0]
+            np.save(result_path, np.array([float(np.max(np.abs(gathered - want)))]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_dp_sharded_matches_full_batch(tmp_path):
+    import multiprocessing as mp
+    import socket
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    res = str(tmp_path / "r.npy")
+    procs = [ctx.Process(target=_dp_worker, args=(r, 2, port, res)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    assert all(p.exitcode == 0 for p in procs)
+    # batch rows are independent: sharded outputs equal the full-batch output exactly
+    assert np.load(res)[0] == 0.0
+
+
+def test_shard_range():
+    from gawee_b200 import dp
+    assert [dp.shard_range(256, 8, r) for r in (0, 7)] == [(0, 32), (224, 256)]
+    assert [dp.shard_range(5, 2, r) for r in (0, 1)] == [(0, 3), (3, 5)]

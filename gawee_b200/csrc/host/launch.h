@@ -24,6 +24,7 @@ struct PackSpec {
 namespace launch {
 using Fn = std::function<void(Runtime&, void*)>;
 Fn remap(kern::RemapParams rp, const View& in, const View& out);
+Fn nchw_to_nhwc4(const View& in, const View& out, int64_t N, int C, int C4, int64_t HW, int64_t in_sn, int64_t in_sc);
 Fn reduce(const View& in, const View& out, const std::vector<bool>& red, bool mean, float count);
 Fn generic_reduce(const View& in, const View& out, const std::vector<bool>& red, const EProgram& body);
 Fn pool(kern::PoolParams pp, const View& in, const View& out);

@@ -778,6 +778,12 @@ class Planner {
       op.name = "to_nhwc";
       op.reads = {x};
       op.writes = {out};
+      if (x.dt == DType::F32 && x.st[3] == 1 && x.st[2] == W) {  // NCHW planes: pixel-vectorised kernel
+        op.launch = launch::nchw_to_nhwc4(x, out, N, (int)C, (int)C4, H * W, N > 1 ? x.st[0] : 0, x.st[1]);
+        add_op(std::move(op));
+        xin = out;
+        goto packed;
+      }
       kern::RemapParams rp{};
       rp.elem_bytes = 4;
       rp.rank = 4;
@@ -798,6 +804,7 @@ class Planner {
       add_op(std::move(op));
       xin = out;
     }
+  packed:
     PackSpec ps;
     ps.src = w;
     ps.batch = 1;

@@ -381,6 +381,13 @@ Fn remap(kern::RemapParams rp, const View& in, const View& out) {
   };
 }
 
+Fn nchw_to_nhwc4(const View& in, const View& out, int64_t N, int C, int C4, int64_t HW, int64_t in_sn, int64_t in_sc) {
+  return [=](Runtime& rt, void* s) {
+    kern::launch_nchw_to_nhwc4(reinterpret_cast<const float*>(rt.ptr(in)), reinterpret_cast<float*>(rt.ptr(out)), N, C,
+                               C4, HW, in_sn, in_sc, static_cast<cudaStream_t>(s));
+  };
+}
+
 static void split_dims(const View& in, const std::vector<bool>& red, kern::ReduceParams* rp,
                        kern::GenericReduceParams* gp, const View& out) {
   std::vector<int64_t> ks, kst, rs, rst;
@@ -891,6 +898,28 @@ gawee_status gawee_ciface_forward(gawee_ctx* ctx, void* result_desc, void* const
       acc *= rtype.shape[k];
     }
   });
+}
+
+gawee_status gawee_embedded_forward(const char* mlir_text, int device, void* result_desc, void* const* arg_descs,
+                                    int nargs) {
+  struct Cache {
+    std::mutex mu;
+    std::vector<std::pair<std::pair<const char*, int>, gawee_ctx*>> ctxs;
+  };
+  static Cache* cache = new Cache();  // contexts live until process exit
+  if (!mlir_text) return GAWEE_ERR_INVALID;
+  gawee_ctx* ctx = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(cache->mu);
+    for (auto& e : cache->ctxs)
+      if (e.first.first == mlir_text && e.first.second == device) ctx = e.second;
+    if (!ctx) {
+      gawee_status st = gawee_create(mlir_text, "forward", device, &ctx);
+      if (st) return st;
+      cache->ctxs.push_back({{mlir_text, device}, ctx});
+    }
+  }
+  return gawee_ciface_forward(ctx, result_desc, arg_descs, nargs);
 }
 
 gawee_status gawee_dp_unique_id(void* id) {

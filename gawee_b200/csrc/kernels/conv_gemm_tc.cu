@@ -8,11 +8,11 @@
 // The tensor core's fp32 accumulation truncates (Fasi et al., "Numerical
 // behavior of NVIDIA tensor cores", 2021), so over thousands of k-steps its
 // error grows linearly with K.  Each 32-wide k-block is therefore accumulated
-// alone in one of two tensor-memory buffers, and four accumulator warps add
-// the block sums into fp32 registers with IEEE round-to-nearest while the next
-// block is multiplied into the other buffer.
+// alone in one of four tensor-memory buffers, and the accumulator warps add
+// the block sums into fp32 registers with IEEE round-to-nearest while later
+// blocks are multiplied into the other buffers.
 //
-// Warp roles (320 threads):
+// Warp roles (448 threads), persistent over output tiles (one CTA per SM):
 //   warps 0-3  gather the A tile (im2col rows of the NHWC input, zero padding,
 //              K tails) with 16-byte loads, split each value into an exact
 //              TF32 high part and an fp32 remainder in registers, and store
@@ -20,12 +20,15 @@
 //   warp 4     issues the TMA loads of the pre-split B planes; owns the TMEM
 //              allocation
 //   warp 5     one elected thread issues tcgen05.mma and tcgen05.commit
-//   warps 6-9  accumulate block sums from TMEM and run the epilogue
+//   warps 6-13 accumulate block sums from TMEM (two warps per TMEM lane
+//              quarter, each owning half the tile's columns) and run the
+//              epilogue of tile t while the MMAs of tile t+1 proceed
 // Stage hand-off uses mbarriers; every wait is bounded in time and on expiry
 // records ST_BARRIER_TIMEOUT in the status word and lets the CTA finish.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <mutex>
 
@@ -39,7 +42,7 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 32;               // fp32 elements per k-block (one 128-byte swizzle row)
-constexpr int kThreadsTC = 320;
+constexpr int kThreadsTC = 448;  // 4 A-producer, 1 TMA, 1 MMA, 8 accumulator warps
 constexpr unsigned long long kWaitNs = 4000000000ull;  // 4 s per barrier wait
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -170,9 +173,10 @@ struct Smem {
   static constexpr int kBTile = BN * kBK * 4;
   static constexpr int kStage = 2 * kATile + 2 * kBTile;
   static constexpr int kBarOff = STAGES * kStage;
-  static constexpr int kNumBars = 3 * STAGES + 5;  // full_a, full_b, empty per stage; tfull[2], tempty[2], done
+  static constexpr int kNumBufs = 4;               // k-block accumulators in tensor memory
+  static constexpr int kNumBars = 3 * STAGES + 2 * kNumBufs + 1;  // full_a/full_b/empty; tfull/tempty; done
   static constexpr int kBytes = kBarOff + 8 * kNumBars + 16 + 1024;  // + alignment slack
-  static constexpr int kTmemCols = 2 * BN;         // two k-block accumulators
+  static constexpr int kTmemCols = kNumBufs * BN;
 };
 
 }  // namespace
@@ -182,29 +186,36 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     conv_gemm_tc_kernel(const __grid_constant__ ConvGemmParams p, const __grid_constant__ CUtensorMap tm_hi,
                         const __grid_constant__ CUtensorMap tm_lo) {
   using L = Smem<BN, STAGES>;
+  constexpr int NB = L::kNumBufs;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* full_a = bars;
   uint64_t* full_b = bars + STAGES;
   uint64_t* empty = bars + 2 * STAGES;
-  uint64_t* tfull = bars + 3 * STAGES;      // [2] block sum ready in TMEM buffer b
-  uint64_t* tempty = bars + 3 * STAGES + 2; // [2] TMEM buffer b drained by the accumulator warps
-  uint64_t* done = bars + 3 * STAGES + 4;   // every MMA issued by this CTA completed
+  uint64_t* tfull = bars + 3 * STAGES;        // [NB] k-block sum ready in TMEM buffer
+  uint64_t* tempty = bars + 3 * STAGES + NB;  // [NB] TMEM buffer drained by the accumulator warps
+  uint64_t* done = bars + 3 * STAGES + 2 * NB;  // every MMA issued by this CTA completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
-  const int64_t m0 = (int64_t)blockIdx.x * kBM;
-  const int n0 = blockIdx.y * BN;
-  const int z = blockIdx.z;
   const int num_kb = (int)((p.K + kBK - 1) / kBK);
+  const int64_t m_tiles = (p.M + kBM - 1) / kBM;
+  const int64_t n_tiles = (p.N + BN - 1) / BN;
+  const int64_t num_tiles = m_tiles * n_tiles * p.nb;
 
-  // batch offsets
-  int64_t a_off = 0, c_off = 0;
-  int b_plane = 0;
-  {
+  // Tile t -> (z, n tile, m tile), m fastest so CTAs running together share B.
+  auto tile_coords = [&](int64_t t, int64_t& m0, int& n0, int& z) {
+    m0 = (t % m_tiles) * kBM;
+    n0 = (int)(((t / m_tiles) % n_tiles) * BN);
+    z = (int)(t / (m_tiles * n_tiles));
+  };
+  auto batch_offsets = [&](int z, int64_t& a_off, int64_t& c_off, int& b_plane) {
+    a_off = 0;
+    c_off = 0;
+    b_plane = 0;
     int64_t rem = z;
     for (int d = p.batch_rank - 1; d >= 0; --d) {
       const int64_t c = rem % p.batch_shape[d];
@@ -213,7 +224,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       c_off += c * p.c_bst[d];
       b_plane += (int)(c * p.b_bst[d]);
     }
-  }
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -221,9 +232,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       mbar_init(smem_u32(&full_b[s]), 1);
       mbar_init(smem_u32(&empty[s]), 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NB; ++b) {
       mbar_init(smem_u32(&tfull[b]), 1);
-      mbar_init(smem_u32(&tempty[b]), 4);
+      mbar_init(smem_u32(&tempty[b]), 8);
     }
     mbar_init(smem_u32(done), 1);
     *abort_flag = 0;
@@ -244,93 +255,118 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     // ------------------------------------------------------------------ A producer
     const int chunk = lane & 7;
     const int rsub = lane >> 3;
-    int64_t rbase[8];
-    int ih0[8], iw0[8];
     const int64_t PQ = p.P * p.Q;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int64_t m = m0 + warp * 32 + i * 4 + rsub;
-      if (m < p.M) {
-        const int64_t img = m / PQ, pq = m % PQ;
-        const int64_t pp = pq / p.Q, qq = pq % p.Q;
-        rbase[i] = a_off + img * p.x_sn;
-        ih0[i] = (int)(pp * p.sh - p.ph);
-        iw0[i] = (int)(qq * p.sw - p.pw);
-      } else {
-        rbase[i] = -1;
-        ih0[i] = 0;
-        iw0[i] = 0;
-      }
-    }
-    auto load_kb = [&](int kb, float4 (&v)[8]) {
-      const int64_t k0 = (int64_t)kb * kBK + chunk * 4;
-      int r = 0, s = 0;
-      int64_t c = 0;
-      const bool kin = k0 < p.K;
-      if (kin) {
-        const int64_t rs = k0 / p.C;
-        c = k0 - rs * p.C;
-        r = (int)(rs / p.S);
-        s = (int)(rs - (int64_t)r * p.S);
-      }
+    int64_t g = 0;  // k-blocks produced so far (all tiles): stage = g % STAGES
+    bool alive = true;
+    for (int64_t t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
+      int64_t m0, a_off, c_off;
+      int n0, z, b_plane;
+      tile_coords(t, m0, n0, z);
+      batch_offsets(z, a_off, c_off, b_plane);
+      int64_t rbase[8];
+      int ih0[8], iw0[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const int ih = ih0[i] + r * p.dh, iw = iw0[i] + s * p.dw;
-        if (kin && rbase[i] >= 0 && ih >= 0 && ih < p.H && iw >= 0 && iw < p.W) {
-          v[i] = __ldg(reinterpret_cast<const float4*>(p.x + rbase[i] + ih * p.x_sh + iw * p.x_sw + c));
+        const int64_t m = m0 + warp * 32 + i * 4 + rsub;
+        if (m < p.M) {
+          const int64_t img = m / PQ, pq = m % PQ;
+          const int64_t pp = pq / p.Q, qq = pq % p.Q;
+          rbase[i] = a_off + img * p.x_sn;
+          ih0[i] = (int)(pp * p.sh - p.ph);
+          iw0[i] = (int)(qq * p.sw - p.pw);
         } else {
-          v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+          rbase[i] = -1;
+          ih0[i] = 0;
+          iw0[i] = 0;
         }
       }
-    };
-    float4 cur[8], nxt[8];
-    if (num_kb > 0) load_kb(0, cur);
-    for (int kb = 0; kb < num_kb; ++kb) {
-      const int st = kb % STAGES;
-      const uint32_t ph = (kb / STAGES) & 1;
-      if (kb + 1 < num_kb) load_kb(kb + 1, nxt);
-      if (!mbar_wait(smem_u32(&empty[st]), ph ^ 1, abort_flag, p.status)) break;
-      uint8_t* a_hi = smem + st * L::kStage;
-      uint8_t* a_lo = a_hi + L::kATile;
+      auto load_kb = [&](int kb, float4 (&v)[8]) {
+        const int64_t k0 = (int64_t)kb * kBK + chunk * 4;
+        int r = 0, s = 0;
+        int64_t c = 0;
+        const bool kin = k0 < p.K;
+        if (kin) {
+          const int64_t rs = k0 / p.C;
+          c = k0 - rs * p.C;
+          r = (int)(rs / p.S);
+          s = (int)(rs - (int64_t)r * p.S);
+        }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int row = warp * 32 + i * 4 + rsub;
-        const int off = row * 128 + ((chunk ^ (row & 7)) << 4);
-        const float4 x = cur[i];
-        const float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
-        const float4 l = make_float4(__fsub_rn(x.x, h.x), __fsub_rn(x.y, h.y), __fsub_rn(x.z, h.z), __fsub_rn(x.w, h.w));
-        *reinterpret_cast<float4*>(a_hi + off) = h;
-        *reinterpret_cast<float4*>(a_lo + off) = l;
+        for (int i = 0; i < 8; ++i) {
+          const int ih = ih0[i] + r * p.dh, iw = iw0[i] + s * p.dw;
+          if (kin && rbase[i] >= 0 && ih >= 0 && ih < p.H && iw >= 0 && iw < p.W) {
+            v[i] = __ldg(reinterpret_cast<const float4*>(p.x + rbase[i] + ih * p.x_sh + iw * p.x_sw + c));
+          } else {
+            v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+      };
+      // Two register buffers alternate between "being stored" and "loads in
+      // flight", so the next k-block's global loads overlap this block's wait,
+      // split and shared-memory stores.
+      auto store_kb = [&](const float4 (&v)[8]) -> bool {
+        const int st = (int)(g % STAGES);
+        const uint32_t ph = (uint32_t)((g / STAGES) & 1);
+        if (!mbar_wait(smem_u32(&empty[st]), ph ^ 1, abort_flag, p.status)) return false;
+        uint8_t* a_hi = smem + st * L::kStage;
+        uint8_t* a_lo = a_hi + L::kATile;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int row = warp * 32 + i * 4 + rsub;
+          const int off = row * 128 + ((chunk ^ (row & 7)) << 4);
+          const float4 x = v[i];
+          const float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
+          const float4 l =
+              make_float4(__fsub_rn(x.x, h.x), __fsub_rn(x.y, h.y), __fsub_rn(x.z, h.z), __fsub_rn(x.w, h.w));
+          *reinterpret_cast<float4*>(a_hi + off) = h;
+          *reinterpret_cast<float4*>(a_lo + off) = l;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&full_a[st]));
+        ++g;
+        return true;
+      };
+      float4 va[8], vb[8];
+      load_kb(0, va);
+      for (int kb = 0; kb < num_kb; kb += 2) {
+        if (kb + 1 < num_kb) load_kb(kb + 1, vb);
+        if (!store_kb(va)) { alive = false; break; }
+        if (kb + 1 >= num_kb) break;
+        if (kb + 2 < num_kb) load_kb(kb + 2, va);
+        if (!store_kb(vb)) { alive = false; break; }
       }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&full_a[st]));
-#pragma unroll
-      for (int i = 0; i < 8; ++i) cur[i] = nxt[i];
     }
   } else if (warp == 4) {
     // ------------------------------------------------------------------ B producer (TMA)
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_hi)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_lo)) : "memory");
-      int issued = 0;
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int st = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (!mbar_wait(smem_u32(&empty[st]), ph ^ 1, abort_flag, p.status)) break;
-        uint8_t* b_hi = smem + st * L::kStage + 2 * L::kATile;
-        uint8_t* b_lo = b_hi + L::kBTile;
-        const uint32_t bar = smem_u32(&full_b[st]);
-        mbar_arrive_tx(bar, 2 * L::kBTile);
-        tma_load_3d(smem_u32(b_hi), &tm_hi, bar, kb * kBK, n0, b_plane);
-        tma_load_3d(smem_u32(b_lo), &tm_lo, bar, kb * kBK, n0, b_plane);
-        issued = kb + 1;
+      int64_t g = 0;
+      bool alive = true;
+      for (int64_t t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
+        int64_t m0, a_off, c_off;
+        int n0, z, b_plane;
+        tile_coords(t, m0, n0, z);
+        batch_offsets(z, a_off, c_off, b_plane);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          const int st = (int)(g % STAGES);
+          const uint32_t ph = (uint32_t)((g / STAGES) & 1);
+          if (!mbar_wait(smem_u32(&empty[st]), ph ^ 1, abort_flag, p.status)) { alive = false; break; }
+          uint8_t* b_hi = smem + st * L::kStage + 2 * L::kATile;
+          uint8_t* b_lo = b_hi + L::kBTile;
+          const uint32_t bar = smem_u32(&full_b[st]);
+          mbar_arrive_tx(bar, 2 * L::kBTile);
+          tma_load_3d(smem_u32(b_hi), &tm_hi, bar, kb * kBK, n0, b_plane);
+          tma_load_3d(smem_u32(b_lo), &tm_lo, bar, kb * kBK, n0, b_plane);
+          ++g;
+        }
       }
       if (*abort_flag) {
         // let copies already in flight land before the CTA retires
-        for (int kb = issued - STAGES < 0 ? 0 : issued - STAGES; kb < issued; ++kb) {
+        for (int64_t k = g - STAGES < 0 ? 0 : g - STAGES; k < g; ++k) {
           volatile int never = 0;
-          mbar_wait(smem_u32(&full_b[kb % STAGES]), (kb / STAGES) & 1, &never, nullptr);
+          mbar_wait(smem_u32(&full_b[k % STAGES]), (uint32_t)((k / STAGES) & 1), &never, nullptr);
         }
       }
     }
@@ -338,72 +374,93 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_tf32<BN>();
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int st = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        const int buf = kb & 1;
-        const uint32_t use = (uint32_t)(kb >> 1) & 1;
-        if (!mbar_wait(smem_u32(&full_a[st]), ph, abort_flag, p.status)) break;
-        if (!mbar_wait(smem_u32(&full_b[st]), ph, abort_flag, p.status)) break;
-        if (!mbar_wait(smem_u32(&tempty[buf]), use ^ 1, abort_flag, p.status)) break;
-        tc_fence_after();
-        const uint32_t a_hi = smem_u32(smem + st * L::kStage);
-        const uint32_t a_lo = a_hi + L::kATile;
-        const uint32_t b_hi = a_hi + 2 * L::kATile;
-        const uint32_t b_lo = b_hi + L::kBTile;
-        const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BN);
+      int64_t g = 0;
+      bool alive = true;
+      for (int64_t t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
+        for (int kb = 0; kb < num_kb; ++kb) {
+          const int st = (int)(g % STAGES);
+          const uint32_t ph = (uint32_t)((g / STAGES) & 1);
+          const int buf = (int)(g % NB);
+          const uint32_t use = (uint32_t)((g / NB) & 1);
+          if (!mbar_wait(smem_u32(&full_a[st]), ph, abort_flag, p.status) ||
+              !mbar_wait(smem_u32(&full_b[st]), ph, abort_flag, p.status) ||
+              !mbar_wait(smem_u32(&tempty[buf]), use ^ 1, abort_flag, p.status)) {
+            alive = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_hi = smem_u32(smem + st * L::kStage);
+          const uint32_t a_lo = a_hi + L::kATile;
+          const uint32_t b_hi = a_hi + 2 * L::kATile;
+          const uint32_t b_lo = b_hi + L::kBTile;
+          const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BN);
 #pragma unroll
-        for (int kk = 0; kk < kBK / 8; ++kk) {
-          const uint32_t koff = kk * 32;  // 8 tf32 = 32 bytes along the swizzled row
-          const uint64_t dah = umma_desc_sw128(a_hi + koff), dal = umma_desc_sw128(a_lo + koff);
-          const uint64_t dbh = umma_desc_sw128(b_hi + koff), dbl = umma_desc_sw128(b_lo + koff);
-          umma_tf32(tmem_d, dal, dbh, idesc, kk != 0);
-          umma_tf32(tmem_d, dah, dbl, idesc, 1);
-          umma_tf32(tmem_d, dah, dbh, idesc, 1);
+          for (int kk = 0; kk < kBK / 8; ++kk) {
+            const uint32_t koff = kk * 32;  // 8 tf32 = 32 bytes along the swizzled row
+            const uint64_t dah = umma_desc_sw128(a_hi + koff), dal = umma_desc_sw128(a_lo + koff);
+            const uint64_t dbh = umma_desc_sw128(b_hi + koff), dbl = umma_desc_sw128(b_lo + koff);
+            umma_tf32(tmem_d, dal, dbh, idesc, kk != 0);
+            umma_tf32(tmem_d, dah, dbl, idesc, 1);
+            umma_tf32(tmem_d, dah, dbh, idesc, 1);
+          }
+          umma_commit(smem_u32(&empty[st]));
+          umma_commit(smem_u32(&tfull[buf]));
+          ++g;
         }
-        umma_commit(smem_u32(&empty[st]));
-        umma_commit(smem_u32(&tfull[buf]));
       }
       umma_commit(smem_u32(done));
     }
   } else {
     // ------------------------------------------------------------------ accumulate + epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // warps 6..13: lane quarter (warp % 4) is fixed by the hardware; two
+    // warps share a quarter and split the tile's columns in halves
+    constexpr int HB = BN / 2;
+    const int q = warp & 3;
+    const int half = (warp - 6) / 4;
+    const int cbase = half * HB;
     const int row = q * 32 + lane;
     const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
-    float acc[BN];
-#pragma unroll
-    for (int j = 0; j < BN; ++j) acc[j] = 0.0f;
+    int64_t g = 0;
     bool ok = true;
-    for (int kb = 0; kb < num_kb; ++kb) {
-      const int buf = kb & 1;
-      const uint32_t use = (uint32_t)(kb >> 1) & 1;
-      if (!mbar_wait(smem_u32(&tfull[buf]), use, abort_flag, p.status)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
+    for (int64_t t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      int64_t m0, a_off, c_off;
+      int n0, z, b_plane;
+      tile_coords(t, m0, n0, z);
+      batch_offsets(z, a_off, c_off, b_plane);
+      float acc[HB];
 #pragma unroll
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(lane_base + (uint32_t)(buf * BN + c0), r);
+      for (int j = 0; j < HB; ++j) acc[j] = 0.0f;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int buf = (int)(g % NB);
+        const uint32_t use = (uint32_t)((g / NB) & 1);
+        if (!mbar_wait(smem_u32(&tfull[buf]), use, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) acc[c0 + j] = __fadd_rn(acc[c0 + j], __uint_as_float(r[j]));
+        for (int c0 = 0; c0 < HB; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld32(lane_base + (uint32_t)(buf * BN + cbase + c0), r);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[c0 + j] = __fadd_rn(acc[c0 + j], __uint_as_float(r[j]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&tempty[buf]));
+        ++g;
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&tempty[buf]));
-    }
-    ok = ok && !*abort_flag;
-    const int64_t m = m0 + row;
-    if (ok && m < p.M) {
+      ok = ok && !*abort_flag;
+      const int64_t m = m0 + row;
+      if (!ok || m >= p.M) continue;
       float* crow = p.out + c_off + m * p.ldc;
+      const int nb0 = n0 + cbase;  // first column of this thread's half tile
       if (EPI == EPI_PROGRAM) {
         Reg regs[kMaxRegs];
         int err = 0;
 #pragma unroll
-        for (int j = 0; j < BN; ++j) {
-          const int64_t n = n0 + j;
+        for (int j = 0; j < HB; ++j) {
+          const int64_t n = nb0 + j;
           if (n < p.N) {
             regs[0].f = p.bias ? __fadd_rn(acc[j], p.bias[n]) : acc[j];
             for (int a = 0; a < p.n_aux; ++a) {
@@ -420,24 +477,29 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         }
         if (err && p.status) atomicCAS(p.status, 0, err);
       } else {
+        const bool vec = p.ldc_n == 1 && nb0 + HB <= p.N && ((reinterpret_cast<uintptr_t>(crow + nb0) & 15) == 0);
+        // 16 columns at a time keeps the bias / residual temporaries small
 #pragma unroll
-        for (int j = 0; j < BN; ++j) {
-          const int64_t n = n0 + j;
-          float x = acc[j];
-          if (EPI >= EPI_BIAS) x = __fadd_rn(x, n < p.N ? p.bias[n] : 0.f);
-          if (EPI == EPI_BIAS_ADD_RELU) x = __fadd_rn(x, n < p.N ? p.res[c_off + m * p.ldc + n * p.ldc_n] : 0.f);
-          if (EPI == EPI_BIAS_RELU || EPI == EPI_BIAS_ADD_RELU) x = maximumf_(x, 0.0f);
-          acc[j] = x;
-        }
-        const bool vec = p.ldc_n == 1 && n0 + BN <= p.N && ((reinterpret_cast<uintptr_t>(crow + n0) & 15) == 0);
-        if (vec) {
+        for (int c0 = 0; c0 < HB; c0 += 16) {
+          float o[16];
 #pragma unroll
-          for (int j = 0; j < BN; j += 4)
-            *reinterpret_cast<float4*>(crow + n0 + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
-        } else {
+          for (int j = 0; j < 16; ++j) {
+            const int64_t n = nb0 + c0 + j;
+            float x = acc[c0 + j];
+            if (EPI >= EPI_BIAS) x = __fadd_rn(x, n < p.N ? __ldg(p.bias + n) : 0.f);
+            if (EPI == EPI_BIAS_ADD_RELU) x = __fadd_rn(x, n < p.N ? __ldg(p.res + c_off + m * p.ldc + n * p.ldc_n) : 0.f);
+            if (EPI == EPI_BIAS_RELU || EPI == EPI_BIAS_ADD_RELU) x = maximumf_(x, 0.0f);
+            o[j] = x;
+          }
+          if (vec) {
 #pragma unroll
-          for (int j = 0; j < BN; ++j)
-            if (n0 + j < p.N) crow[(int64_t)(n0 + j) * p.ldc_n] = acc[j];
+            for (int j = 0; j < 16; j += 4)
+              *reinterpret_cast<float4*>(crow + nb0 + c0 + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (nb0 + c0 + j < p.N) crow[(int64_t)(nb0 + c0 + j) * p.ldc_n] = o[j];
+          }
         }
       }
     }
@@ -483,7 +545,15 @@ bool launch_t(const ConvGemmParams& p, const void* tmh, const void* tml, cudaStr
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return false;
     attr = true;
   }
-  dim3 grid((unsigned)((p.M + kBM - 1) / kBM), (unsigned)((p.N + BN - 1) / BN), (unsigned)p.nb);
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  const int64_t tiles = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN) * p.nb;
+  dim3 grid((unsigned)std::min<int64_t>(tiles, sms), 1, 1);
   kern<<<grid, kThreadsTC, smem, s>>>(p, *static_cast<const CUtensorMap*>(tmh), *static_cast<const CUtensorMap*>(tml));
   return true;
 }
@@ -535,7 +605,7 @@ bool launch_conv_gemm_tc(const ConvGemmParams& p, const void* tmap_hi, const voi
     return false;
   for (int d = 0; d < p.batch_rank; ++d)
     if (p.a_bst[d] % 4 != 0) return false;
-  if (p.nb > 65535 || (p.N + block_n - 1) / block_n > 65535) return false;
+  if (p.nb > (1 << 30)) return false;
   if (block_n == 64) return launch_epi<64, 4>(p, tmap_hi, tmap_lo, s);
   if (block_n == 128) return launch_epi<128, 3>(p, tmap_hi, tmap_lo, s);
   return false;

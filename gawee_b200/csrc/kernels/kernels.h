@@ -147,6 +147,11 @@ struct RemapParams {
 };
 void launch_remap(const RemapParams& p, cudaStream_t s);
 
+// NCHW (channel stride in_sc, image stride in_sn, pixels contiguous) to dense
+// NHWC with C4 >= C channels (multiple of 4), zero in the padding channels.
+void launch_nchw_to_nhwc4(const float* in, float* out, int64_t N, int C, int C4, int64_t HW, int64_t in_sn,
+                          int64_t in_sc, cudaStream_t s);
+
 // out[i] = start + i * delta
 struct RangeParams {
   void* out;

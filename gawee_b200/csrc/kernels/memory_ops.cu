@@ -332,31 +332,63 @@ void launch_gather_elements(const GatherElementsParams& p, cudaStream_t s) {
 // ---------------------------------------------------------------------------
 // Index remap (pad / tile / resize)
 // ---------------------------------------------------------------------------
+template <typename T>
 __global__ void __launch_bounds__(kThreads) remap_kernel(const __grid_constant__ RemapParams p) {
+  const T fill = *reinterpret_cast<const T*>(&p.fill_bits);
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < p.numel; i += (int64_t)gridDim.x * blockDim.x) {
     int64_t rem = i, src = 0, dst = 0;
     bool inside = true;
     for (int d = p.rank - 1; d >= 0; --d) {
-      int64_t o = rem % p.out_shape[d];
+      const int64_t o = rem % p.out_shape[d];
       rem /= p.out_shape[d];
       dst += o * p.out_st[d];
-      int64_t c = ((o / p.div[d]) % p.mod[d]) - p.sub[d];
+      const int64_t c = ((o / p.div[d]) % p.mod[d]) - p.sub[d];
       if (c < 0 || c >= p.in_shape[d]) inside = false;
       src += c * p.in_st[d];
     }
-    unsigned char* dp = static_cast<unsigned char*>(p.out) + dst * p.elem_bytes;
-    if (inside) {
-      const unsigned char* sp = static_cast<const unsigned char*>(p.in) + src * p.elem_bytes;
-      for (int b = 0; b < p.elem_bytes; ++b) dp[b] = sp[b];
-    } else {
-      for (int b = 0; b < p.elem_bytes; ++b) dp[b] = (unsigned char)(p.fill_bits >> (8 * b));
-    }
+    static_cast<T*>(p.out)[dst] = inside ? static_cast<const T*>(p.in)[src] : fill;
   }
 }
 
 void launch_remap(const RemapParams& p, cudaStream_t s) {
   if (p.numel <= 0) return;
-  remap_kernel<<<grid_for(p.numel), kThreads, 0, s>>>(p);
+  const unsigned g = grid_for(p.numel);
+  switch (p.elem_bytes) {
+    case 1: remap_kernel<uint8_t><<<g, kThreads, 0, s>>>(p); break;
+    case 2: remap_kernel<uint16_t><<<g, kThreads, 0, s>>>(p); break;
+    case 4: remap_kernel<uint32_t><<<g, kThreads, 0, s>>>(p); break;
+    default: remap_kernel<uint64_t><<<g, kThreads, 0, s>>>(p); break;
+  }
+}
+
+// NCHW -> NHWC with the channel dim padded (zeros) to C4, a multiple of 4:
+// each thread writes one pixel's 4 channels with a 16-byte store; the reads
+// of a warp stay within 4 channel planes at consecutive pixels.
+__global__ void __launch_bounds__(kThreads) nchw_to_nhwc4_kernel(const float* __restrict__ in, float* __restrict__ out,
+                                                                 int64_t N, int C, int C4, int64_t HW,
+                                                                 int64_t in_sn, int64_t in_sc) {
+  const int cg = C4 / 4;
+  const int64_t total = N * HW * cg;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int g = (int)(i % cg);
+    const int64_t pix = (i / cg) % HW;
+    const int64_t n = i / (cg * HW);
+    const float* src = in + n * in_sn + pix;
+    float v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int c = g * 4 + k;
+      v[k] = c < C ? __ldg(src + (int64_t)c * in_sc) : 0.0f;
+    }
+    reinterpret_cast<float4*>(out)[i] = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
+void launch_nchw_to_nhwc4(const float* in, float* out, int64_t N, int C, int C4, int64_t HW, int64_t in_sn,
+                          int64_t in_sc, cudaStream_t s) {
+  const int64_t total = N * HW * (C4 / 4);
+  if (total <= 0) return;
+  nchw_to_nhwc4_kernel<<<grid_for(total), kThreads, 0, s>>>(in, out, N, C, C4, HW, in_sn, in_sc);
 }
 
 __global__ void range_kernel(const __grid_constant__ RangeParams p) {
@@ -411,10 +443,54 @@ __global__ void __launch_bounds__(kThreads) pool_kernel(const __grid_constant__ 
   }
 }
 
+// Dense NHWC on both sides with C % 4 == 0: one thread per 4 channels of an
+// output pixel, 16-byte loads and stores, 32-bit spatial indices.
+__global__ void __launch_bounds__(kThreads) pool_nhwc4_kernel(const __grid_constant__ PoolParams p) {
+  const int cg = (int)(p.C / 4);
+  const int64_t total = p.N * p.OH * p.OW * cg;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int g = (int)(i % cg);
+    int64_t r = i / cg;
+    const int ow = (int)(r % p.OW);
+    r /= p.OW;
+    const int oh = (int)(r % p.OH);
+    const int64_t n = r / p.OH;
+    const float* base = p.in + n * p.in_st[0] + g * 4;
+    float4 acc = p.mode == 0 ? make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int kh = 0; kh < p.kh; ++kh) {
+      const int ih = oh * p.sh + kh * p.dh - p.ph;
+      for (int kw = 0; kw < p.kw; ++kw) {
+        const int iw = ow * p.sw + kw * p.dw - p.pw;
+        const bool in = ih >= 0 && ih < p.H && iw >= 0 && iw < p.W;
+        float4 v;
+        if (in) v = __ldg(reinterpret_cast<const float4*>(base + ih * p.in_st[2] + iw * p.in_st[3]));
+        else v = p.mode == 0 ? make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY) : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (p.mode == 0) {
+          acc.x = maximumf_(acc.x, v.x); acc.y = maximumf_(acc.y, v.y);
+          acc.z = maximumf_(acc.z, v.z); acc.w = maximumf_(acc.w, v.w);
+        } else {
+          acc.x = __fadd_rn(acc.x, v.x); acc.y = __fadd_rn(acc.y, v.y);
+          acc.z = __fadd_rn(acc.z, v.z); acc.w = __fadd_rn(acc.w, v.w);
+        }
+      }
+    }
+    if (p.mode == 1) {
+      acc.x = __fdiv_rn(acc.x, p.count); acc.y = __fdiv_rn(acc.y, p.count);
+      acc.z = __fdiv_rn(acc.z, p.count); acc.w = __fdiv_rn(acc.w, p.count);
+    }
+    *reinterpret_cast<float4*>(p.out + n * p.out_st[0] + (int64_t)oh * p.out_st[2] + (int64_t)ow * p.out_st[3] + g * 4) = acc;
+  }
+}
+
 void launch_pool(const PoolParams& p, cudaStream_t s) {
   const int64_t total = p.N * p.C * p.OH * p.OW;
   if (total <= 0) return;
-  pool_kernel<<<grid_for(total), kThreads, 0, s>>>(p);
+  const bool nhwc4 = p.C % 4 == 0 && p.in_st[1] == 1 && p.out_st[1] == 1 && p.in_st[3] == p.C &&
+                     p.out_st[3] == p.C && p.in_st[2] % 4 == 0 && p.out_st[2] % 4 == 0 && p.in_st[0] % 4 == 0 &&
+                     p.out_st[0] % 4 == 0 && (reinterpret_cast<uintptr_t>(p.in) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
+  if (nhwc4) pool_nhwc4_kernel<<<grid_for(total / 4), kThreads, 0, s>>>(p);
+  else pool_kernel<<<grid_for(total), kThreads, 0, s>>>(p);
 }
 
 // ---------------------------------------------------------------------------

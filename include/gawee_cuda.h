@@ -140,6 +140,14 @@ gawee_status gawee_plan_summary(const gawee_ctx* ctx, char* buf, size_t n);
  * ------------------------------------------------------------------------- */
 gawee_status gawee_ciface_forward(gawee_ctx* ctx, void* result_desc, void* const* arg_descs, int nargs);
 
+/* Entry point for code produced by the `--gawee-to-cuda` pipeline: the
+ * lowered module keeps the gawee-level `forward` text as a global string and
+ * its `_mlir_ciface_forward` calls this.  The first call on a thread plans the
+ * text for `device` and caches the context (keyed by the string's address);
+ * later calls reuse it.  Semantics as gawee_ciface_forward. */
+gawee_status gawee_embedded_forward(const char* mlir_text, int device, void* result_desc, void* const* arg_descs,
+                                    int nargs);
+
 /* ---------------------------------------------------------------------------
  * Data parallelism: batch sharding with replicated weights (one process or
  * thread per GPU).  The only collective is the gather of each rank's output

@@ -24,6 +24,7 @@ BIN = os.path.join(HERE, "bin")
 SOURCES = [
     "kernels/memory_ops.cu",
     "kernels/conv_gemm_tc.cu",
+    "kernels/noalloc_gemm.cu",
     "host/ir.cpp",
     "host/plan.cpp",
     "host/runtime.cpp",

@@ -661,6 +661,11 @@ int value_info(const gawee::Value& v, int* dtype, int* rank, int64_t* shape) {
 
 }  // namespace
 
+namespace gawee {
+// Error text for calls without a context (creation, context-free entry points).
+void set_thread_error(const std::string& msg) { g_create_error = msg; }
+}  // namespace gawee
+
 extern "C" {
 
 gawee_status gawee_create(const char* mlir_text, const char* entry, int device, gawee_ctx** out) {

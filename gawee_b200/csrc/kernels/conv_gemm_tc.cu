@@ -540,18 +540,21 @@ template <int BN, int STAGES, int EPI>
 bool launch_t(const ConvGemmParams& p, const void* tmh, const void* tml, cudaStream_t s) {
   auto kern = conv_gemm_tc_kernel<BN, STAGES, EPI>;
   constexpr int smem = Smem<BN, STAGES>::kBytes;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return false;
-    attr = true;
+  // the shared-memory opt-in is per device
+  static std::mutex mu;
+  static uint64_t attr_devices = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 64 && !(attr_devices >> dev & 1)) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return false;
+      attr_devices |= uint64_t(1) << dev;
+    }
   }
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-  }
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (sms <= 0) sms = 148;
   const int64_t tiles = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN) * p.nb;
   dim3 grid((unsigned)std::min<int64_t>(tiles, sms), 1, 1);
   kern<<<grid, kThreadsTC, smem, s>>>(p, *static_cast<const CUtensorMap*>(tmh), *static_cast<const CUtensorMap*>(tml));

@@ -71,6 +71,7 @@ def load_library(path: str = LIB_PATH):
             "gawee_profile_forward": (c.c_int, [P, P, c.POINTER(c.c_float), c.c_int]),
             "gawee_ciface_forward": (c.c_int, [P, P, c.POINTER(P), c.c_int]),
             "gawee_embedded_forward": (c.c_int, [c.c_char_p, c.c_int, P, c.POINTER(P), c.c_int]),
+            "gawee_matmul_f32_noalloc": (c.c_int, [P, P, P, c.c_int64, c.c_int64, c.c_int64, P]),
             "gawee_dp_unique_id": (c.c_int, [P]),
             "gawee_dp_init": (c.c_int, [P, c.c_int, c.c_int, P]),
             "gawee_dp_gather_output": (c.c_int, [P, c.c_int, P, P]),

@@ -149,6 +149,29 @@ gawee_status gawee_embedded_forward(const char* mlir_text, int device, void* res
                                     int nargs);
 
 /* ---------------------------------------------------------------------------
+ * Allocation-free matrix product (no counterpart in the reference).
+ *
+ * C[m][n] = A[m][k] . B[k][n], fp32 row-major device arrays owned by the
+ * caller, computed on the tensor-core kernel with split-precision TF32
+ * (the same arithmetic as gawee.matmul in a planned graph), enqueued on
+ * `stream`.  For callers that cannot allocate device memory when they need
+ * the product: inside CUDA stream capture, under a fixed memory budget or
+ * pool, or on an error path.  It calls no cudaMalloc/cudaFree: the packed
+ * TF32 planes of B use a 16 MiB array in the library's static device memory,
+ * which every GPU that loads the library holds until the process exits.
+ *   - Limits: k a multiple of 4, A 16-byte aligned, n * k <= 2,097,152
+ *     (two planes of n x k floats in 16 MiB); larger shapes return
+ *     GAWEE_ERR_INVALID with a message for gawee_last_error(NULL, ...).
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - Every call shares the one array: calls that overlap on the GPU (on
+ *     different streams, or from several threads) race.  Each call rewrites
+ *     all of the scratch it reads, so nothing needs clearing between calls.
+ * ------------------------------------------------------------------------- */
+gawee_status gawee_matmul_f32_noalloc(const float* a, const float* b, float* c, int64_t m, int64_t n, int64_t k,
+                                      void* stream);
+
+/* ---------------------------------------------------------------------------
  * Data parallelism: batch sharding with replicated weights (one process or
  * thread per GPU).  The only collective is the gather of each rank's output
  * rows to rank 0 over NCCL.

@@ -29,6 +29,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <climits>
 #include <cstdio>
 #include <mutex>
 
@@ -44,6 +45,10 @@ constexpr int kBM = 128;
 constexpr int kBK = 32;               // fp32 elements per k-block (one 128-byte swizzle row)
 constexpr int kThreadsTC = 448;  // 4 A-producer, 1 TMA, 1 MMA, 8 accumulator warps
 constexpr unsigned long long kWaitNs = 4000000000ull;  // 4 s per barrier wait
+// MMA stages and raw A k-blocks in flight per tile width (shared memory:
+// 3 x 48 KB + 4 x 16 KB for BN 64, 3 x 64 KB + 2 x 16 KB for BN 128)
+constexpr int kStages64 = 3, kRaw64 = 4;
+constexpr int kStages128 = 3, kRaw128 = 2;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -96,6 +101,21 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 16-byte global -> shared copy that bypasses registers; `bytes` 0 writes zeros.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ float4 lds128(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -167,12 +187,13 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int RD>
 struct Smem {
   static constexpr int kATile = kBM * kBK * 4;  // 16 KB
   static constexpr int kBTile = BN * kBK * 4;
   static constexpr int kStage = 2 * kATile + 2 * kBTile;
-  static constexpr int kBarOff = STAGES * kStage;
+  static constexpr int kRawOff = STAGES * kStage;  // RD raw A k-blocks in flight (cp.async targets)
+  static constexpr int kBarOff = kRawOff + RD * kATile;
   static constexpr int kNumBufs = 4;               // k-block accumulators in tensor memory
   static constexpr int kNumBars = 3 * STAGES + 2 * kNumBufs + 1;  // full_a/full_b/empty; tfull/tempty; done
   static constexpr int kBytes = kBarOff + 8 * kNumBars + 16 + 1024;  // + alignment slack
@@ -181,11 +202,11 @@ struct Smem {
 
 }  // namespace
 
-template <int BN, int STAGES, int EPI>
+template <int BN, int STAGES, int RD, int EPI>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     conv_gemm_tc_kernel(const __grid_constant__ ConvGemmParams p, const __grid_constant__ CUtensorMap tm_hi,
                         const __grid_constant__ CUtensorMap tm_lo) {
-  using L = Smem<BN, STAGES>;
+  using L = Smem<BN, STAGES, RD>;
   constexpr int NB = L::kNumBufs;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -253,90 +274,115 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 
   if (warp < 4) {
     // ------------------------------------------------------------------ A producer
+    // Thread (warp, lane) owns the 16-byte chunk `chunk` of rows
+    // warp*32 + i*4 + rsub (i < 8) of every A k-block: eight rows of 128
+    // bytes per instruction, so each load is fully coalesced.  The chunks go
+    // with cp.async into a ring of RD raw k-blocks that only this thread
+    // touches (no barrier), RD k-blocks ahead of the one being split; the
+    // split writes the TF32 high part and the fp32 remainder into the MMA
+    // stage.
     const int chunk = lane & 7;
     const int rsub = lane >> 3;
     const int64_t PQ = p.P * p.Q;
-    int64_t g = 0;  // k-blocks produced so far (all tiles): stage = g % STAGES
-    bool alive = true;
-    for (int64_t t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
+    const int64_t my_tiles = (int64_t)blockIdx.x < num_tiles ? (num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int64_t G = my_tiles * num_kb;  // k-blocks this CTA runs through
+    const uint32_t raw0 = smem_u32(smem + L::kRawOff) + (uint32_t)((warp * 32 + rsub) * 128 + chunk * 16);
+
+    // load cursor: tile, k-block, and the chunk's (c, r, s) within the filter window
+    int64_t lt = blockIdx.x;
+    int lkb = 0;
+    int64_t li = 0;
+    int64_t rowoff[8];
+    int ih0[8], iw0[8];
+    int kc = 0, kr = 0, ks = 0;
+    const int H = (int)p.H, W = (int)p.W, C = (int)p.C;
+    auto start_tile = [&]() {
       int64_t m0, a_off, c_off;
       int n0, z, b_plane;
-      tile_coords(t, m0, n0, z);
+      tile_coords(lt, m0, n0, z);
       batch_offsets(z, a_off, c_off, b_plane);
-      int64_t rbase[8];
-      int ih0[8], iw0[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int64_t m = m0 + warp * 32 + i * 4 + rsub;
         if (m < p.M) {
-          const int64_t img = m / PQ, pq = m % PQ;
-          const int64_t pp = pq / p.Q, qq = pq % p.Q;
-          rbase[i] = a_off + img * p.x_sn;
+          const int64_t img = m / PQ, pq = m - img * PQ;
+          const int64_t pp = pq / p.Q, qq = pq - pp * p.Q;
           ih0[i] = (int)(pp * p.sh - p.ph);
           iw0[i] = (int)(qq * p.sw - p.pw);
+          rowoff[i] = a_off + img * p.x_sn + (int64_t)ih0[i] * p.x_sh + (int64_t)iw0[i] * p.x_sw;
         } else {
-          rbase[i] = -1;
-          ih0[i] = 0;
+          ih0[i] = INT_MIN / 2;  // fails every bounds test
           iw0[i] = 0;
+          rowoff[i] = 0;
         }
       }
-      auto load_kb = [&](int kb, float4 (&v)[8]) {
-        const int64_t k0 = (int64_t)kb * kBK + chunk * 4;
-        int r = 0, s = 0;
-        int64_t c = 0;
-        const bool kin = k0 < p.K;
-        if (kin) {
-          const int64_t rs = k0 / p.C;
-          c = k0 - rs * p.C;
-          r = (int)(rs / p.S);
-          s = (int)(rs - (int64_t)r * p.S);
-        }
+      const int rs = (chunk * 4) / C;
+      kc = chunk * 4 - rs * C;
+      kr = rs / p.S;
+      ks = rs - kr * p.S;
+    };
+    auto issue = [&]() {
+      if (li < G) {
+        if (lkb == 0) start_tile();
+        const uint32_t dst = raw0 + (uint32_t)((li % RD) * L::kATile);
+        const bool kin = (int64_t)lkb * kBK + chunk * 4 < p.K;
+        const int dr = kr * p.dh, ds = ks * p.dw;
+        const int64_t koff = (int64_t)dr * p.x_sh + (int64_t)ds * p.x_sw + kc;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const int ih = ih0[i] + r * p.dh, iw = iw0[i] + s * p.dw;
-          if (kin && rbase[i] >= 0 && ih >= 0 && ih < p.H && iw >= 0 && iw < p.W) {
-            v[i] = __ldg(reinterpret_cast<const float4*>(p.x + rbase[i] + ih * p.x_sh + iw * p.x_sw + c));
-          } else {
-            v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+          const bool ok = kin && (unsigned)(ih0[i] + dr) < (unsigned)H && (unsigned)(iw0[i] + ds) < (unsigned)W;
+          cp_async16(dst + i * 4 * 128, ok ? (const void*)(p.x + rowoff[i] + koff) : (const void*)p.x, ok ? 16u : 0u);
+        }
+        // next k-block of the same chunk: k advances by 32
+        if (++lkb == num_kb) {
+          lkb = 0;
+          lt += gridDim.x;
+        } else {
+          kc += kBK;
+          while (kc >= C) {
+            kc -= C;
+            if (++ks == p.S) {
+              ks = 0;
+              ++kr;
+            }
           }
         }
-      };
-      // Two register buffers alternate between "being stored" and "loads in
-      // flight", so the next k-block's global loads overlap this block's wait,
-      // split and shared-memory stores.
-      auto store_kb = [&](const float4 (&v)[8]) -> bool {
-        const int st = (int)(g % STAGES);
-        const uint32_t ph = (uint32_t)((g / STAGES) & 1);
-        if (!mbar_wait(smem_u32(&empty[st]), ph ^ 1, abort_flag, p.status)) return false;
-        uint8_t* a_hi = smem + st * L::kStage;
-        uint8_t* a_lo = a_hi + L::kATile;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int row = warp * 32 + i * 4 + rsub;
-          const int off = row * 128 + ((chunk ^ (row & 7)) << 4);
-          const float4 x = v[i];
-          const float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
-          const float4 l =
-              make_float4(__fsub_rn(x.x, h.x), __fsub_rn(x.y, h.y), __fsub_rn(x.z, h.z), __fsub_rn(x.w, h.w));
-          *reinterpret_cast<float4*>(a_hi + off) = h;
-          *reinterpret_cast<float4*>(a_lo + off) = l;
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&full_a[st]));
-        ++g;
-        return true;
-      };
-      float4 va[8], vb[8];
-      load_kb(0, va);
-      for (int kb = 0; kb < num_kb; kb += 2) {
-        if (kb + 1 < num_kb) load_kb(kb + 1, vb);
-        if (!store_kb(va)) { alive = false; break; }
-        if (kb + 1 >= num_kb) break;
-        if (kb + 2 < num_kb) load_kb(kb + 2, va);
-        if (!store_kb(vb)) { alive = false; break; }
       }
+      cp_async_commit();  // empty groups past the end keep the group count uniform
+      ++li;
+    };
+
+#pragma unroll
+    for (int j = 0; j < RD; ++j) issue();
+    for (int64_t g = 0; g < G; ++g) {
+      cp_async_wait<RD - 1>();  // this thread's copies of k-block g have landed
+      const uint32_t src = raw0 + (uint32_t)((g % RD) * L::kATile);
+      float4 h[8], l[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 x = lds128(src + i * 4 * 128);
+        h[i] = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
+        l[i] = make_float4(__fsub_rn(x.x, h[i].x), __fsub_rn(x.y, h[i].y), __fsub_rn(x.z, h[i].z),
+                           __fsub_rn(x.w, h[i].w));
+      }
+      issue();  // refill the slot just read (its values are in registers)
+      const int st = (int)(g % STAGES);
+      const uint32_t ph = (uint32_t)((g / STAGES) & 1);
+      if (!mbar_wait(smem_u32(&empty[st]), ph ^ 1, abort_flag, p.status)) break;
+      uint8_t* a_hi = smem + st * L::kStage;
+      uint8_t* a_lo = a_hi + L::kATile;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int row = warp * 32 + i * 4 + rsub;
+        const int off = row * 128 + ((chunk ^ (row & 7)) << 4);
+        *reinterpret_cast<float4*>(a_hi + off) = h[i];
+        *reinterpret_cast<float4*>(a_lo + off) = l[i];
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&full_a[st]));
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");  // nothing of this thread in flight at exit
   } else if (warp == 4) {
     // ------------------------------------------------------------------ B producer (TMA)
     if (lane == 0) {
@@ -536,10 +582,11 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-template <int BN, int STAGES, int EPI>
+template <int BN, int STAGES, int RD, int EPI>
 bool launch_t(const ConvGemmParams& p, const void* tmh, const void* tml, cudaStream_t s) {
-  auto kern = conv_gemm_tc_kernel<BN, STAGES, EPI>;
-  constexpr int smem = Smem<BN, STAGES>::kBytes;
+  auto kern = conv_gemm_tc_kernel<BN, STAGES, RD, EPI>;
+  constexpr int smem = Smem<BN, STAGES, RD>::kBytes;
+  static_assert(smem <= 232448, "shared memory per CTA");
   // the shared-memory opt-in is per device
   static std::mutex mu;
   static uint64_t attr_devices = 0;
@@ -561,14 +608,14 @@ bool launch_t(const ConvGemmParams& p, const void* tmh, const void* tml, cudaStr
   return true;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int RD>
 bool launch_epi(const ConvGemmParams& p, const void* tmh, const void* tml, cudaStream_t s) {
   switch (p.epi) {
-    case EPI_NONE: return launch_t<BN, STAGES, EPI_NONE>(p, tmh, tml, s);
-    case EPI_BIAS: return launch_t<BN, STAGES, EPI_BIAS>(p, tmh, tml, s);
-    case EPI_BIAS_RELU: return launch_t<BN, STAGES, EPI_BIAS_RELU>(p, tmh, tml, s);
-    case EPI_BIAS_ADD_RELU: return launch_t<BN, STAGES, EPI_BIAS_ADD_RELU>(p, tmh, tml, s);
-    case EPI_PROGRAM: return launch_t<BN, STAGES, EPI_PROGRAM>(p, tmh, tml, s);
+    case EPI_NONE: return launch_t<BN, STAGES, RD, EPI_NONE>(p, tmh, tml, s);
+    case EPI_BIAS: return launch_t<BN, STAGES, RD, EPI_BIAS>(p, tmh, tml, s);
+    case EPI_BIAS_RELU: return launch_t<BN, STAGES, RD, EPI_BIAS_RELU>(p, tmh, tml, s);
+    case EPI_BIAS_ADD_RELU: return launch_t<BN, STAGES, RD, EPI_BIAS_ADD_RELU>(p, tmh, tml, s);
+    case EPI_PROGRAM: return launch_t<BN, STAGES, RD, EPI_PROGRAM>(p, tmh, tml, s);
     default: return false;
   }
 }
@@ -576,7 +623,7 @@ bool launch_epi(const ConvGemmParams& p, const void* tmh, const void* tml, cudaS
 }  // namespace
 
 int conv_gemm_smem_bytes(int block_n) {
-  return block_n == 64 ? Smem<64, 4>::kBytes : Smem<128, 3>::kBytes;
+  return block_n == 64 ? Smem<64, kStages64, kRaw64>::kBytes : Smem<128, kStages128, kRaw128>::kBytes;
 }
 
 bool make_b_tensor_maps(const float* hi, const float* lo, int64_t batch, int64_t N, int64_t ldk, int block_n,
@@ -609,8 +656,8 @@ bool launch_conv_gemm_tc(const ConvGemmParams& p, const void* tmap_hi, const voi
   for (int d = 0; d < p.batch_rank; ++d)
     if (p.a_bst[d] % 4 != 0) return false;
   if (p.nb > (1 << 30)) return false;
-  if (block_n == 64) return launch_epi<64, 4>(p, tmap_hi, tmap_lo, s);
-  if (block_n == 128) return launch_epi<128, 3>(p, tmap_hi, tmap_lo, s);
+  if (block_n == 64) return launch_epi<64, kStages64, kRaw64>(p, tmap_hi, tmap_lo, s);
+  if (block_n == 128) return launch_epi<128, kStages128, kRaw128>(p, tmap_hi, tmap_lo, s);
   return false;
 }
 

@@ -3,23 +3,29 @@
 // One CTA computes a 128 x BN tile of C = A . B^T with fp32 accuracy from
 // TF32 tensor cores: three tcgen05.mma per k-step (hi*hi + hi*lo + lo*hi; see
 // Ootomo & Yokota, "Recovering single precision accuracy from Tensor Cores
-// while surpassing the FP32 theoretical peak performance", 2022).
+// while surpassing the FP32 theoretical peak performance", 2022).  The tensor
+// core reads an fp32 operand as TF32 by dropping its 13 low mantissa bits, so
+// the raw value serves as the high part and only the remainder x - tf32(x)
+// is formed explicitly.
 //
 // The tensor core's fp32 accumulation truncates (Fasi et al., "Numerical
 // behavior of NVIDIA tensor cores", 2021), so over thousands of k-steps its
 // error grows linearly with K.  Each 32-wide k-block is therefore accumulated
-// alone in one of four tensor-memory buffers, and the accumulator warps add
-// the block sums into fp32 registers with IEEE round-to-nearest while later
-// blocks are multiplied into the other buffers.
+// alone in a tensor-memory buffer, and the accumulator warps add the block
+// sums into fp32 registers with IEEE round-to-nearest while later blocks are
+// multiplied into the other buffers.
+//
+// Operands: A (im2col rows of the NHWC input, or GEMM rows) lives in tensor
+// memory, B (pre-split weight planes) in shared memory, so the MMAs read only
+// B through the shared-memory port (tcgen05.mma with [a-tmem]).
 //
 // Warp roles (448 threads), persistent over output tiles (one CTA per SM):
-//   warps 0-3  gather the A tile (im2col rows of the NHWC input, zero padding,
-//              K tails) with 16-byte loads, split each value into an exact
-//              TF32 high part and an fp32 remainder in registers, and store
-//              both into 128B-swizzled K-major shared-memory tiles
-//   warp 4     issues the TMA loads of the pre-split B planes; owns the TMEM
-//              allocation
-//   warp 5     one elected thread issues tcgen05.mma and tcgen05.commit
+//   warps 0-3  copy the A rows with cp.async into a shared-memory ring several
+//              k-blocks ahead (zero padding and K tails by zero-fill), then
+//              write raw values and remainders into the A stage in tensor
+//              memory with tcgen05.st (warp w owns TMEM lanes 32w..32w+31)
+//   warp 4     issues the TMA loads of the B planes; owns the TMEM allocation
+//   warp 5     lane 0 issues tcgen05.mma and the tcgen05.commit that track them
 //   warps 6-13 accumulate block sums from TMEM (two warps per TMEM lane
 //              quarter, each owning half the tile's columns) and run the
 //              epilogue of tile t while the MMAs of tile t+1 proceed
@@ -45,10 +51,20 @@ constexpr int kBM = 128;
 constexpr int kBK = 32;               // fp32 elements per k-block (one 128-byte swizzle row)
 constexpr int kThreadsTC = 448;  // 4 A-producer, 1 TMA, 1 MMA, 8 accumulator warps
 constexpr unsigned long long kWaitNs = 4000000000ull;  // 4 s per barrier wait
-// MMA stages and raw A k-blocks in flight per tile width (shared memory:
-// 3 x 48 KB + 4 x 16 KB for BN 64, 3 x 64 KB + 2 x 16 KB for BN 128)
-constexpr int kStages64 = 3, kRaw64 = 4;
-constexpr int kStages128 = 3, kRaw128 = 2;
+// Pipeline depths per tile width: B stages, raw A k-blocks in flight, A stages
+// and accumulators in tensor memory.  Shared memory: 6 x 16 KB + 6 x 16 KB
+// for BN 64, 4 x 32 KB + 5 x 16 KB for BN 128; tensor memory: 4 x 64 + 4 x 64
+// and 2 x 128 + 4 x 64 of its 512 columns.
+template <int BN>
+struct TcConfig;
+template <>
+struct TcConfig<64> {
+  static constexpr int SB = 6, RD = 6, SA = 4, NB = 4;
+};
+template <>
+struct TcConfig<128> {
+  static constexpr int SB = 4, RD = 5, SA = 4, NB = 2;
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -99,9 +115,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 
 // 16-byte global -> shared copy that bypasses registers; `bytes` 0 writes zeros.
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
@@ -146,13 +159,26 @@ __device__ __forceinline__ uint32_t umma_idesc_tf32() {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accumulate) {
+
+// D (tensor memory) += A (tensor memory, lane = row, one column per k) . B (shared memory)
+__device__ __forceinline__ void umma_tf32_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
 
@@ -160,18 +186,6 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
-      "[%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
@@ -187,36 +201,42 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
 
-template <int BN, int STAGES, int RD>
+// Shared memory: SB stages of B (hi and lo planes, TMA), RD raw A k-blocks
+// (cp.async ring, 128 rows x 128 B, 16-byte chunks swizzled by row), then the
+// barriers.  Tensor memory: NB k-block accumulators of BN columns, then SA
+// A stages of 64 columns (32 raw values, 32 remainders; lane = row).
+template <int BN, int SB, int RD, int SA, int NB>
 struct Smem {
   static constexpr int kATile = kBM * kBK * 4;  // 16 KB
   static constexpr int kBTile = BN * kBK * 4;
-  static constexpr int kStage = 2 * kATile + 2 * kBTile;
-  static constexpr int kRawOff = STAGES * kStage;  // RD raw A k-blocks in flight (cp.async targets)
+  static constexpr int kBStage = 2 * kBTile;
+  static constexpr int kRawOff = SB * kBStage;
   static constexpr int kBarOff = kRawOff + RD * kATile;
-  static constexpr int kNumBufs = 4;               // k-block accumulators in tensor memory
-  static constexpr int kNumBars = 3 * STAGES + 2 * kNumBufs + 1;  // full_a/full_b/empty; tfull/tempty; done
+  static constexpr int kNumBars = 2 * SA + 2 * SB + 2 * NB + 1;  // full/empty A, B, TMEM buffers; done
   static constexpr int kBytes = kBarOff + 8 * kNumBars + 16 + 1024;  // + alignment slack
-  static constexpr int kTmemCols = kNumBufs * BN;
+  static constexpr int kACol = NB * BN;
+  static constexpr int kUsedCols = NB * BN + SA * 2 * kBK;
+  static constexpr int kTmemCols = kUsedCols <= 256 ? 256 : 512;
+  static_assert(kUsedCols <= 512, "tensor memory columns");
 };
 
 }  // namespace
 
-template <int BN, int STAGES, int RD, int EPI>
+template <int BN, int SB, int RD, int SA, int NB, int EPI>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     conv_gemm_tc_kernel(const __grid_constant__ ConvGemmParams p, const __grid_constant__ CUtensorMap tm_hi,
                         const __grid_constant__ CUtensorMap tm_lo) {
-  using L = Smem<BN, STAGES, RD>;
-  constexpr int NB = L::kNumBufs;
+  using L = Smem<BN, SB, RD, SA, NB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
-  uint64_t* full_a = bars;
-  uint64_t* full_b = bars + STAGES;
-  uint64_t* empty = bars + 2 * STAGES;
-  uint64_t* tfull = bars + 3 * STAGES;        // [NB] k-block sum ready in TMEM buffer
-  uint64_t* tempty = bars + 3 * STAGES + NB;  // [NB] TMEM buffer drained by the accumulator warps
-  uint64_t* done = bars + 3 * STAGES + 2 * NB;  // every MMA issued by this CTA completed
+  uint64_t* full_a = bars;                  // [SA] A stage written to tensor memory (4 producer warps)
+  uint64_t* empty_a = bars + SA;            // [SA] A stage consumed by the MMAs
+  uint64_t* full_b = bars + 2 * SA;         // [SB] B stage landed (TMA transaction bytes)
+  uint64_t* empty_b = bars + 2 * SA + SB;   // [SB] B stage consumed by the MMAs
+  uint64_t* tfull = bars + 2 * SA + 2 * SB;        // [NB] k-block sum ready in a TMEM buffer
+  uint64_t* tempty = bars + 2 * SA + 2 * SB + NB;  // [NB] TMEM buffer drained by the accumulator warps
+  uint64_t* done = bars + 2 * SA + 2 * SB + 2 * NB;  // every MMA issued by this CTA completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -233,6 +253,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     n0 = (int)(((t / m_tiles) % n_tiles) * BN);
     z = (int)(t / (m_tiles * n_tiles));
   };
+  // Each tile walks its k-blocks starting at (m tile index mod num_kb):
+  // CTAs that run side by side then fetch different k-blocks of the shared
+  // B operand instead of all hitting the same L2 lines at once.
+  auto k_rotation = [&](int64_t t) -> int { return (int)((t % m_tiles) % num_kb); };
   auto batch_offsets = [&](int z, int64_t& a_off, int64_t& c_off, int& b_plane) {
     a_off = 0;
     c_off = 0;
@@ -248,10 +272,13 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < SA; ++s) {
       mbar_init(smem_u32(&full_a[s]), 4);
+      mbar_init(smem_u32(&empty_a[s]), 1);
+    }
+    for (int s = 0; s < SB; ++s) {
       mbar_init(smem_u32(&full_b[s]), 1);
-      mbar_init(smem_u32(&empty[s]), 1);
+      mbar_init(smem_u32(&empty_b[s]), 1);
     }
     for (int b = 0; b < NB; ++b) {
       mbar_init(smem_u32(&tfull[b]), 1);
@@ -274,28 +301,37 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 
   if (warp < 4) {
     // ------------------------------------------------------------------ A producer
-    // Thread (warp, lane) owns the 16-byte chunk `chunk` of rows
-    // warp*32 + i*4 + rsub (i < 8) of every A k-block: eight rows of 128
-    // bytes per instruction, so each load is fully coalesced.  The chunks go
-    // with cp.async into a ring of RD raw k-blocks that only this thread
-    // touches (no barrier), RD k-blocks ahead of the one being split; the
-    // split writes the TF32 high part and the fp32 remainder into the MMA
-    // stage.
+    // Warp w owns rows 32w..32w+31 of every A tile: the tensor-memory lanes
+    // it may write.  Its lanes copy those rows with cp.async in 16-byte
+    // chunks (lane -> chunk lane%8 of rows i*4 + lane/8, so each instruction
+    // reads four whole 128-byte rows) into a ring of RD raw k-blocks that
+    // only this warp touches, RD k-blocks ahead.  Then each lane takes its
+    // own row, stores the raw values (the tensor core reads fp32 as TF32 by
+    // dropping the low 13 mantissa bits, so raw is the high part) and the
+    // remainders x - tf32(x) into the A stage in tensor memory.
     const int chunk = lane & 7;
     const int rsub = lane >> 3;
     const int64_t PQ = p.P * p.Q;
     const int64_t my_tiles = (int64_t)blockIdx.x < num_tiles ? (num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
     const int64_t G = my_tiles * num_kb;  // k-blocks this CTA runs through
-    const uint32_t raw0 = smem_u32(smem + L::kRawOff) + (uint32_t)((warp * 32 + rsub) * 128 + chunk * 16);
+    const uint32_t raw_base = smem_u32(smem + L::kRawOff);
+    const uint32_t tmem_rows = tmem_base + ((uint32_t)(warp * 32) << 16);
 
     // load cursor: tile, k-block, and the chunk's (c, r, s) within the filter window
     int64_t lt = blockIdx.x;
-    int lkb = 0;
+    int lkb = 0;  // k-blocks of the current tile issued so far
+    int lka = 0;  // the k-block they are at (rotated order)
     int64_t li = 0;
     int64_t rowoff[8];
     int ih0[8], iw0[8];
     int kc = 0, kr = 0, ks = 0;
     const int H = (int)p.H, W = (int)p.W, C = (int)p.C;
+    auto decompose = [&](int k) {
+      const int rs = k / C;
+      kc = k - rs * C;
+      kr = rs / p.S;
+      ks = rs - kr * p.S;
+    };
     auto start_tile = [&]() {
       int64_t m0, a_off, c_off;
       int n0, z, b_plane;
@@ -316,27 +352,30 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           rowoff[i] = 0;
         }
       }
-      const int rs = (chunk * 4) / C;
-      kc = chunk * 4 - rs * C;
-      kr = rs / p.S;
-      ks = rs - kr * p.S;
+      lka = k_rotation(lt);
+      decompose(lka * kBK + chunk * 4);
     };
     auto issue = [&]() {
       if (li < G) {
         if (lkb == 0) start_tile();
-        const uint32_t dst = raw0 + (uint32_t)((li % RD) * L::kATile);
-        const bool kin = (int64_t)lkb * kBK + chunk * 4 < p.K;
+        const uint32_t slot = raw_base + (uint32_t)((li % RD) * L::kATile);
+        const bool kin = (int64_t)lka * kBK + chunk * 4 < p.K;
         const int dr = kr * p.dh, ds = ks * p.dw;
         const int64_t koff = (int64_t)dr * p.x_sh + (int64_t)ds * p.x_sw + kc;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
+          const int row = warp * 32 + i * 4 + rsub;
           const bool ok = kin && (unsigned)(ih0[i] + dr) < (unsigned)H && (unsigned)(iw0[i] + ds) < (unsigned)W;
-          cp_async16(dst + i * 4 * 128, ok ? (const void*)(p.x + rowoff[i] + koff) : (const void*)p.x, ok ? 16u : 0u);
+          cp_async16(slot + row * 128 + ((chunk ^ (row & 7)) << 4),
+                     ok ? (const void*)(p.x + rowoff[i] + koff) : (const void*)p.x, ok ? 16u : 0u);
         }
-        // next k-block of the same chunk: k advances by 32
+        // next k-block of the same chunk: k advances by 32 (wrapping to 0)
         if (++lkb == num_kb) {
           lkb = 0;
           lt += gridDim.x;
+        } else if (++lka == num_kb) {
+          lka = 0;
+          decompose(chunk * 4);
         } else {
           kc += kBK;
           while (kc >= C) {
@@ -352,35 +391,40 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       ++li;
     };
 
+    const int row = warp * 32 + lane;
 #pragma unroll
     for (int j = 0; j < RD; ++j) issue();
     for (int64_t g = 0; g < G; ++g) {
-      cp_async_wait<RD - 1>();  // this thread's copies of k-block g have landed
-      const uint32_t src = raw0 + (uint32_t)((g % RD) * L::kATile);
-      float4 h[8], l[8];
+      cp_async_wait<RD - 1>();  // this lane's copies of k-block g have landed
+      __syncwarp();             // ... and every other lane's
+      const int sa = (int)(g % SA);
+      if (!mbar_wait(smem_u32(&empty_a[sa]), (uint32_t)(((g / SA) & 1) ^ 1), abort_flag, p.status)) break;
+      tc_fence_after();
+      const uint32_t src = raw_base + (uint32_t)((g % RD) * L::kATile) + row * 128;
+      uint32_t x[32];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 x = lds128(src + i * 4 * 128);
-        h[i] = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
-        l[i] = make_float4(__fsub_rn(x.x, h[i].x), __fsub_rn(x.y, h[i].y), __fsub_rn(x.z, h[i].z),
-                           __fsub_rn(x.w, h[i].w));
+      for (int c = 0; c < 8; ++c) {
+        const float4 v = lds128(src + ((c ^ (row & 7)) << 4));
+        x[4 * c] = __float_as_uint(v.x);
+        x[4 * c + 1] = __float_as_uint(v.y);
+        x[4 * c + 2] = __float_as_uint(v.z);
+        x[4 * c + 3] = __float_as_uint(v.w);
       }
-      issue();  // refill the slot just read (its values are in registers)
-      const int st = (int)(g % STAGES);
-      const uint32_t ph = (uint32_t)((g / STAGES) & 1);
-      if (!mbar_wait(smem_u32(&empty[st]), ph ^ 1, abort_flag, p.status)) break;
-      uint8_t* a_hi = smem + st * L::kStage;
-      uint8_t* a_lo = a_hi + L::kATile;
+      const uint32_t acol = tmem_rows + (uint32_t)(L::kACol + sa * 2 * kBK);
+      tmem_st32(acol, x);
+      uint32_t y[32];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int row = warp * 32 + i * 4 + rsub;
-        const int off = row * 128 + ((chunk ^ (row & 7)) << 4);
-        *reinterpret_cast<float4*>(a_hi + off) = h[i];
-        *reinterpret_cast<float4*>(a_lo + off) = l[i];
+      for (int j = 0; j < 32; ++j) {
+        const float v = __uint_as_float(x[j]);
+        y[j] = __float_as_uint(__fsub_rn(v, tf32_hi(v)));
       }
-      fence_proxy_async_smem();
+      __syncwarp();  // every lane has read its row: the slot may be refilled
+      issue();
+      tmem_st32(acol + kBK, y);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&full_a[st]));
+      if (lane == 0) mbar_arrive(smem_u32(&full_a[sa]));
     }
     asm volatile("cp.async.wait_all;" ::: "memory");  // nothing of this thread in flight at exit
   } else if (warp == 4) {
@@ -395,67 +439,79 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         int n0, z, b_plane;
         tile_coords(t, m0, n0, z);
         batch_offsets(z, a_off, c_off, b_plane);
+        int ka = k_rotation(t);
         for (int kb = 0; kb < num_kb; ++kb) {
-          const int st = (int)(g % STAGES);
-          const uint32_t ph = (uint32_t)((g / STAGES) & 1);
-          if (!mbar_wait(smem_u32(&empty[st]), ph ^ 1, abort_flag, p.status)) { alive = false; break; }
-          uint8_t* b_hi = smem + st * L::kStage + 2 * L::kATile;
+          const int sb = (int)(g % SB);
+          if (!mbar_wait(smem_u32(&empty_b[sb]), (uint32_t)(((g / SB) & 1) ^ 1), abort_flag, p.status)) {
+            alive = false;
+            break;
+          }
+          uint8_t* b_hi = smem + sb * L::kBStage;
           uint8_t* b_lo = b_hi + L::kBTile;
-          const uint32_t bar = smem_u32(&full_b[st]);
+          const uint32_t bar = smem_u32(&full_b[sb]);
           mbar_arrive_tx(bar, 2 * L::kBTile);
-          tma_load_3d(smem_u32(b_hi), &tm_hi, bar, kb * kBK, n0, b_plane);
-          tma_load_3d(smem_u32(b_lo), &tm_lo, bar, kb * kBK, n0, b_plane);
+          tma_load_3d(smem_u32(b_hi), &tm_hi, bar, ka * kBK, n0, b_plane);
+          tma_load_3d(smem_u32(b_lo), &tm_lo, bar, ka * kBK, n0, b_plane);
+          if (++ka == num_kb) ka = 0;
           ++g;
         }
       }
       if (*abort_flag) {
         // let copies already in flight land before the CTA retires
-        for (int64_t k = g - STAGES < 0 ? 0 : g - STAGES; k < g; ++k) {
+        for (int64_t k = g - SB < 0 ? 0 : g - SB; k < g; ++k) {
           volatile int never = 0;
-          mbar_wait(smem_u32(&full_b[k % STAGES]), (uint32_t)((k / STAGES) & 1), &never, nullptr);
+          mbar_wait(smem_u32(&full_b[k % SB]), (uint32_t)((k / SB) & 1), &never, nullptr);
         }
       }
     }
   } else if (warp == 5) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = umma_idesc_tf32<BN>();
-      int64_t g = 0;
-      bool alive = true;
-      for (int64_t t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
-        for (int kb = 0; kb < num_kb; ++kb) {
-          const int st = (int)(g % STAGES);
-          const uint32_t ph = (uint32_t)((g / STAGES) & 1);
-          const int buf = (int)(g % NB);
-          const uint32_t use = (uint32_t)((g / NB) & 1);
-          if (!mbar_wait(smem_u32(&full_a[st]), ph, abort_flag, p.status) ||
-              !mbar_wait(smem_u32(&full_b[st]), ph, abort_flag, p.status) ||
-              !mbar_wait(smem_u32(&tempty[buf]), use ^ 1, abort_flag, p.status)) {
-            alive = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a_hi = smem_u32(smem + st * L::kStage);
-          const uint32_t a_lo = a_hi + L::kATile;
-          const uint32_t b_hi = a_hi + 2 * L::kATile;
-          const uint32_t b_lo = b_hi + L::kBTile;
-          const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BN);
+    // The whole warp runs the loop (its values stay warp-uniform); lane 0
+    // issues the MMAs and the commits that track them.  A comes from tensor
+    // memory (raw and remainder columns), B from shared memory.
+    const uint32_t idesc = umma_idesc_tf32<BN>();
+    const uint64_t desc0 = umma_desc_sw128(smem_u32(smem));
+    constexpr uint64_t kBStageDesc = (uint64_t)(L::kBStage >> 4);  // descriptor start-address units
+    constexpr uint64_t kBTileDesc = (uint64_t)(L::kBTile >> 4);
+    int64_t g = 0;
+    bool alive = true;
+    for (int64_t t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int sa = (int)(g % SA);
+        const int sb = (int)(g % SB);
+        const int buf = (int)(g % NB);
+        if (!mbar_wait(smem_u32(&full_a[sa]), (uint32_t)((g / SA) & 1), abort_flag, p.status) ||
+            !mbar_wait(smem_u32(&full_b[sb]), (uint32_t)((g / SB) & 1), abort_flag, p.status) ||
+            !mbar_wait(smem_u32(&tempty[buf]), (uint32_t)(((g / NB) & 1) ^ 1), abort_flag, p.status)) {
+          alive = false;
+          break;
+        }
+        tc_fence_after();
+        // the start address of a K-major SW128 descriptor advances 32 bytes
+        // (2 units) per 8-wide k-step; an A column holds one k
+        const uint64_t dbh = desc0 + (uint64_t)sb * kBStageDesc;
+        const uint64_t dbl = dbh + kBTileDesc;
+        const uint32_t a_raw = tmem_base + (uint32_t)(L::kACol + sa * 2 * kBK);
+        const uint32_t a_rem = a_raw + kBK;
+        const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BN);
+        if (lane == 0) {
 #pragma unroll
           for (int kk = 0; kk < kBK / 8; ++kk) {
-            const uint32_t koff = kk * 32;  // 8 tf32 = 32 bytes along the swizzled row
-            const uint64_t dah = umma_desc_sw128(a_hi + koff), dal = umma_desc_sw128(a_lo + koff);
-            const uint64_t dbh = umma_desc_sw128(b_hi + koff), dbl = umma_desc_sw128(b_lo + koff);
-            umma_tf32(tmem_d, dal, dbh, idesc, kk != 0);
-            umma_tf32(tmem_d, dah, dbl, idesc, 1);
-            umma_tf32(tmem_d, dah, dbh, idesc, 1);
+            const uint64_t o = (uint64_t)(2 * kk);
+            const uint32_t ka = (uint32_t)(8 * kk);
+            umma_tf32_ts(tmem_d, a_rem + ka, dbh + o, idesc, kk != 0);
+            umma_tf32_ts(tmem_d, a_raw + ka, dbl + o, idesc, 1);
+            umma_tf32_ts(tmem_d, a_raw + ka, dbh + o, idesc, 1);
           }
-          umma_commit(smem_u32(&empty[st]));
+          umma_commit(smem_u32(&empty_a[sa]));
+          umma_commit(smem_u32(&empty_b[sb]));
           umma_commit(smem_u32(&tfull[buf]));
-          ++g;
         }
+        __syncwarp();
+        ++g;
       }
-      umma_commit(smem_u32(done));
     }
+    if (lane == 0) umma_commit(smem_u32(done));
   } else {
     // ------------------------------------------------------------------ accumulate + epilogue
     // warps 6..13: lane quarter (warp % 4) is fixed by the hardware; two
@@ -582,10 +638,11 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-template <int BN, int STAGES, int RD, int EPI>
+template <int BN, int EPI>
 bool launch_t(const ConvGemmParams& p, const void* tmh, const void* tml, cudaStream_t s) {
-  auto kern = conv_gemm_tc_kernel<BN, STAGES, RD, EPI>;
-  constexpr int smem = Smem<BN, STAGES, RD>::kBytes;
+  using Cfg = TcConfig<BN>;
+  auto kern = conv_gemm_tc_kernel<BN, Cfg::SB, Cfg::RD, Cfg::SA, Cfg::NB, EPI>;
+  constexpr int smem = Smem<BN, Cfg::SB, Cfg::RD, Cfg::SA, Cfg::NB>::kBytes;
   static_assert(smem <= 232448, "shared memory per CTA");
   // the shared-memory opt-in is per device
   static std::mutex mu;
@@ -608,14 +665,14 @@ bool launch_t(const ConvGemmParams& p, const void* tmh, const void* tml, cudaStr
   return true;
 }
 
-template <int BN, int STAGES, int RD>
+template <int BN>
 bool launch_epi(const ConvGemmParams& p, const void* tmh, const void* tml, cudaStream_t s) {
   switch (p.epi) {
-    case EPI_NONE: return launch_t<BN, STAGES, RD, EPI_NONE>(p, tmh, tml, s);
-    case EPI_BIAS: return launch_t<BN, STAGES, RD, EPI_BIAS>(p, tmh, tml, s);
-    case EPI_BIAS_RELU: return launch_t<BN, STAGES, RD, EPI_BIAS_RELU>(p, tmh, tml, s);
-    case EPI_BIAS_ADD_RELU: return launch_t<BN, STAGES, RD, EPI_BIAS_ADD_RELU>(p, tmh, tml, s);
-    case EPI_PROGRAM: return launch_t<BN, STAGES, RD, EPI_PROGRAM>(p, tmh, tml, s);
+    case EPI_NONE: return launch_t<BN, EPI_NONE>(p, tmh, tml, s);
+    case EPI_BIAS: return launch_t<BN, EPI_BIAS>(p, tmh, tml, s);
+    case EPI_BIAS_RELU: return launch_t<BN, EPI_BIAS_RELU>(p, tmh, tml, s);
+    case EPI_BIAS_ADD_RELU: return launch_t<BN, EPI_BIAS_ADD_RELU>(p, tmh, tml, s);
+    case EPI_PROGRAM: return launch_t<BN, EPI_PROGRAM>(p, tmh, tml, s);
     default: return false;
   }
 }
@@ -623,7 +680,10 @@ bool launch_epi(const ConvGemmParams& p, const void* tmh, const void* tml, cudaS
 }  // namespace
 
 int conv_gemm_smem_bytes(int block_n) {
-  return block_n == 64 ? Smem<64, kStages64, kRaw64>::kBytes : Smem<128, kStages128, kRaw128>::kBytes;
+  using C64 = TcConfig<64>;
+  using C128 = TcConfig<128>;
+  return block_n == 64 ? Smem<64, C64::SB, C64::RD, C64::SA, C64::NB>::kBytes
+                       : Smem<128, C128::SB, C128::RD, C128::SA, C128::NB>::kBytes;
 }
 
 bool make_b_tensor_maps(const float* hi, const float* lo, int64_t batch, int64_t N, int64_t ldk, int block_n,
@@ -656,8 +716,8 @@ bool launch_conv_gemm_tc(const ConvGemmParams& p, const void* tmap_hi, const voi
   for (int d = 0; d < p.batch_rank; ++d)
     if (p.a_bst[d] % 4 != 0) return false;
   if (p.nb > (1 << 30)) return false;
-  if (block_n == 64) return launch_epi<64, kStages64, kRaw64>(p, tmap_hi, tmap_lo, s);
-  if (block_n == 128) return launch_epi<128, kStages128, kRaw128>(p, tmap_hi, tmap_lo, s);
+  if (block_n == 64) return launch_epi<64>(p, tmap_hi, tmap_lo, s);
+  if (block_n == 128) return launch_epi<128>(p, tmap_hi, tmap_lo, s);
   return false;
 }
 

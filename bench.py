@@ -302,6 +302,15 @@ def main():
         sys.stderr.write("per-kernel ms (one eager forward):\n")
         for (n, tc, f), t in sorted(zip(kern, prof), key=lambda x: -x[1])[:12]:
             sys.stderr.write(f"  {t:8.3f} ms  {'TC' if tc else '  '} {f / 1e9:9.2f} GFLOP  {n}\n")
+        groups = {}
+        for (n, tc, f), t in zip(kern, prof):
+            g = groups.setdefault(n, [0, 0.0, 0.0])
+            g[0] += 1
+            g[1] += t
+            g[2] += f
+        sys.stderr.write("by op (launches, total ms, GFLOP):\n")
+        for n, (c, t, f) in sorted(groups.items(), key=lambda x: -x[1][1]):
+            sys.stderr.write(f"  {t:9.3f} ms  {c:5d}  {f / 1e9:9.2f} GFLOP  {n}\n")
         print(json.dumps(line), flush=True)
     m.close()
     if world > 1:

@@ -203,6 +203,33 @@ static kern::DProgram to_device(const EProgram& p) {
   return d;
 }
 
+// Recognises the GEMM epilogue programs the emitter's decoder blocks produce
+// (residual add, score scale + mask, SiLU-gated product) so the kernel can
+// evaluate them without the interpreter.  Registers: r0 = accumulator,
+// r1.. = aux operands; every match checks the exact operation sequence, so
+// the fast path computes the same IEEE operations in the same order.
+static int match_fast_epilogue(const EProgram& p, float* c) {
+  const auto& k = p.code;
+  auto f32 = [&](const EInstr& in) { return in.ty == DType::F32 && in.rty == DType::F32; };
+  auto uses = [](const EInstr& in, int x, int y) { return (in.a == x && in.b == y) || (in.a == y && in.b == x); };
+  for (const auto& in : k)
+    if (!f32(in)) return kern::FAST_NONE;
+  if (p.n_args == 2 && k.size() == 1 && k[0].op == EOp::ADDF && uses(k[0], 0, 1) && p.result == k[0].dst)
+    return kern::FAST_ADD;
+  if (p.n_args == 2 && k.size() == 3 && k[0].op == EOp::CONST && k[1].op == EOp::DIVF && k[1].a == 0 &&
+      k[1].b == k[0].dst && k[2].op == EOp::ADDF && uses(k[2], k[1].dst, 1) && p.result == k[2].dst) {
+    *c = (float)k[0].fimm;
+    return kern::FAST_DIVC_ADD;
+  }
+  if (p.n_args == 3 && k.size() == 7 && k[0].op == EOp::CONST && k[0].fimm == 1.0 && k[1].op == EOp::NEGF &&
+      k[1].a == 2 && k[2].op == EOp::EXP && k[2].a == k[1].dst && k[3].op == EOp::ADDF &&
+      uses(k[3], k[0].dst, k[2].dst) && k[4].op == EOp::DIVF && k[4].a == k[0].dst && k[4].b == k[3].dst &&
+      k[5].op == EOp::MULF && uses(k[5], 1, k[4].dst) && k[6].op == EOp::MULF && uses(k[6], k[5].dst, 0) &&
+      p.result == k[6].dst)
+    return kern::FAST_SIGMOID_MUL;
+  return kern::FAST_NONE;
+}
+
 static void launch_ew(Runtime& rt, const Op& op, cudaStream_t s) {
   const View& out = op.out;
   int r = out.rank();
@@ -306,7 +333,10 @@ static void launch_tc(Runtime& rt, int o, const Op& op, cudaStream_t s) {
     p.aux_sn[a] = v.st[r - 1];
     for (int d = 0; d < t.batch_rank; ++d) p.aux_sb[a][d] = v.st[d];
   }
-  if (t.epi == kern::EPI_PROGRAM) p.prog = to_device(t.prog);
+  if (t.epi == kern::EPI_PROGRAM) {
+    p.prog = to_device(t.prog);
+    p.fast = match_fast_epilogue(t.prog, &p.fast_c);
+  }
   p.status = rt.status();
   if (!kern::launch_conv_gemm_tc(p, rt.tmaps[o][0].b, rt.tmaps[o][1].b, t.block_n, s))
     throw StatusError(GAWEE_ERR_UNSUPPORTED, "tensor-core launch rejected the shape of op " + op.name);

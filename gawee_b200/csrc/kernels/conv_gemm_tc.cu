@@ -558,23 +558,70 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       float* crow = p.out + c_off + m * p.ldc;
       const int nb0 = n0 + cbase;  // first column of this thread's half tile
       if (EPI == EPI_PROGRAM) {
+        // operand offsets of this row: the batch coordinate is fixed per tile
+        int64_t aux_row[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+          aux_row[a] = 0;
+          if (a < p.n_aux) {
+            int64_t o = m * p.aux_sm[a], rem = z;
+            for (int d = p.batch_rank - 1; d >= 0; --d) {
+              o += (rem % p.batch_shape[d]) * p.aux_sb[a][d];
+              rem /= p.batch_shape[d];
+            }
+            aux_row[a] = o;
+          }
+        }
+        const bool vec = p.ldc_n == 1 && nb0 + HB <= p.N && ((reinterpret_cast<uintptr_t>(crow + nb0) & 15) == 0);
         Reg regs[kMaxRegs];
         int err = 0;
+        // 8 columns at a time: their operand loads are all in flight before
+        // the program runs on them
+        for (int c0 = 0; c0 < HB; c0 += 8) {
+          float av[4][8];
 #pragma unroll
-        for (int j = 0; j < HB; ++j) {
-          const int64_t n = nb0 + j;
-          if (n < p.N) {
-            regs[0].f = p.bias ? __fadd_rn(acc[j], p.bias[n]) : acc[j];
-            for (int a = 0; a < p.n_aux; ++a) {
-              int64_t ao = m * p.aux_sm[a] + n * p.aux_sn[a];
-              int64_t rem = z;
-              for (int d = p.batch_rank - 1; d >= 0; --d) {
-                ao += (rem % p.batch_shape[d]) * p.aux_sb[a][d];
-                rem /= p.batch_shape[d];
-              }
-              regs[1 + a].f = p.aux[a][ao];
+          for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int64_t n = nb0 + c0 + j;
+              av[a][j] = (a < p.n_aux && n < p.N) ? __ldg(p.aux[a] + aux_row[a] + n * p.aux_sn[a]) : 0.f;
             }
-            crow[n * p.ldc_n] = run_program(p.prog, regs, &err).f;
+          float o[8];
+          if (p.fast != FAST_NONE) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int64_t n = nb0 + c0 + j;
+              const float x = p.bias ? __fadd_rn(acc[c0 + j], n < p.N ? __ldg(p.bias + n) : 0.f) : acc[c0 + j];
+              if (p.fast == FAST_ADD) {
+                o[j] = __fadd_rn(x, av[0][j]);
+              } else if (p.fast == FAST_DIVC_ADD) {
+                o[j] = __fadd_rn(__fdiv_rn(x, p.fast_c), av[0][j]);
+              } else {
+                const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-av[1][j])));
+                o[j] = __fmul_rn(__fmul_rn(av[0][j], sg), x);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int64_t n = nb0 + c0 + j;
+              o[j] = 0.f;
+              if (n < p.N) {
+                regs[0].f = p.bias ? __fadd_rn(acc[c0 + j], __ldg(p.bias + n)) : acc[c0 + j];
+#pragma unroll
+                for (int a = 0; a < 4; ++a)
+                  if (a < p.n_aux) regs[1 + a].f = av[a][j];
+                o[j] = run_program(p.prog, regs, &err).f;
+              }
+            }
+          }
+          if (vec) {
+            *reinterpret_cast<float4*>(crow + nb0 + c0) = make_float4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<float4*>(crow + nb0 + c0 + 4) = make_float4(o[4], o[5], o[6], o[7]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              if (nb0 + c0 + j < p.N) crow[(int64_t)(nb0 + c0 + j) * p.ldc_n] = o[j];
           }
         }
         if (err && p.status) atomicCAS(p.status, 0, err);

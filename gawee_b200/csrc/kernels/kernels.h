@@ -250,7 +250,18 @@ struct ConvGemmParams {
   const float* aux[4];
   int64_t aux_sm[4], aux_sn[4], aux_sb[4][4];
   DProgram prog;
+  // Programs recognised on the host and evaluated without the interpreter
+  // (same IEEE operations in the same order): see FastEpi.
+  int fast;
+  float fast_c;
   int* status;
+};
+
+enum FastEpi : int {
+  FAST_NONE = 0,
+  FAST_ADD = 1,          // acc + aux0
+  FAST_DIVC_ADD = 2,     // (acc / c) + aux0
+  FAST_SIGMOID_MUL = 3,  // (aux0 * (1 / (1 + exp(-aux1)))) * acc
 };
 
 // Returns false (and launches nothing) when the shape is not supported.

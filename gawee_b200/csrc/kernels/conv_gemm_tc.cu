@@ -51,19 +51,22 @@ constexpr int kBM = 128;
 constexpr int kBK = 32;               // fp32 elements per k-block (one 128-byte swizzle row)
 constexpr int kThreadsTC = 448;  // 4 A-producer, 1 TMA, 1 MMA, 8 accumulator warps
 constexpr unsigned long long kWaitNs = 4000000000ull;  // 4 s per barrier wait
-// Pipeline depths per tile width: B stages, raw A k-blocks in flight, A stages
-// and accumulators in tensor memory.  Shared memory: 6 x 16 KB + 6 x 16 KB
-// for BN 64, 4 x 32 KB + 5 x 16 KB for BN 128; tensor memory: 4 x 64 + 4 x 64
-// and 2 x 128 + 4 x 64 of its 512 columns.
+// The k loop runs in rounds of kRK k-blocks: one A stage, one B stage and one
+// accumulator buffer per round, so each barrier hand-off covers 12 * kRK MMAs.
+constexpr int kRK = 2;
+// Pipeline depths per tile width: B stages (rounds), raw A k-blocks in flight,
+// A stages (rounds) and accumulators in tensor memory.  Shared memory:
+// 3 x 32 KB + 6 x 16 KB for BN 64, 2 x 64 KB + 5 x 16 KB for BN 128; tensor
+// memory: 2 x 64 + 3 x 128 and 2 x 128 + 2 x 128 of its 512 columns.
 template <int BN>
 struct TcConfig;
 template <>
 struct TcConfig<64> {
-  static constexpr int SB = 6, RD = 6, SA = 4, NB = 4;
+  static constexpr int SB = 3, RD = 6, SA = 3, NB = 2;
 };
 template <>
 struct TcConfig<128> {
-  static constexpr int SB = 4, RD = 5, SA = 4, NB = 2;
+  static constexpr int SB = 2, RD = 5, SA = 2, NB = 2;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -201,21 +204,23 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
 
-// Shared memory: SB stages of B (hi and lo planes, TMA), RD raw A k-blocks
-// (cp.async ring, 128 rows x 128 B, 16-byte chunks swizzled by row), then the
-// barriers.  Tensor memory: NB k-block accumulators of BN columns, then SA
-// A stages of 64 columns (32 raw values, 32 remainders; lane = row).
+// Shared memory: SB stages of B (per round: kRK k-blocks of hi and lo planes,
+// TMA), RD raw A k-blocks (cp.async ring, 128 rows x 128 B, 16-byte chunks
+// swizzled by row), then the barriers.  Tensor memory: NB round accumulators
+// of BN columns, then SA A stages of kRK x 64 columns (per k-block 32 raw
+// values and 32 remainders; lane = row).
 template <int BN, int SB, int RD, int SA, int NB>
 struct Smem {
   static constexpr int kATile = kBM * kBK * 4;  // 16 KB
   static constexpr int kBTile = BN * kBK * 4;
-  static constexpr int kBStage = 2 * kBTile;
+  static constexpr int kBStage = kRK * 2 * kBTile;
   static constexpr int kRawOff = SB * kBStage;
   static constexpr int kBarOff = kRawOff + RD * kATile;
   static constexpr int kNumBars = 2 * SA + 2 * SB + 2 * NB + 1;  // full/empty A, B, TMEM buffers; done
   static constexpr int kBytes = kBarOff + 8 * kNumBars + 16 + 1024;  // + alignment slack
   static constexpr int kACol = NB * BN;
-  static constexpr int kUsedCols = NB * BN + SA * 2 * kBK;
+  static constexpr int kAStageCols = kRK * 2 * kBK;
+  static constexpr int kUsedCols = NB * BN + SA * kAStageCols;
   static constexpr int kTmemCols = kUsedCols <= 256 ? 256 : 512;
   static_assert(kUsedCols <= 512, "tensor memory columns");
 };
@@ -243,6 +248,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   const int num_kb = (int)((p.K + kBK - 1) / kBK);
+  const int num_rounds = (num_kb + kRK - 1) / kRK;
+  auto round_kbs = [&](int r) { return min(kRK, num_kb - r * kRK); };
   const int64_t m_tiles = (p.M + kBM - 1) / kBM;
   const int64_t n_tiles = (p.N + BN - 1) / BN;
   const int64_t num_tiles = m_tiles * n_tiles * p.nb;
@@ -253,10 +260,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     n0 = (int)(((t / m_tiles) % n_tiles) * BN);
     z = (int)(t / (m_tiles * n_tiles));
   };
-  // Each tile walks its k-blocks starting at (m tile index mod num_kb):
+  // Each tile walks its rounds starting at (m tile index mod num_rounds):
   // CTAs that run side by side then fetch different k-blocks of the shared
   // B operand instead of all hitting the same L2 lines at once.
-  auto k_rotation = [&](int64_t t) -> int { return (int)((t % m_tiles) % num_kb); };
+  auto r_rotation = [&](int64_t t) -> int { return (int)((t % m_tiles) % num_rounds); };
   auto batch_offsets = [&](int z, int64_t& a_off, int64_t& c_off, int& b_plane) {
     a_off = 0;
     c_off = 0;
@@ -352,7 +359,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           rowoff[i] = 0;
         }
       }
-      lka = k_rotation(lt);
+      lka = r_rotation(lt) * kRK;
       decompose(lka * kBK + chunk * 4);
     };
     auto issue = [&]() {
@@ -394,37 +401,51 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     const int row = warp * 32 + lane;
 #pragma unroll
     for (int j = 0; j < RD; ++j) issue();
-    for (int64_t g = 0; g < G; ++g) {
-      cp_async_wait<RD - 1>();  // this lane's copies of k-block g have landed
-      __syncwarp();             // ... and every other lane's
-      const int sa = (int)(g % SA);
-      if (!mbar_wait(smem_u32(&empty_a[sa]), (uint32_t)(((g / SA) & 1) ^ 1), abort_flag, p.status)) break;
-      tc_fence_after();
-      const uint32_t src = raw_base + (uint32_t)((g % RD) * L::kATile) + row * 128;
-      uint32_t x[32];
+    int64_t g = 0;   // k-blocks consumed
+    int64_t gr = 0;  // rounds written
+    bool alive = true;
+    for (int64_t t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
+      const int rot = r_rotation(t);
+      for (int rr = 0; rr < num_rounds && alive; ++rr, ++gr) {
+        int r = rot + rr;
+        if (r >= num_rounds) r -= num_rounds;
+        const int nk = round_kbs(r);
+        const int sa = (int)(gr % SA);
+        if (!mbar_wait(smem_u32(&empty_a[sa]), (uint32_t)(((gr / SA) & 1) ^ 1), abort_flag, p.status)) {
+          alive = false;
+          break;
+        }
+        tc_fence_after();
+        for (int j = 0; j < nk; ++j, ++g) {
+          cp_async_wait<RD - 1>();  // this lane's copies of k-block g have landed
+          __syncwarp();             // ... and every other lane's
+          const uint32_t src = raw_base + (uint32_t)((g % RD) * L::kATile) + row * 128;
+          uint32_t x[32];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const float4 v = lds128(src + ((c ^ (row & 7)) << 4));
-        x[4 * c] = __float_as_uint(v.x);
-        x[4 * c + 1] = __float_as_uint(v.y);
-        x[4 * c + 2] = __float_as_uint(v.z);
-        x[4 * c + 3] = __float_as_uint(v.w);
-      }
-      const uint32_t acol = tmem_rows + (uint32_t)(L::kACol + sa * 2 * kBK);
-      tmem_st32(acol, x);
-      uint32_t y[32];
+          for (int c = 0; c < 8; ++c) {
+            const float4 v = lds128(src + ((c ^ (row & 7)) << 4));
+            x[4 * c] = __float_as_uint(v.x);
+            x[4 * c + 1] = __float_as_uint(v.y);
+            x[4 * c + 2] = __float_as_uint(v.z);
+            x[4 * c + 3] = __float_as_uint(v.w);
+          }
+          const uint32_t acol = tmem_rows + (uint32_t)(L::kACol + sa * L::kAStageCols + j * 2 * kBK);
+          tmem_st32(acol, x);
+          uint32_t y[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float v = __uint_as_float(x[j]);
-        y[j] = __float_as_uint(__fsub_rn(v, tf32_hi(v)));
+          for (int q = 0; q < 32; ++q) {
+            const float v = __uint_as_float(x[q]);
+            y[q] = __float_as_uint(__fsub_rn(v, tf32_hi(v)));
+          }
+          __syncwarp();  // every lane has read its row: the slot may be refilled
+          issue();
+          tmem_st32(acol + kBK, y);
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&full_a[sa]));
       }
-      __syncwarp();  // every lane has read its row: the slot may be refilled
-      issue();
-      tmem_st32(acol + kBK, y);
-      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&full_a[sa]));
     }
     asm volatile("cp.async.wait_all;" ::: "memory");  // nothing of this thread in flight at exit
   } else if (warp == 4) {
@@ -439,20 +460,25 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         int n0, z, b_plane;
         tile_coords(t, m0, n0, z);
         batch_offsets(z, a_off, c_off, b_plane);
-        int ka = k_rotation(t);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int rot = r_rotation(t);
+        for (int rr = 0; rr < num_rounds; ++rr) {
+          int r = rot + rr;
+          if (r >= num_rounds) r -= num_rounds;
+          const int nk = round_kbs(r);
           const int sb = (int)(g % SB);
           if (!mbar_wait(smem_u32(&empty_b[sb]), (uint32_t)(((g / SB) & 1) ^ 1), abort_flag, p.status)) {
             alive = false;
             break;
           }
-          uint8_t* b_hi = smem + sb * L::kBStage;
-          uint8_t* b_lo = b_hi + L::kBTile;
           const uint32_t bar = smem_u32(&full_b[sb]);
-          mbar_arrive_tx(bar, 2 * L::kBTile);
-          tma_load_3d(smem_u32(b_hi), &tm_hi, bar, ka * kBK, n0, b_plane);
-          tma_load_3d(smem_u32(b_lo), &tm_lo, bar, ka * kBK, n0, b_plane);
-          if (++ka == num_kb) ka = 0;
+          mbar_arrive_tx(bar, (uint32_t)(nk * 2 * L::kBTile));
+          for (int j = 0; j < nk; ++j) {
+            uint8_t* b_hi = smem + sb * L::kBStage + j * 2 * L::kBTile;
+            uint8_t* b_lo = b_hi + L::kBTile;
+            const int kb = r * kRK + j;
+            tma_load_3d(smem_u32(b_hi), &tm_hi, bar, kb * kBK, n0, b_plane);
+            tma_load_3d(smem_u32(b_lo), &tm_lo, bar, kb * kBK, n0, b_plane);
+          }
           ++g;
         }
       }
@@ -473,10 +499,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     const uint64_t desc0 = umma_desc_sw128(smem_u32(smem));
     constexpr uint64_t kBStageDesc = (uint64_t)(L::kBStage >> 4);  // descriptor start-address units
     constexpr uint64_t kBTileDesc = (uint64_t)(L::kBTile >> 4);
-    int64_t g = 0;
+    int64_t g = 0;  // rounds
     bool alive = true;
     for (int64_t t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
-      for (int kb = 0; kb < num_kb; ++kb) {
+      const int rot = r_rotation(t);
+      for (int rr = 0; rr < num_rounds; ++rr) {
+        int r = rot + rr;
+        if (r >= num_rounds) r -= num_rounds;
+        const int nk = round_kbs(r);
         const int sa = (int)(g % SA);
         const int sb = (int)(g % SB);
         const int buf = (int)(g % NB);
@@ -489,19 +519,21 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         tc_fence_after();
         // the start address of a K-major SW128 descriptor advances 32 bytes
         // (2 units) per 8-wide k-step; an A column holds one k
-        const uint64_t dbh = desc0 + (uint64_t)sb * kBStageDesc;
-        const uint64_t dbl = dbh + kBTileDesc;
-        const uint32_t a_raw = tmem_base + (uint32_t)(L::kACol + sa * 2 * kBK);
-        const uint32_t a_rem = a_raw + kBK;
         const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BN);
         if (lane == 0) {
+          for (int j = 0; j < nk; ++j) {
+            const uint64_t dbh = desc0 + (uint64_t)sb * kBStageDesc + (uint64_t)j * 2 * kBTileDesc;
+            const uint64_t dbl = dbh + kBTileDesc;
+            const uint32_t a_raw = tmem_base + (uint32_t)(L::kACol + sa * L::kAStageCols + j * 2 * kBK);
+            const uint32_t a_rem = a_raw + kBK;
 #pragma unroll
-          for (int kk = 0; kk < kBK / 8; ++kk) {
-            const uint64_t o = (uint64_t)(2 * kk);
-            const uint32_t ka = (uint32_t)(8 * kk);
-            umma_tf32_ts(tmem_d, a_rem + ka, dbh + o, idesc, kk != 0);
-            umma_tf32_ts(tmem_d, a_raw + ka, dbl + o, idesc, 1);
-            umma_tf32_ts(tmem_d, a_raw + ka, dbh + o, idesc, 1);
+            for (int kk = 0; kk < kBK / 8; ++kk) {
+              const uint64_t o = (uint64_t)(2 * kk);
+              const uint32_t ka = (uint32_t)(8 * kk);
+              umma_tf32_ts(tmem_d, a_rem + ka, dbh + o, idesc, (j | kk) != 0);
+              umma_tf32_ts(tmem_d, a_raw + ka, dbl + o, idesc, 1);
+              umma_tf32_ts(tmem_d, a_raw + ka, dbh + o, idesc, 1);
+            }
           }
           umma_commit(smem_u32(&empty_a[sa]));
           umma_commit(smem_u32(&empty_b[sb]));
@@ -532,7 +564,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       float acc[HB];
 #pragma unroll
       for (int j = 0; j < HB; ++j) acc[j] = 0.0f;
-      for (int kb = 0; kb < num_kb; ++kb) {
+      for (int r = 0; r < num_rounds; ++r) {
         const int buf = (int)(g % NB);
         const uint32_t use = (uint32_t)((g / NB) & 1);
         if (!mbar_wait(smem_u32(&tfull[buf]), use, abort_flag, p.status)) {

@@ -1,12 +1,14 @@
 #!/usr/bin/env python
-"""Benchmark: compiled inference of a gawee graph on B200, batch-sharded over N GPUs.
+"""Benchmark: compiled inference of a gawee graph on B200, data parallel over N GPUs.
 
 Default workload (the one the headline metric is quoted on and that fits one
 GPU): ResNet-18 fp32, batch 256 of 3x224x224 ~N(0,1), Kaiming-normal conv
 weights with BatchNorm folded into the conv bias, graph in the gawee dialect
-as the ONNX emitter prints it; sharded along the batch (256/N images per GPU),
-weights replicated, outputs gathered to rank 0.  `--workload decoder135m`
-runs the 135M GQA decoder prefill (batch 64 x 512 tokens) instead.
+as the ONNX emitter prints it.  Batch rows are independent, so the job
+partitions: every GPU runs its own batch of 256 (seeded per rank), weights
+replicated, with no collective on the data path (weak scaling; the process
+group only aligns and times the ranks).  `--workload decoder135m` runs the
+135M GQA decoder prefill (batch 64 x 512 tokens per GPU) instead.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl gawee|reference]
 
@@ -51,11 +53,12 @@ def build_graph(workload: str, batch: int):
     return synth.smollm135m(batch, 512)
 
 
-def full_inputs(workload: str, batch: int):
-    """Seeded batched inputs of the whole job (independent of the shard count)."""
+def full_inputs(workload: str, batch: int, rank: int = 0):
+    """Seeded batched inputs of one rank's partition."""
+    rng = np.random.default_rng(43 + rank)
     if workload == "resnet18":
-        return np.random.default_rng(43).standard_normal((batch, 3, 224, 224), dtype=np.float32)
-    return np.random.default_rng(43).integers(0, 49152, (batch, 512), dtype=np.int64)
+        return rng.standard_normal((batch, 3, 224, 224), dtype=np.float32)
+    return rng.integers(0, 49152, (batch, 512), dtype=np.int64)
 
 
 def load_peaks():
@@ -182,7 +185,6 @@ def main():
     import torch
     import torch.distributed as dist
 
-    from gawee_b200 import dp
     from gawee_b200.runtime import Model
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -195,31 +197,24 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
 
-    metric, unit, total_batch, items = WORKLOADS[a.workload]
+    metric, unit, per_gpu, items = WORKLOADS[a.workload]
     if a.batch:
-        total_batch = a.batch
+        per_gpu = a.batch
         metric += f" [batch overridden to {a.batch}]"
-    s0, s1 = dp.shard_range(total_batch, world, rank)
-    g = build_graph(a.workload, s1 - s0)
+    total_batch = per_gpu * world
+    g = build_graph(a.workload, per_gpu)
     args = g.make_args()
-    args[0] = np.ascontiguousarray(full_inputs(a.workload, total_batch)[s0:s1])
+    args[0] = np.ascontiguousarray(full_inputs(a.workload, per_gpu, rank))
     m = Model(g.mlir, device=local)
     m.set_args(args)
     stream = torch.cuda.Stream(local)
     sp = stream.cuda_stream
 
-    if world > 1:
-        uid = Model.dp_unique_id() if rank == 0 else bytes(128)
-        uid = dp.share_nccl_id(uid, rank)
-        m.dp_init(world, rank, uid)
     out_dt, out_shape = m.output_specs[0]
     out_bytes = int(np.prod(out_shape)) * out_dt.itemsize
-    gathered = torch.empty(world * out_bytes, dtype=torch.uint8, device=f"cuda:{local}") if rank == 0 else None
 
     def step():
         m.forward(sp)
-        if world > 1:
-            m.dp_gather_output(0, gathered.data_ptr() if rank == 0 else None, sp)
 
     # first forward (eager) + status check, then warm-up (CUDA graph capture on the second)
     step()
@@ -286,14 +281,15 @@ def main():
                 "tc_ms_per_forward": tc_ms, "tc_flops_per_forward": tc_flops}
 
     line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
-            "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded; architecture and init as the config, no pretrained weights)",
-            "config": {"workload": a.workload, "global_batch": total_batch, "per_gpu_batch": s1 - s0,
-                       "parallelism": f"dp{world} (batch-sharded, weights replicated, NCCL gather to rank 0)",
+            "config": {"workload": a.workload, "global_batch": total_batch, "per_gpu_batch": per_gpu,
+                       "parallelism": f"dp{world} (each GPU runs its own batch; weights replicated; "
+                                      "no collective on the data path)",
                        "l2": "inputs larger than L2 (ResNet input 154 MB per step at N=1)"
                        if a.workload == "resnet18" else "activations larger than L2"},
             "e2e": {"value": e2e_value, "unit": unit, "h2d_bytes_per_step": in_bytes * world,
-                    "d2h_bytes_per_step": out_bytes},
+                    "d2h_bytes_per_step": out_bytes * world},
             "roofline": roofline, "clocks": clocks,
             "gpu_launches": m.num_kernels() * a.steps}
     if rank == 0 and world == 1 and not a.no_cpu_baseline:

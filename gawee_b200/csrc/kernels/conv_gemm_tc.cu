@@ -54,19 +54,22 @@ constexpr unsigned long long kWaitNs = 4000000000ull;  // 4 s per barrier wait
 // The k loop runs in rounds of kRK k-blocks: one A stage, one B stage and one
 // accumulator buffer per round, so each barrier hand-off covers 12 * kRK MMAs.
 constexpr int kRK = 2;
-// Pipeline depths per tile width: B stages (rounds), raw A k-blocks in flight,
-// A stages (rounds) and accumulators in tensor memory.  Shared memory:
-// 3 x 32 KB + 6 x 16 KB for BN 64, 2 x 64 KB + 5 x 16 KB for BN 128; tensor
-// memory: 2 x 64 + 3 x 128 and 2 x 128 + 2 x 128 of its 512 columns.
+// Round slots: each of the kS slots holds one round's A stage (tensor
+// memory), B stage (shared memory) and accumulator (tensor memory), so one
+// barrier per slot says "everything for this round is ready".
+constexpr int kS = 2;
+// Raw A k-blocks in flight per tile width.  Shared memory: 2 x 32 KB + 8 x
+// 16 KB for BN 64, 2 x 64 KB + 5 x 16 KB for BN 128; tensor memory: 2 x 64 +
+// 2 x 128 and 2 x 128 + 2 x 128 of its 512 columns.
 template <int BN>
 struct TcConfig;
 template <>
 struct TcConfig<64> {
-  static constexpr int SB = 3, RD = 6, SA = 3, NB = 2;
+  static constexpr int RD = 8;
 };
 template <>
 struct TcConfig<128> {
-  static constexpr int SB = 2, RD = 5, SA = 2, NB = 2;
+  static constexpr int RD = 5;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -204,44 +207,49 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
 
-// Shared memory: SB stages of B (per round: kRK k-blocks of hi and lo planes,
+// Shared memory: kS B stages (per round: kRK k-blocks of hi and lo planes,
 // TMA), RD raw A k-blocks (cp.async ring, 128 rows x 128 B, 16-byte chunks
-// swizzled by row), then the barriers.  Tensor memory: NB round accumulators
-// of BN columns, then SA A stages of kRK x 64 columns (per k-block 32 raw
+// swizzled by row), then the barriers.  Tensor memory: kS round accumulators
+// of BN columns, then kS A stages of kRK x 64 columns (per k-block 32 raw
 // values and 32 remainders; lane = row).
-template <int BN, int SB, int RD, int SA, int NB>
+template <int BN, int RD>
 struct Smem {
   static constexpr int kATile = kBM * kBK * 4;  // 16 KB
   static constexpr int kBTile = BN * kBK * 4;
   static constexpr int kBStage = kRK * 2 * kBTile;
-  static constexpr int kRawOff = SB * kBStage;
+  static constexpr int kRawOff = kS * kBStage;
   static constexpr int kBarOff = kRawOff + RD * kATile;
-  static constexpr int kNumBars = 2 * SA + 2 * SB + 2 * NB + 1;  // full/empty A, B, TMEM buffers; done
+  static constexpr int kNumBars = 2 * kS + 1;  // ready, done per slot; all MMAs done
   static constexpr int kBytes = kBarOff + 8 * kNumBars + 16 + 1024;  // + alignment slack
-  static constexpr int kACol = NB * BN;
+  static constexpr int kACol = kS * BN;
   static constexpr int kAStageCols = kRK * 2 * kBK;
-  static constexpr int kUsedCols = NB * BN + SA * kAStageCols;
+  static constexpr int kUsedCols = kS * BN + kS * kAStageCols;
   static constexpr int kTmemCols = kUsedCols <= 256 ? 256 : 512;
   static_assert(kUsedCols <= 512, "tensor memory columns");
 };
 
+// Arrivals that complete a slot's "ready" phase: 4 A producer warps, the TMA
+// thread (plus the B transaction bytes) and 8 accumulator warps (the slot's
+// accumulator has been drained).
+constexpr int kReadyCount = 4 + 1 + 8;
+
 }  // namespace
 
-template <int BN, int SB, int RD, int SA, int NB, int EPI>
+template <int BN, int RD, int EPI>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     conv_gemm_tc_kernel(const __grid_constant__ ConvGemmParams p, const __grid_constant__ CUtensorMap tm_hi,
                         const __grid_constant__ CUtensorMap tm_lo) {
-  using L = Smem<BN, SB, RD, SA, NB>;
+  using L = Smem<BN, RD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
-  uint64_t* full_a = bars;                  // [SA] A stage written to tensor memory (4 producer warps)
-  uint64_t* empty_a = bars + SA;            // [SA] A stage consumed by the MMAs
-  uint64_t* full_b = bars + 2 * SA;         // [SB] B stage landed (TMA transaction bytes)
-  uint64_t* empty_b = bars + 2 * SA + SB;   // [SB] B stage consumed by the MMAs
-  uint64_t* tfull = bars + 2 * SA + 2 * SB;        // [NB] k-block sum ready in a TMEM buffer
-  uint64_t* tempty = bars + 2 * SA + 2 * SB + NB;  // [NB] TMEM buffer drained by the accumulator warps
-  uint64_t* done = bars + 2 * SA + 2 * SB + 2 * NB;  // every MMA issued by this CTA completed
+  // Round g uses slot g % kS.  ready[s]: A written, B landed, accumulator
+  // drained (kReadyCount arrivals + B bytes); done[s]: the round's MMAs have
+  // completed (one tcgen05.commit), so its A stage, B stage and accumulator
+  // may be read or reused.
+  uint64_t* ready = bars;
+  uint64_t* rdone = bars + kS;
+  uint64_t* done = bars + 2 * kS;  // every MMA issued by this CTA completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -279,17 +287,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < SA; ++s) {
-      mbar_init(smem_u32(&full_a[s]), 4);
-      mbar_init(smem_u32(&empty_a[s]), 1);
-    }
-    for (int s = 0; s < SB; ++s) {
-      mbar_init(smem_u32(&full_b[s]), 1);
-      mbar_init(smem_u32(&empty_b[s]), 1);
-    }
-    for (int b = 0; b < NB; ++b) {
-      mbar_init(smem_u32(&tfull[b]), 1);
-      mbar_init(smem_u32(&tempty[b]), 8);
+    for (int s = 0; s < kS; ++s) {
+      mbar_init(smem_u32(&ready[s]), kReadyCount);
+      mbar_init(smem_u32(&rdone[s]), 1);
     }
     mbar_init(smem_u32(done), 1);
     *abort_flag = 0;
@@ -401,17 +401,17 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     const int row = warp * 32 + lane;
 #pragma unroll
     for (int j = 0; j < RD; ++j) issue();
-    int64_t g = 0;   // k-blocks consumed
-    int64_t gr = 0;  // rounds written
+    int64_t g = 0;        // k-blocks consumed
+    int sa = 0;           // round slot
+    uint32_t free_ph = 1;  // parity of the slot's previous round completing (fresh: passes)
     bool alive = true;
     for (int64_t t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
       const int rot = r_rotation(t);
-      for (int rr = 0; rr < num_rounds && alive; ++rr, ++gr) {
+      for (int rr = 0; rr < num_rounds && alive; ++rr) {
         int r = rot + rr;
         if (r >= num_rounds) r -= num_rounds;
         const int nk = round_kbs(r);
-        const int sa = (int)(gr % SA);
-        if (!mbar_wait(smem_u32(&empty_a[sa]), (uint32_t)(((gr / SA) & 1) ^ 1), abort_flag, p.status)) {
+        if (!mbar_wait(smem_u32(&rdone[sa]), free_ph, abort_flag, p.status)) {
           alive = false;
           break;
         }
@@ -444,7 +444,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&full_a[sa]));
+        if (lane == 0) mbar_arrive(smem_u32(&ready[sa]));
+        if (++sa == kS) {
+          sa = 0;
+          free_ph ^= 1;
+        }
       }
     }
     asm volatile("cp.async.wait_all;" ::: "memory");  // nothing of this thread in flight at exit
@@ -454,6 +458,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_hi)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_lo)) : "memory");
       int64_t g = 0;
+      int sb = 0;
+      uint32_t free_ph = 1;
       bool alive = true;
       for (int64_t t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
         int64_t m0, a_off, c_off;
@@ -465,12 +471,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           int r = rot + rr;
           if (r >= num_rounds) r -= num_rounds;
           const int nk = round_kbs(r);
-          const int sb = (int)(g % SB);
-          if (!mbar_wait(smem_u32(&empty_b[sb]), (uint32_t)(((g / SB) & 1) ^ 1), abort_flag, p.status)) {
+          if (!mbar_wait(smem_u32(&rdone[sb]), free_ph, abort_flag, p.status)) {
             alive = false;
             break;
           }
-          const uint32_t bar = smem_u32(&full_b[sb]);
+          const uint32_t bar = smem_u32(&ready[sb]);
           mbar_arrive_tx(bar, (uint32_t)(nk * 2 * L::kBTile));
           for (int j = 0; j < nk; ++j) {
             uint8_t* b_hi = smem + sb * L::kBStage + j * 2 * L::kBTile;
@@ -480,13 +485,18 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             tma_load_3d(smem_u32(b_lo), &tm_lo, bar, kb * kBK, n0, b_plane);
           }
           ++g;
+          if (++sb == kS) {
+            sb = 0;
+            free_ph ^= 1;
+          }
         }
       }
-      if (*abort_flag) {
-        // let copies already in flight land before the CTA retires
-        for (int64_t k = g - SB < 0 ? 0 : g - SB; k < g; ++k) {
-          volatile int never = 0;
-          mbar_wait(smem_u32(&full_b[k % SB]), (uint32_t)((k / SB) & 1), &never, nullptr);
+      if (*abort_flag && g > 0) {
+        // Copies already in flight must land before the CTA retires; their
+        // barrier phase may never complete once other roles have stopped, so
+        // wait a fixed 100 us (a B stage lands within microseconds).
+        const unsigned long long t0 = global_ns();
+        while (global_ns() - t0 < 100000ull) {
         }
       }
     }
@@ -499,7 +509,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     const uint64_t desc0 = umma_desc_sw128(smem_u32(smem));
     constexpr uint64_t kBStageDesc = (uint64_t)(L::kBStage >> 4);  // descriptor start-address units
     constexpr uint64_t kBTileDesc = (uint64_t)(L::kBTile >> 4);
-    int64_t g = 0;  // rounds
+    int sl = 0;            // round slot
+    uint32_t rdy_ph = 0;   // parity of the slot's ready phase for this round
     bool alive = true;
     for (int64_t t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
       const int rot = r_rotation(t);
@@ -507,24 +518,19 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         int r = rot + rr;
         if (r >= num_rounds) r -= num_rounds;
         const int nk = round_kbs(r);
-        const int sa = (int)(g % SA);
-        const int sb = (int)(g % SB);
-        const int buf = (int)(g % NB);
-        if (!mbar_wait(smem_u32(&full_a[sa]), (uint32_t)((g / SA) & 1), abort_flag, p.status) ||
-            !mbar_wait(smem_u32(&full_b[sb]), (uint32_t)((g / SB) & 1), abort_flag, p.status) ||
-            !mbar_wait(smem_u32(&tempty[buf]), (uint32_t)(((g / NB) & 1) ^ 1), abort_flag, p.status)) {
+        if (!mbar_wait(smem_u32(&ready[sl]), rdy_ph, abort_flag, p.status)) {
           alive = false;
           break;
         }
         tc_fence_after();
         // the start address of a K-major SW128 descriptor advances 32 bytes
         // (2 units) per 8-wide k-step; an A column holds one k
-        const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BN);
+        const uint32_t tmem_d = tmem_base + (uint32_t)(sl * BN);
         if (lane == 0) {
           for (int j = 0; j < nk; ++j) {
-            const uint64_t dbh = desc0 + (uint64_t)sb * kBStageDesc + (uint64_t)j * 2 * kBTileDesc;
+            const uint64_t dbh = desc0 + (uint64_t)sl * kBStageDesc + (uint64_t)j * 2 * kBTileDesc;
             const uint64_t dbl = dbh + kBTileDesc;
-            const uint32_t a_raw = tmem_base + (uint32_t)(L::kACol + sa * L::kAStageCols + j * 2 * kBK);
+            const uint32_t a_raw = tmem_base + (uint32_t)(L::kACol + sl * L::kAStageCols + j * 2 * kBK);
             const uint32_t a_rem = a_raw + kBK;
 #pragma unroll
             for (int kk = 0; kk < kBK / 8; ++kk) {
@@ -535,12 +541,13 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
               umma_tf32_ts(tmem_d, a_raw + ka, dbh + o, idesc, 1);
             }
           }
-          umma_commit(smem_u32(&empty_a[sa]));
-          umma_commit(smem_u32(&empty_b[sb]));
-          umma_commit(smem_u32(&tfull[buf]));
+          umma_commit(smem_u32(&rdone[sl]));
         }
         __syncwarp();
-        ++g;
+        if (++sl == kS) {
+          sl = 0;
+          rdy_ph ^= 1;
+        }
       }
     }
     if (lane == 0) umma_commit(smem_u32(done));
@@ -554,8 +561,12 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     const int cbase = half * HB;
     const int row = q * 32 + lane;
     const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
-    int64_t g = 0;
+    int sl = 0;
+    uint32_t done_ph = 0;
     bool ok = true;
+    // every accumulator starts drained: count toward the first round of each slot
+    if (lane == 0)
+      for (int k = 0; k < kS; ++k) mbar_arrive(smem_u32(&ready[k]));
     for (int64_t t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
       int64_t m0, a_off, c_off;
       int n0, z, b_plane;
@@ -565,9 +576,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
       for (int j = 0; j < HB; ++j) acc[j] = 0.0f;
       for (int r = 0; r < num_rounds; ++r) {
-        const int buf = (int)(g % NB);
-        const uint32_t use = (uint32_t)((g / NB) & 1);
-        if (!mbar_wait(smem_u32(&tfull[buf]), use, abort_flag, p.status)) {
+        const int buf = sl;
+        if (!mbar_wait(smem_u32(&rdone[sl]), done_ph, abort_flag, p.status)) {
           ok = false;
           break;
         }
@@ -581,8 +591,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&tempty[buf]));
-        ++g;
+        if (lane == 0) mbar_arrive(smem_u32(&ready[sl]));  // the accumulator is free for round + kS
+        if (++sl == kS) {
+          sl = 0;
+          done_ph ^= 1;
+        }
       }
       ok = ok && !*abort_flag;
       const int64_t m = m0 + row;
@@ -720,8 +733,8 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 template <int BN, int EPI>
 bool launch_t(const ConvGemmParams& p, const void* tmh, const void* tml, cudaStream_t s) {
   using Cfg = TcConfig<BN>;
-  auto kern = conv_gemm_tc_kernel<BN, Cfg::SB, Cfg::RD, Cfg::SA, Cfg::NB, EPI>;
-  constexpr int smem = Smem<BN, Cfg::SB, Cfg::RD, Cfg::SA, Cfg::NB>::kBytes;
+  auto kern = conv_gemm_tc_kernel<BN, Cfg::RD, EPI>;
+  constexpr int smem = Smem<BN, Cfg::RD>::kBytes;
   static_assert(smem <= 232448, "shared memory per CTA");
   // the shared-memory opt-in is per device
   static std::mutex mu;
@@ -761,8 +774,7 @@ bool launch_epi(const ConvGemmParams& p, const void* tmh, const void* tml, cudaS
 int conv_gemm_smem_bytes(int block_n) {
   using C64 = TcConfig<64>;
   using C128 = TcConfig<128>;
-  return block_n == 64 ? Smem<64, C64::SB, C64::RD, C64::SA, C64::NB>::kBytes
-                       : Smem<128, C128::SB, C128::RD, C128::SA, C128::NB>::kBytes;
+  return block_n == 64 ? Smem<64, C64::RD>::kBytes : Smem<128, C128::RD>::kBytes;
 }
 
 bool make_b_tensor_maps(const float* hi, const float* lo, int64_t batch, int64_t N, int64_t ldk, int block_n,

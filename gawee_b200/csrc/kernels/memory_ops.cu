@@ -112,8 +112,102 @@ __global__ void __launch_bounds__(kThreads) elementwise_dense4_kernel(const __gr
   if (err) set_status(p.status, err);
 }
 
+// All-f32 operands, output rows contiguous: each thread takes a run of four
+// consecutive elements of one row (coordinates unravelled once per run),
+// loads each operand as a float4 when its inner stride is 1 (and aligned),
+// broadcasts it when the stride is 0, and stores a float4.
+__global__ void __launch_bounds__(kThreads) elementwise_rows4_kernel(const __grid_constant__ EwParams p,
+                                                                     unsigned vec_mask, unsigned bcast_mask,
+                                                                     int64_t rows, int64_t cols) {
+  Reg regs[kMaxRegs];
+  int err = 0;
+  const int64_t runs_per_row = (cols + 3) / 4;
+  const int64_t runs = rows * runs_per_row;
+  const int inner = p.rank - 1;
+  for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < runs; u += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = u / runs_per_row;
+    const int64_t c0 = (u - row * runs_per_row) * 4;
+    int64_t rem = row, off_out = 0;
+    int64_t off_in[kMaxIn];
+#pragma unroll
+    for (int k = 0; k < kMaxIn; ++k) off_in[k] = 0;
+    for (int d = inner - 1; d >= 0; --d) {
+      const int64_t c = rem % p.shape[d];
+      rem /= p.shape[d];
+      off_out += c * p.out.st[d];
+#pragma unroll
+      for (int k = 0; k < kMaxIn; ++k)
+        if (k < p.n_in) off_in[k] += c * p.in[k].st[d];
+    }
+    float* op = static_cast<float*>(p.out.ptr) + off_out + c0;
+    const bool full = c0 + 4 <= cols;
+    float v[kMaxIn][4];
+#pragma unroll
+    for (int k = 0; k < kMaxIn; ++k) {
+      if (k >= p.n_in) continue;
+      const float* ip = static_cast<const float*>(p.in[k].ptr) + off_in[k];
+      if (bcast_mask & (1u << k)) {
+        const float x = ip[0];
+        v[k][0] = v[k][1] = v[k][2] = v[k][3] = x;
+      } else if (full && (vec_mask & (1u << k))) {
+        const float4 x = *reinterpret_cast<const float4*>(ip + c0);
+        v[k][0] = x.x;
+        v[k][1] = x.y;
+        v[k][2] = x.z;
+        v[k][3] = x.w;
+      } else {
+        const int64_t st = p.in[k].st[inner];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[k][e] = c0 + e < cols ? ip[(c0 + e) * st] : 0.f;
+      }
+    }
+    float o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+#pragma unroll
+      for (int k = 0; k < kMaxIn; ++k)
+        if (k < p.n_in) regs[k].f = v[k][e];
+      o[e] = run_program(p.prog, regs, &err).f;
+    }
+    if (full && (vec_mask & (1u << 31))) {
+      *reinterpret_cast<float4*>(op) = make_float4(o[0], o[1], o[2], o[3]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (c0 + e < cols) op[e] = o[e];
+    }
+  }
+  if (err) set_status(p.status, err);
+}
+
 void launch_elementwise(const EwParams& p, cudaStream_t s) {
   if (p.numel <= 0) return;
+  // Rows fast path: every operand f32 and the output's inner stride 1
+  // (operands with other inner strides are read element by element).
+  if (p.rank >= 2 && p.out.dt == DT_F32 && p.out.st[p.rank - 1] == 1) {
+    const int inner = p.rank - 1;
+    bool ok = true;
+    unsigned vec_mask = 0, bcast_mask = 0;
+    const int64_t cols = p.shape[inner];
+    for (int k = 0; k < p.n_in && ok; ++k) {
+      if (p.in[k].dt != DT_F32) ok = false;
+      else if (p.in[k].st[inner] == 0) bcast_mask |= 1u << k;
+      else if (p.in[k].st[inner] == 1) {
+        bool aligned = (reinterpret_cast<uintptr_t>(p.in[k].ptr) & 15) == 0;
+        for (int d = 0; d < inner; ++d) aligned = aligned && (p.in[k].st[d] % 4 == 0);
+        if (aligned) vec_mask |= 1u << k;
+      }
+    }
+    bool out_aligned = (reinterpret_cast<uintptr_t>(p.out.ptr) & 15) == 0;
+    for (int d = 0; d < inner; ++d) out_aligned = out_aligned && (p.out.st[d] % 4 == 0);
+    if (out_aligned) vec_mask |= 1u << 31;
+    if (ok && cols >= 4) {
+      const int64_t rows = p.numel / cols;
+      const int64_t runs = rows * ((cols + 3) / 4);
+      elementwise_rows4_kernel<<<grid_for(runs), kThreads, 0, s>>>(p, vec_mask, bcast_mask, rows, cols);
+      return;
+    }
+  }
   // Dense float fast path: rank-1 iteration, unit strides or scalars, 16-byte aligned.
   bool dense = p.rank == 1 && p.out.dt == DT_F32 && p.out.st[0] == 1 &&
                (reinterpret_cast<uintptr_t>(p.out.ptr) & 15) == 0;
@@ -444,17 +538,21 @@ __global__ void __launch_bounds__(kThreads) pool_kernel(const __grid_constant__ 
 }
 
 // Dense NHWC on both sides with C % 4 == 0: one thread per 4 channels of an
-// output pixel, 16-byte loads and stores, 32-bit spatial indices.
+// output pixel, 16-byte loads and stores, 32-bit spatial indices.  Idx is the
+// type of the flat output index (32-bit when the output has < 2^31 groups:
+// its divisions cost a fraction of 64-bit ones).
+template <typename Idx>
 __global__ void __launch_bounds__(kThreads) pool_nhwc4_kernel(const __grid_constant__ PoolParams p) {
-  const int cg = (int)(p.C / 4);
-  const int64_t total = p.N * p.OH * p.OW * cg;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+  const Idx cg = (Idx)(p.C / 4);
+  const Idx OW = (Idx)p.OW, OH = (Idx)p.OH;
+  const Idx total = (Idx)(p.N * p.OH * p.OW) * cg;
+  for (Idx i = blockIdx.x * (Idx)blockDim.x + threadIdx.x; i < total; i += (Idx)gridDim.x * blockDim.x) {
     const int g = (int)(i % cg);
-    int64_t r = i / cg;
-    const int ow = (int)(r % p.OW);
-    r /= p.OW;
-    const int oh = (int)(r % p.OH);
-    const int64_t n = r / p.OH;
+    Idx r = i / cg;
+    const int ow = (int)(r % OW);
+    r /= OW;
+    const int oh = (int)(r % OH);
+    const int64_t n = (int64_t)(r / OH);
     const float* base = p.in + n * p.in_st[0] + g * 4;
     float4 acc = p.mode == 0 ? make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY) : make_float4(0.f, 0.f, 0.f, 0.f);
     for (int kh = 0; kh < p.kh; ++kh) {
@@ -489,7 +587,8 @@ void launch_pool(const PoolParams& p, cudaStream_t s) {
                      p.out_st[3] == p.C && p.in_st[2] % 4 == 0 && p.out_st[2] % 4 == 0 && p.in_st[0] % 4 == 0 &&
                      p.out_st[0] % 4 == 0 && (reinterpret_cast<uintptr_t>(p.in) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
-  if (nhwc4) pool_nhwc4_kernel<<<grid_for(total / 4), kThreads, 0, s>>>(p);
+  if (nhwc4 && total / 4 < (int64_t(1) << 31)) pool_nhwc4_kernel<uint32_t><<<grid_for(total / 4), kThreads, 0, s>>>(p);
+  else if (nhwc4) pool_nhwc4_kernel<int64_t><<<grid_for(total / 4), kThreads, 0, s>>>(p);
   else pool_kernel<<<grid_for(total), kThreads, 0, s>>>(p);
 }
 

@@ -23,6 +23,25 @@ def test_binary_broadcast_and_ints():
     parity(*build(g_))
 
 
+@pytest.mark.parametrize("cols", [4, 5, 7, 64, 577])
+def test_elementwise_rows_path(cols):
+    """f32 elementwise ops whose output rows are contiguous take the row-run
+    kernel: full, row-broadcast ([rows,1]), column-broadcast ([cols]) and
+    transposed (inner stride != 1) operands, ragged row tails; IEEE add/mul/div
+    are exact, so the result must equal the oracle bit for bit."""
+    rows = 37
+
+    def g_(g):
+        x = rand_input(g, (2, rows, cols), 11)
+        r = rand_input(g, (2, rows, 1), 12)
+        w = rand_input(g, (cols,), 13)
+        t = rand_input(g, (2, cols, rows), 14)
+        tt = g.transpose(t, (0, 2, 1))
+        y = g.mul(g.div(x, g.add(g.mul(r, r), r)), w)
+        return [y, g.add(x, tt), g.sub(g.mul(x, r), w)]
+    parity(*build(g_), atol=0.0, rtol=0.0)
+
+
 def test_unary_activations():
     def g_(g):
         x = rand_input(g, (3, 37, 11), 7, scale=3.0)

@@ -9,6 +9,7 @@
 #include <array>
 #include <cstdio>
 #include <cstdlib>
+#include <cmath>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -219,6 +220,15 @@ static int match_fast_epilogue(const EProgram& p, float* c) {
   if (p.n_args == 2 && k.size() == 3 && k[0].op == EOp::CONST && k[1].op == EOp::DIVF && k[1].a == 0 &&
       k[1].b == k[0].dst && k[2].op == EOp::ADDF && uses(k[2], k[1].dst, 1) && p.result == k[2].dst) {
     *c = (float)k[0].fimm;
+    // For c = 2^e, x / c and x * 2^-e are the same real number, and IEEE
+    // division and multiplication both round that exact value, so the two
+    // agree bit for bit (2^-e must itself be a normal float: e <= 126).
+    int e = 0;
+    const float mant = std::frexp(*c, &e);
+    if (mant == 0.5f && e >= 1 && e <= 64) {
+      *c = std::ldexp(1.0f, 1 - e);
+      return kern::FAST_MULC_ADD;
+    }
     return kern::FAST_DIVC_ADD;
   }
   if (p.n_args == 3 && k.size() == 7 && k[0].op == EOp::CONST && k[0].fimm == 1.0 && k[1].op == EOp::NEGF &&
@@ -336,6 +346,7 @@ static void launch_tc(Runtime& rt, int o, const Op& op, cudaStream_t s) {
   if (t.epi == kern::EPI_PROGRAM) {
     p.prog = to_device(t.prog);
     p.fast = match_fast_epilogue(t.prog, &p.fast_c);
+    if (p.fast != kern::FAST_NONE) p.epi = kern::EPI_FAST;
   }
   p.status = rt.status();
   if (!kern::launch_conv_gemm_tc(p, rt.tmaps[o][0].b, rt.tmaps[o][1].b, t.block_n, s))

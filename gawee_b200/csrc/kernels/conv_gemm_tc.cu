@@ -10,10 +10,10 @@
 //
 // The tensor core's fp32 accumulation truncates (Fasi et al., "Numerical
 // behavior of NVIDIA tensor cores", 2021), so over thousands of k-steps its
-// error grows linearly with K.  Each 32-wide k-block is therefore accumulated
-// alone in a tensor-memory buffer, and the accumulator warps add the block
-// sums into fp32 registers with IEEE round-to-nearest while later blocks are
-// multiplied into the other buffers.
+// error grows linearly with K.  Each 64-wide round (two k-blocks) is
+// therefore accumulated alone in a tensor-memory buffer, and the accumulator
+// warps add the round sums into fp32 registers with IEEE round-to-nearest
+// while later rounds are multiplied into the other buffer.
 //
 // Operands: A (im2col rows of the NHWC input, or GEMM rows) lives in tensor
 // memory, B (pre-split weight planes) in shared memory, so the MMAs read only
@@ -263,23 +263,31 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   const int64_t num_tiles = m_tiles * n_tiles * p.nb;
 
   // Tile t -> (z, n tile, m tile), m fastest so CTAs running together share B.
+  // Tile, row and batch coordinates fit in 32 bits (the launcher checks), so
+  // their divisions use 32-bit arithmetic.
+  const uint32_t m_tiles32 = (uint32_t)m_tiles, n_tiles32 = (uint32_t)n_tiles;
   auto tile_coords = [&](int64_t t, int64_t& m0, int& n0, int& z) {
-    m0 = (t % m_tiles) * kBM;
-    n0 = (int)(((t / m_tiles) % n_tiles) * BN);
-    z = (int)(t / (m_tiles * n_tiles));
+    const uint32_t tt = (uint32_t)t;
+    const uint32_t mn = tt / m_tiles32;
+    m0 = (int64_t)(tt - mn * m_tiles32) * kBM;
+    const uint32_t zz = mn / n_tiles32;
+    n0 = (int)((mn - zz * n_tiles32) * BN);
+    z = (int)zz;
   };
   // Each tile walks its rounds starting at (m tile index mod num_rounds):
   // CTAs that run side by side then fetch different k-blocks of the shared
   // B operand instead of all hitting the same L2 lines at once.
-  auto r_rotation = [&](int64_t t) -> int { return (int)((t % m_tiles) % num_rounds); };
+  auto r_rotation = [&](int64_t t) -> int { return (int)(((uint32_t)t % m_tiles32) % (uint32_t)num_rounds); };
   auto batch_offsets = [&](int z, int64_t& a_off, int64_t& c_off, int& b_plane) {
     a_off = 0;
     c_off = 0;
     b_plane = 0;
-    int64_t rem = z;
+    uint32_t rem = (uint32_t)z;
     for (int d = p.batch_rank - 1; d >= 0; --d) {
-      const int64_t c = rem % p.batch_shape[d];
-      rem /= p.batch_shape[d];
+      const uint32_t sh = (uint32_t)p.batch_shape[d];
+      const uint32_t q = rem / sh;
+      const int64_t c = rem - q * sh;
+      rem = q;
       a_off += c * p.a_bst[d];
       c_off += c * p.c_bst[d];
       b_plane += (int)(c * p.b_bst[d]);
@@ -348,8 +356,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       for (int i = 0; i < 8; ++i) {
         const int64_t m = m0 + warp * 32 + i * 4 + rsub;
         if (m < p.M) {
-          const int64_t img = m / PQ, pq = m - img * PQ;
-          const int64_t pp = pq / p.Q, qq = pq - pp * p.Q;
+          const uint32_t m32 = (uint32_t)m, PQ32 = (uint32_t)PQ, Q32 = (uint32_t)p.Q;
+          const uint32_t img32 = m32 / PQ32, pq = m32 - img32 * PQ32;
+          const uint32_t pp = pq / Q32, qq = pq - pp * Q32;
+          const int64_t img = img32;
           ih0[i] = (int)(pp * p.sh - p.ph);
           iw0[i] = (int)(qq * p.sw - p.pw);
           rowoff[i] = a_off + img * p.x_sn + (int64_t)ih0[i] * p.x_sh + (int64_t)iw0[i] * p.x_sw;
@@ -602,64 +612,26 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       if (!ok || m >= p.M) continue;
       float* crow = p.out + c_off + m * p.ldc;
       const int nb0 = n0 + cbase;  // first column of this thread's half tile
-      if (EPI == EPI_PROGRAM) {
+      if (EPI == EPI_PROGRAM || EPI == EPI_FAST) {
         // operand offsets of this row: the batch coordinate is fixed per tile
         int64_t aux_row[4];
 #pragma unroll
         for (int a = 0; a < 4; ++a) {
           aux_row[a] = 0;
           if (a < p.n_aux) {
-            int64_t o = m * p.aux_sm[a], rem = z;
+            int64_t o = m * p.aux_sm[a];
+            uint32_t rem = (uint32_t)z;
             for (int d = p.batch_rank - 1; d >= 0; --d) {
-              o += (rem % p.batch_shape[d]) * p.aux_sb[a][d];
-              rem /= p.batch_shape[d];
+              const uint32_t sh = (uint32_t)p.batch_shape[d];
+              const uint32_t q = rem / sh;
+              o += (int64_t)(rem - q * sh) * p.aux_sb[a][d];
+              rem = q;
             }
             aux_row[a] = o;
           }
         }
         const bool vec = p.ldc_n == 1 && nb0 + HB <= p.N && ((reinterpret_cast<uintptr_t>(crow + nb0) & 15) == 0);
-        Reg regs[kMaxRegs];
-        int err = 0;
-        // 8 columns at a time: their operand loads are all in flight before
-        // the program runs on them
-        for (int c0 = 0; c0 < HB; c0 += 8) {
-          float av[4][8];
-#pragma unroll
-          for (int a = 0; a < 4; ++a)
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int64_t n = nb0 + c0 + j;
-              av[a][j] = (a < p.n_aux && n < p.N) ? __ldg(p.aux[a] + aux_row[a] + n * p.aux_sn[a]) : 0.f;
-            }
-          float o[8];
-          if (p.fast != FAST_NONE) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int64_t n = nb0 + c0 + j;
-              const float x = p.bias ? __fadd_rn(acc[c0 + j], n < p.N ? __ldg(p.bias + n) : 0.f) : acc[c0 + j];
-              if (p.fast == FAST_ADD) {
-                o[j] = __fadd_rn(x, av[0][j]);
-              } else if (p.fast == FAST_DIVC_ADD) {
-                o[j] = __fadd_rn(__fdiv_rn(x, p.fast_c), av[0][j]);
-              } else {
-                const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-av[1][j])));
-                o[j] = __fmul_rn(__fmul_rn(av[0][j], sg), x);
-              }
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int64_t n = nb0 + c0 + j;
-              o[j] = 0.f;
-              if (n < p.N) {
-                regs[0].f = p.bias ? __fadd_rn(acc[c0 + j], __ldg(p.bias + n)) : acc[c0 + j];
-#pragma unroll
-                for (int a = 0; a < 4; ++a)
-                  if (a < p.n_aux) regs[1 + a].f = av[a][j];
-                o[j] = run_program(p.prog, regs, &err).f;
-              }
-            }
-          }
+        auto store8 = [&](int c0, const float (&o)[8]) {
           if (vec) {
             *reinterpret_cast<float4*>(crow + nb0 + c0) = make_float4(o[0], o[1], o[2], o[3]);
             *reinterpret_cast<float4*>(crow + nb0 + c0 + 4) = make_float4(o[4], o[5], o[6], o[7]);
@@ -667,6 +639,90 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
             for (int j = 0; j < 8; ++j)
               if (nb0 + c0 + j < p.N) crow[(int64_t)(nb0 + c0 + j) * p.ldc_n] = o[j];
+          }
+        };
+        int err = 0;
+        if (EPI == EPI_FAST) {
+          // Fully unrolled: the accumulators stay in registers.  8 columns at
+          // a time, their operand loads all in flight before they are used.
+          bool aux_vec = p.aux_sn[0] == 1 && nb0 + HB <= p.N &&
+                         ((reinterpret_cast<uintptr_t>(p.aux[0] + aux_row[0] + nb0) & 15) == 0);
+          if (p.fast == FAST_SIGMOID_MUL)
+            aux_vec = aux_vec && p.aux_sn[1] == 1 && ((reinterpret_cast<uintptr_t>(p.aux[1] + aux_row[1] + nb0) & 15) == 0);
+#pragma unroll
+          for (int c0 = 0; c0 < HB; c0 += 8) {
+            float a0[8], a1[8], o[8];
+            if (aux_vec) {  // unit column stride, 16-byte aligned rows, whole chunk in range
+              const float4* q0 = reinterpret_cast<const float4*>(p.aux[0] + aux_row[0] + nb0 + c0);
+              const float4 u = __ldg(q0), v = __ldg(q0 + 1);
+              a0[0] = u.x; a0[1] = u.y; a0[2] = u.z; a0[3] = u.w;
+              a0[4] = v.x; a0[5] = v.y; a0[6] = v.z; a0[7] = v.w;
+              if (p.fast == FAST_SIGMOID_MUL) {
+                const float4* q1 = reinterpret_cast<const float4*>(p.aux[1] + aux_row[1] + nb0 + c0);
+                const float4 w = __ldg(q1), x = __ldg(q1 + 1);
+                a1[0] = w.x; a1[1] = w.y; a1[2] = w.z; a1[3] = w.w;
+                a1[4] = x.x; a1[5] = x.y; a1[6] = x.z; a1[7] = x.w;
+              } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) a1[j] = 0.f;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int64_t n = nb0 + c0 + j;
+                const bool in = n < p.N;
+                a0[j] = in ? __ldg(p.aux[0] + aux_row[0] + n * p.aux_sn[0]) : 0.f;
+                a1[j] = (in && p.fast == FAST_SIGMOID_MUL) ? __ldg(p.aux[1] + aux_row[1] + n * p.aux_sn[1]) : 0.f;
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int64_t n = nb0 + c0 + j;
+              const float x = p.bias ? __fadd_rn(acc[c0 + j], n < p.N ? __ldg(p.bias + n) : 0.f) : acc[c0 + j];
+              if (p.fast == FAST_ADD) {
+                o[j] = __fadd_rn(x, a0[j]);
+              } else if (p.fast == FAST_DIVC_ADD) {
+                o[j] = __fadd_rn(__fdiv_rn(x, p.fast_c), a0[j]);
+              } else if (p.fast == FAST_MULC_ADD) {
+                o[j] = __fadd_rn(__fmul_rn(x, p.fast_c), a0[j]);
+              } else {
+                const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-a1[j])));
+                o[j] = __fmul_rn(__fmul_rn(a0[j], sg), x);
+              }
+            }
+            store8(c0, o);
+          }
+        } else {
+          // Interpreter (its own instantiation, EPI_PROGRAM): the row's sums
+          // go to a separate array first, so the dynamically indexed loop
+          // below does not move `acc` itself out of registers.
+          float accl[HB];
+#pragma unroll
+          for (int j = 0; j < HB; ++j) accl[j] = acc[j];
+          Reg regs[kMaxRegs];
+          for (int c0 = 0; c0 < HB; c0 += 8) {
+            float av[4][8];
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int64_t n = nb0 + c0 + j;
+                av[a][j] = (a < p.n_aux && n < p.N) ? __ldg(p.aux[a] + aux_row[a] + n * p.aux_sn[a]) : 0.f;
+              }
+            float o[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int64_t n = nb0 + c0 + j;
+              o[j] = 0.f;
+              if (n < p.N) {
+                regs[0].f = p.bias ? __fadd_rn(accl[c0 + j], __ldg(p.bias + n)) : accl[c0 + j];
+#pragma unroll
+                for (int a = 0; a < 4; ++a)
+                  if (a < p.n_aux) regs[1 + a].f = av[a][j];
+                o[j] = run_program(p.prog, regs, &err).f;
+              }
+            }
+            store8(c0, o);
           }
         }
         if (err && p.status) atomicCAS(p.status, 0, err);
@@ -765,6 +821,7 @@ bool launch_epi(const ConvGemmParams& p, const void* tmh, const void* tml, cudaS
     case EPI_BIAS_RELU: return launch_t<BN, EPI_BIAS_RELU>(p, tmh, tml, s);
     case EPI_BIAS_ADD_RELU: return launch_t<BN, EPI_BIAS_ADD_RELU>(p, tmh, tml, s);
     case EPI_PROGRAM: return launch_t<BN, EPI_PROGRAM>(p, tmh, tml, s);
+    case EPI_FAST: return launch_t<BN, EPI_FAST>(p, tmh, tml, s);
     default: return false;
   }
 }
@@ -807,6 +864,9 @@ bool launch_conv_gemm_tc(const ConvGemmParams& p, const void* tmap_hi, const voi
   for (int d = 0; d < p.batch_rank; ++d)
     if (p.a_bst[d] % 4 != 0) return false;
   if (p.nb > (1 << 30)) return false;
+  // tile, row and batch coordinates use 32-bit arithmetic in the kernel
+  const int64_t tiles = ((p.M + kBM - 1) / kBM) * ((p.N + block_n - 1) / block_n) * p.nb;
+  if (p.M >= (int64_t(1) << 31) || tiles >= (int64_t(1) << 31) || p.P * p.Q >= (int64_t(1) << 31)) return false;
   if (block_n == 64) return launch_epi<64>(p, tmap_hi, tmap_lo, s);
   if (block_n == 128) return launch_epi<128>(p, tmap_hi, tmap_lo, s);
   return false;

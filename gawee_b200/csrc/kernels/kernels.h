@@ -221,6 +221,7 @@ enum Epi : int {
   EPI_BIAS_RELU = 2,  // C = max(acc + bias[n], 0)
   EPI_BIAS_ADD_RELU = 3,  // C = max((acc + bias[n]) + res[m][n], 0)
   EPI_PROGRAM = 4,    // C = program(acc, aux...) with aux operands indexed like C
+  EPI_FAST = 5,       // a program recognised on the host (ConvGemmParams::fast), no interpreter
 };
 
 struct ConvGemmParams {
@@ -262,6 +263,7 @@ enum FastEpi : int {
   FAST_ADD = 1,          // acc + aux0
   FAST_DIVC_ADD = 2,     // (acc / c) + aux0
   FAST_SIGMOID_MUL = 3,  // (aux0 * (1 / (1 + exp(-aux1)))) * acc
+  FAST_MULC_ADD = 4,     // (acc * c) + aux0: acc / d with d a power of two, c = 1 / d (exact)
 };
 
 // Returns false (and launches nothing) when the shape is not supported.

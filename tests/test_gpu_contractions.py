@@ -82,6 +82,22 @@ def test_matmul_fused_epilogues():
     parity(*build(g_), atol=2e-4, rtol=1e-4)
 
 
+@pytest.mark.parametrize("scale", [8.0, 6.928203230275509])
+def test_attention_score_epilogue(scale):
+    """Batched Q.K^T with the score epilogue the emitter produces: divide by a
+    constant, add a broadcast mask.  A power-of-two divisor takes the exact
+    reciprocal-multiply path, any other the IEEE division; both must match the
+    oracle, as must a residual add on a second product."""
+    def g_(g):
+        q = rand_input(g, (2, 3, 130, 64), 31)
+        k = rand_input(g, (2, 3, 64, 136), 32)
+        mask = rand_input(g, (1, 1, 130, 136), 33, scale=5.0)
+        sc = g.add(g.div(g.matmul(q, k), g.const(scale, F)), mask)
+        res = rand_input(g, (2, 3, 130, 136), 34)
+        return [sc, g.add(res, g.matmul(q, k))]
+    parity(*build(g_), atol=2e-4, rtol=1e-4)
+
+
 CONVS = [
     # (N, C, H, W, F, k, stride, pad, dil)
     (1, 3, 33, 31, 16, 7, 2, 3, 1),     # stem-like, C=3 -> padded to 4 channels

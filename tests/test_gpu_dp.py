@@ -1,7 +1,10 @@
 """Data parallelism on two GPUs: each rank runs its batch slice of ResNet-18,
 rank 0 gathers the output rows over NCCL (gawee_dp_gather_output), and the
-result equals the single-GPU full-batch forward (batch rows are independent,
-and every rank runs the same kernels on its rows)."""
+result matches the single-GPU full-batch forward.  Batch rows are
+independent, but a row's 128-row tile position differs between the sharded
+and the full batch, and the tensor-core kernel starts each tile's k loop at a
+rotation that depends on that position, so the fp32 sums are ordered
+differently: the comparison uses the reference's ResNet tolerance."""
 import os
 import socket
 import subprocess
@@ -73,4 +76,4 @@ def test_two_gpu_batch_sharding_matches_one_gpu(tmp_path):
         want = m.run(args)[0]
     finally:
         m.close()
-    np.testing.assert_allclose(gathered, want, atol=1e-5, rtol=1e-5)
+    np.testing.assert_allclose(gathered, want, atol=1e-4, rtol=1e-4)

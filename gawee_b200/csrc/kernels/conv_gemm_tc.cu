@@ -59,8 +59,9 @@ constexpr int kRK = 2;
 // barrier per slot says "everything for this round is ready".
 constexpr int kS = 2;
 // Raw A k-blocks in flight per tile width.  Shared memory: 2 x 32 KB + 8 x
-// 16 KB for BN 64, 2 x 64 KB + 5 x 16 KB for BN 128; tensor memory: 2 x 64 +
-// 2 x 128 and 2 x 128 + 2 x 128 of its 512 columns.
+// 16 KB for BN 64, 2 x 64 KB + 4 x 16 KB for BN 128, plus 20 KB of epilogue
+// staging; tensor memory: 2 x 64 + 2 x 128 and 2 x 128 + 2 x 128 of its 512
+// columns.
 template <int BN>
 struct TcConfig;
 template <>
@@ -69,8 +70,13 @@ struct TcConfig<64> {
 };
 template <>
 struct TcConfig<128> {
-  static constexpr int RD = 5;
+  static constexpr int RD = 4;
 };
+// Epilogue staging: each accumulator warp transposes 16-column chunks of its
+// 32 rows through shared memory (row pitch 20 floats: conflict-free float4
+// writes by row, float4 reads by column group).
+constexpr int kStagePitch = 20;
+constexpr int kStageWarpFloats = 32 * kStagePitch;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -218,7 +224,8 @@ struct Smem {
   static constexpr int kBTile = BN * kBK * 4;
   static constexpr int kBStage = kRK * 2 * kBTile;
   static constexpr int kRawOff = kS * kBStage;
-  static constexpr int kBarOff = kRawOff + RD * kATile;
+  static constexpr int kStageOff = kRawOff + RD * kATile;
+  static constexpr int kBarOff = kStageOff + 8 * kStageWarpFloats * 4;
   static constexpr int kNumBars = 2 * kS + 1;  // ready, done per slot; all MMAs done
   static constexpr int kBytes = kBarOff + 8 * kNumBars + 16 + 1024;  // + alignment slack
   static constexpr int kACol = kS * BN;
@@ -587,7 +594,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       for (int j = 0; j < HB; ++j) acc[j] = 0.0f;
       for (int r = 0; r < num_rounds; ++r) {
         const int buf = sl;
-        if (!mbar_wait(smem_u32(&rdone[sl]), done_ph, abort_flag, p.status)) {
+        // warp-uniform outcome: the epilogue below uses warp-collective steps
+        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&rdone[sl]), done_ph, abort_flag, p.status))) {
           ok = false;
           break;
         }
@@ -607,7 +615,72 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           done_ph ^= 1;
         }
       }
-      ok = ok && !*abort_flag;
+      ok = __all_sync(0xffffffffu, ok && !*abort_flag);
+      if (EPI < EPI_PROGRAM) {
+        // Coalesced epilogue: the warp writes its 32 rows 16 columns at a
+        // time into shared memory, then stores them four lanes per row, so a
+        // store instruction covers 8 rows x 64 contiguous bytes instead of 32
+        // rows x 16 bytes; bias and residual come as whole float4 groups.
+        const bool coal = p.ldc_n == 1 && (p.ldc & 3) == 0 && (c_off & 3) == 0 &&
+                          (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 &&
+                          (EPI != EPI_BIAS_ADD_RELU || (reinterpret_cast<uintptr_t>(p.res) & 15) == 0);
+        if (coal && __all_sync(0xffffffffu, ok)) {
+          float* stage = reinterpret_cast<float*>(smem + L::kStageOff) + (warp - 6) * kStageWarpFloats;
+          const int nb0 = n0 + cbase;
+          const int c4 = lane & 3;
+#pragma unroll
+          for (int c0 = 0; c0 < HB; c0 += 16) {
+            float* srow = stage + lane * kStagePitch;
+#pragma unroll
+            for (int j = 0; j < 16; j += 4)
+              *reinterpret_cast<float4*>(srow + j) = make_float4(acc[c0 + j], acc[c0 + j + 1], acc[c0 + j + 2], acc[c0 + j + 3]);
+            __syncwarp();
+            const int64_t n = nb0 + c0 + c4 * 4;
+            float b[4] = {0.f, 0.f, 0.f, 0.f};
+            if (EPI >= EPI_BIAS) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) b[e] = n + e < p.N ? __ldg(p.bias + n + e) : 0.f;
+            }
+#pragma unroll
+            for (int it = 0; it < 4; ++it) {
+              const int r = it * 8 + (lane >> 2);
+              const int64_t m = m0 + q * 32 + r;
+              const float4 v = *reinterpret_cast<const float4*>(stage + r * kStagePitch + c4 * 4);
+              if (m < p.M && n < p.N) {
+                float x[4] = {v.x, v.y, v.z, v.w};
+                const bool full = n + 3 < p.N;
+                float rv[4] = {0.f, 0.f, 0.f, 0.f};
+                if (EPI == EPI_BIAS_ADD_RELU) {
+                  const float* rp = p.res + c_off + m * p.ldc + n;
+                  if (full) {
+                    const float4 t = __ldg(reinterpret_cast<const float4*>(rp));
+                    rv[0] = t.x; rv[1] = t.y; rv[2] = t.z; rv[3] = t.w;
+                  } else {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) rv[e] = n + e < p.N ? __ldg(rp + e) : 0.f;
+                  }
+                }
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  if (EPI >= EPI_BIAS) x[e] = __fadd_rn(x[e], b[e]);
+                  if (EPI == EPI_BIAS_ADD_RELU) x[e] = __fadd_rn(x[e], rv[e]);
+                  if (EPI == EPI_BIAS_RELU || EPI == EPI_BIAS_ADD_RELU) x[e] = maximumf_(x[e], 0.0f);
+                }
+                float* cp = p.out + c_off + m * p.ldc + n;
+                if (full) {
+                  *reinterpret_cast<float4*>(cp) = make_float4(x[0], x[1], x[2], x[3]);
+                } else {
+#pragma unroll
+                  for (int e = 0; e < 4; ++e)
+                    if (n + e < p.N) cp[e] = x[e];
+                }
+              }
+            }
+            __syncwarp();  // the staging rows are rewritten by the next chunk
+          }
+          continue;
+        }
+      }
       const int64_t m = m0 + row;
       if (!ok || m >= p.M) continue;
       float* crow = p.out + c_off + m * p.ldc;

@@ -541,7 +541,9 @@ __global__ void __launch_bounds__(kThreads) pool_kernel(const __grid_constant__ 
 // output pixel, 16-byte loads and stores, 32-bit spatial indices.  Idx is the
 // type of the flat output index (32-bit when the output has < 2^31 groups:
 // its divisions cost a fraction of 64-bit ones).
-template <typename Idx>
+// KW > 0 fixes the window at compile time (KW x KW), so the window's loads are
+// all issued before the first is used.
+template <typename Idx, int KW>
 __global__ void __launch_bounds__(kThreads) pool_nhwc4_kernel(const __grid_constant__ PoolParams p) {
   const Idx cg = (Idx)(p.C / 4);
   const Idx OW = (Idx)p.OW, OH = (Idx)p.OH;
@@ -555,9 +557,12 @@ __global__ void __launch_bounds__(kThreads) pool_nhwc4_kernel(const __grid_const
     const int64_t n = (int64_t)(r / OH);
     const float* base = p.in + n * p.in_st[0] + g * 4;
     float4 acc = p.mode == 0 ? make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY) : make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int kh = 0; kh < p.kh; ++kh) {
+    const int nkh = KW > 0 ? KW : p.kh, nkw = KW > 0 ? KW : p.kw;
+#pragma unroll
+    for (int kh = 0; kh < nkh; ++kh) {
       const int ih = oh * p.sh + kh * p.dh - p.ph;
-      for (int kw = 0; kw < p.kw; ++kw) {
+#pragma unroll
+      for (int kw = 0; kw < nkw; ++kw) {
         const int iw = ow * p.sw + kw * p.dw - p.pw;
         const bool in = ih >= 0 && ih < p.H && iw >= 0 && iw < p.W;
         float4 v;
@@ -587,8 +592,11 @@ void launch_pool(const PoolParams& p, cudaStream_t s) {
                      p.out_st[3] == p.C && p.in_st[2] % 4 == 0 && p.out_st[2] % 4 == 0 && p.in_st[0] % 4 == 0 &&
                      p.out_st[0] % 4 == 0 && (reinterpret_cast<uintptr_t>(p.in) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
-  if (nhwc4 && total / 4 < (int64_t(1) << 31)) pool_nhwc4_kernel<uint32_t><<<grid_for(total / 4), kThreads, 0, s>>>(p);
-  else if (nhwc4) pool_nhwc4_kernel<int64_t><<<grid_for(total / 4), kThreads, 0, s>>>(p);
+  const bool small = total / 4 < (int64_t(1) << 31);
+  if (nhwc4 && small && p.kh == 3 && p.kw == 3)
+    pool_nhwc4_kernel<uint32_t, 3><<<grid_for(total / 4), kThreads, 0, s>>>(p);
+  else if (nhwc4 && small) pool_nhwc4_kernel<uint32_t, 0><<<grid_for(total / 4), kThreads, 0, s>>>(p);
+  else if (nhwc4) pool_nhwc4_kernel<int64_t, 0><<<grid_for(total / 4), kThreads, 0, s>>>(p);
   else pool_kernel<<<grid_for(total), kThreads, 0, s>>>(p);
 }
 

@@ -16,7 +16,9 @@ One JSON line on rank 0:
   value       whole-job images/s (or tokens/s), inputs resident in HBM, device
               time of K forwards (CUDA events on the launch stream, max over ranks)
   e2e         same metric through the C ABI with pinned host buffers: each step
-              copies the input in, runs the forward and copies the output back
+              copies its input in, runs the forward and copies its output back;
+              consecutive steps are pipelined (upload, compute and download on
+              three streams, two staging buffers each way)
   roofline    tensor-core kernels: algorithmic FLOPs / their device time in an
               eagerly profiled forward, against the measured peaks
   cpu_baseline  the CPU oracle (a C++ port of the reference lowering semantics)
@@ -246,21 +248,65 @@ def main():
     clocks = clk.summary()
     value = total_batch * items * a.steps / (ms / 1e3)
 
-    # end to end through the C ABI: pinned host input in, output back, every step
-    h_in = torch.from_numpy(args[0]).pin_memory()
-    h_out = torch.empty(out_bytes, dtype=torch.uint8).pin_memory()
+    # End to end through the C ABI, every step: the step's input from pinned
+    # host memory to the GPU, gawee_set_arg_device + gawee_forward, the result
+    # back to pinned host memory.  Steps are pipelined the way a serving loop
+    # would run them: step i+1's upload (its own stream) overlaps step i's
+    # forward and step i's download (another stream) overlaps step i+1's, with
+    # two device staging buffers each way and events ordering the hand-offs.
+    from cuda.bindings import runtime as cudart
     in_bytes = args[0].nbytes
+    h_in = torch.from_numpy(args[0]).pin_memory().view(torch.uint8).reshape(-1)
+    h_out = [torch.empty(out_bytes, dtype=torch.uint8).pin_memory() for _ in range(2)]
+    dev = f"cuda:{local}"
+    d_in = [torch.empty(in_bytes, dtype=torch.uint8, device=dev) for _ in range(2)]
+    d_out = [torch.empty(out_bytes, dtype=torch.uint8, device=dev) for _ in range(2)]
+    up, down = torch.cuda.Stream(local), torch.cuda.Stream(local)
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    in_free = [torch.cuda.Event() for _ in range(2)]
+    out_ready = [torch.cuda.Event() for _ in range(2)]
+    out_free = [torch.cuda.Event() for _ in range(2)]
+    out_ptr = m.output_ptr(0)
+    d2d = cudart.cudaMemcpyKind.cudaMemcpyDeviceToDevice
 
-    def e2e_step():
-        m._check(m._lib.gawee_set_arg(m._h, 0, h_in.data_ptr(), in_bytes, sp))
-        step()
-        m._check(m._lib.gawee_get_output(m._h, 0, h_out.data_ptr(), out_bytes, sp))
+    def e2e_steps(k):
+        for i in range(k):
+            b = i & 1
+            if i >= 2:
+                up.wait_event(in_free[b])      # step i-2 has consumed this staging buffer
+            with torch.cuda.stream(up):
+                d_in[b].copy_(h_in, non_blocking=True)
+            in_ready[b].record(up)
+            stream.wait_event(in_ready[b])
+            m._check(m._lib.gawee_set_arg_device(m._h, 0, d_in[b].data_ptr(), in_bytes, sp))
+            in_free[b].record(stream)
+            step()
+            if i >= 2:
+                stream.wait_event(out_free[b])  # step i-2's result has reached the host
+            err, = cudart.cudaMemcpyAsync(d_out[b].data_ptr(), out_ptr, out_bytes, d2d, cudart.cudaStream_t(sp))
+            if err != cudart.cudaError_t.cudaSuccess:
+                raise RuntimeError(f"cudaMemcpyAsync: {err}")
+            out_ready[b].record(stream)
+            down.wait_event(out_ready[b])
+            with torch.cuda.stream(down):
+                h_out[b].copy_(d_out[b], non_blocking=True)
+            out_free[b].record(down)
 
-    for _ in range(2):
-        e2e_step()
-    m.synchronize(sp)
-    ms_e2e = timed(e2e_step, a.steps)
-    m.synchronize(sp)
+    e2e_steps(2)
+    torch.cuda.synchronize(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(up)
+    e2e_steps(a.steps)
+    e1.record(down)                              # after the last step's download
+    torch.cuda.synchronize(local)
+    ms_e2e = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms_e2e], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t.item())
     e2e_value = total_batch * items * a.steps / (ms_e2e / 1e3)
 
     # per-kernel device times of one eager forward -> tensor-core roofline

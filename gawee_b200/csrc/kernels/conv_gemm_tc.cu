@@ -228,9 +228,13 @@ struct Smem {
   static constexpr int kBarOff = kStageOff + 8 * kStageWarpFloats * 4;
   static constexpr int kNumBars = 2 * kS + 1;  // ready, done per slot; all MMAs done
   static constexpr int kBytes = kBarOff + 8 * kNumBars + 16 + 1024;  // + alignment slack
-  static constexpr int kACol = kS * BN;
+  // BN 64 folds two passes into one N = 128 MMA (see the MMA issuer), so its
+  // round accumulator spans 2 x BN columns.
+  static constexpr bool kFold = BN == 64;
+  static constexpr int kAccCols = kFold ? 2 * BN : BN;
+  static constexpr int kACol = kS * kAccCols;
   static constexpr int kAStageCols = kRK * 2 * kBK;
-  static constexpr int kUsedCols = kS * BN + kS * kAStageCols;
+  static constexpr int kUsedCols = kS * kAccCols + kS * kAStageCols;
   static constexpr int kTmemCols = kUsedCols <= 256 ? 256 : 512;
   static_assert(kUsedCols <= 512, "tensor memory columns");
 };
@@ -523,6 +527,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     // issues the MMAs and the commits that track them.  A comes from tensor
     // memory (raw and remainder columns), B from shared memory.
     const uint32_t idesc = umma_idesc_tf32<BN>();
+    const uint32_t idesc2 = umma_idesc_tf32<2 * BN>();  // B's hi and lo planes as one operand
     const uint64_t desc0 = umma_desc_sw128(smem_u32(smem));
     constexpr uint64_t kBStageDesc = (uint64_t)(L::kBStage >> 4);  // descriptor start-address units
     constexpr uint64_t kBTileDesc = (uint64_t)(L::kBTile >> 4);
@@ -542,7 +547,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         tc_fence_after();
         // the start address of a K-major SW128 descriptor advances 32 bytes
         // (2 units) per 8-wide k-step; an A column holds one k
-        const uint32_t tmem_d = tmem_base + (uint32_t)(sl * BN);
+        const uint32_t tmem_d = tmem_base + (uint32_t)(sl * L::kAccCols);
         if (lane == 0) {
           for (int j = 0; j < nk; ++j) {
             const uint64_t dbh = desc0 + (uint64_t)sl * kBStageDesc + (uint64_t)j * 2 * kBTileDesc;
@@ -553,9 +558,19 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             for (int kk = 0; kk < kBK / 8; ++kk) {
               const uint64_t o = (uint64_t)(2 * kk);
               const uint32_t ka = (uint32_t)(8 * kk);
-              umma_tf32_ts(tmem_d, a_rem + ka, dbh + o, idesc, (j | kk) != 0);
-              umma_tf32_ts(tmem_d, a_raw + ka, dbl + o, idesc, 1);
-              umma_tf32_ts(tmem_d, a_raw + ka, dbh + o, idesc, 1);
+              if (L::kFold) {
+                // The B stage holds the hi plane's BN rows directly followed by
+                // the lo plane's, so one N = 2*BN MMA gives [hi*hi | hi*lo];
+                // lo*hi (N = BN) accumulates into the first half.  An M = 128
+                // MMA costs nearly the same for N = 64 and 128, so this issues
+                // two MMAs per k-step instead of three.
+                umma_tf32_ts(tmem_d, a_raw + ka, dbh + o, idesc2, (j | kk) != 0);
+                umma_tf32_ts(tmem_d, a_rem + ka, dbh + o, idesc, 1);
+              } else {
+                umma_tf32_ts(tmem_d, a_rem + ka, dbh + o, idesc, (j | kk) != 0);
+                umma_tf32_ts(tmem_d, a_raw + ka, dbl + o, idesc, 1);
+                umma_tf32_ts(tmem_d, a_raw + ka, dbh + o, idesc, 1);
+              }
             }
           }
           umma_commit(smem_u32(&rdone[sl]));
@@ -603,9 +618,17 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
         for (int c0 = 0; c0 < HB; c0 += 32) {
           uint32_t r[32];
-          tmem_ld32(lane_base + (uint32_t)(buf * BN + cbase + c0), r);
+          tmem_ld32(lane_base + (uint32_t)(buf * L::kAccCols + cbase + c0), r);
+          if (L::kFold) {  // the round's sum is split over the two halves
+            uint32_t r2[32];
+            tmem_ld32(lane_base + (uint32_t)(buf * L::kAccCols + BN + cbase + c0), r2);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[c0 + j] = __fadd_rn(acc[c0 + j], __uint_as_float(r[j]));
+            for (int j = 0; j < 32; ++j)
+              acc[c0 + j] = __fadd_rn(acc[c0 + j], __fadd_rn(__uint_as_float(r[j]), __uint_as_float(r2[j])));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[c0 + j] = __fadd_rn(acc[c0 + j], __uint_as_float(r[j]));
+          }
         }
         tc_fence_before();
         __syncwarp();

@@ -404,6 +404,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         } else if (++lka == num_kb) {
           lka = 0;
           decompose(chunk * 4);
+        } else if (C < kBK) {
+          decompose(lka * kBK + chunk * 4);  // k crosses several (r, s) positions: divide directly
         } else {
           kc += kBK;
           while (kc >= C) {

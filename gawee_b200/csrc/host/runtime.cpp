@@ -240,6 +240,57 @@ static int match_fast_epilogue(const EProgram& p, float* c) {
   return kern::FAST_NONE;
 }
 
+// Recognises the small f32 elementwise programs decoder and normalisation
+// blocks produce (copy, square, negate, sqrt(x + eps), x / r * w, a*b + c*d)
+// so the kernels evaluate them without the interpreter; each match checks
+// the exact operation sequence and records operand indices.
+static void match_fast_ew(const EProgram& p, kern::EwParams& e) {
+  const auto& k = p.code;
+  int fast = kern::EW_INTERP;
+  std::vector<int> sel;  // program arguments in the order the fast form reads them
+  for (DType t : p.reg_types)
+    if (t != DType::F32) return;
+  for (const auto& in : k)
+    if (in.ty != DType::F32 || in.rty != DType::F32) return;
+  auto arg = [&](int r) { return r >= 0 && r < p.n_args; };
+  if (k.empty() && arg(p.result)) {
+    fast = kern::EW_COPY;
+    sel = {p.result};
+  } else if (k.size() == 1 && k[0].dst == p.result && k[0].op == EOp::NEGF && arg(k[0].a)) {
+    fast = kern::EW_NEG;
+    sel = {k[0].a};
+  } else if (k.size() == 1 && k[0].dst == p.result && k[0].op == EOp::MULF && arg(k[0].a) && k[0].a == k[0].b) {
+    fast = kern::EW_SQR;
+    sel = {k[0].a};
+  } else if (k.size() == 2 && k[0].op == EOp::CONST && k[1].op == EOp::POWF && k[0].fimm == 2.0 && arg(k[1].a) &&
+             k[1].b == k[0].dst && k[1].dst == p.result) {
+    fast = kern::EW_SQR;  // the interpreter evaluates powf(x, 2) as x * x
+    sel = {k[1].a};
+  } else if (k.size() == 2 && k[0].op == EOp::DIVF && arg(k[0].a) && arg(k[0].b) && k[1].op == EOp::MULF &&
+             k[1].dst == p.result && ((k[1].a == k[0].dst && arg(k[1].b)) || (k[1].b == k[0].dst && arg(k[1].a)))) {
+    fast = kern::EW_DIV_MUL;
+    sel = {k[0].a, k[0].b, k[1].a == k[0].dst ? k[1].b : k[1].a};
+  } else if (k.size() == 3 && k[0].op == EOp::CONST && k[1].op == EOp::ADDF && k[2].op == EOp::SQRT &&
+             k[2].a == k[1].dst && k[2].dst == p.result &&
+             ((k[1].a == k[0].dst && arg(k[1].b)) || (k[1].b == k[0].dst && arg(k[1].a)))) {
+    fast = kern::EW_ADDC_SQRT;
+    sel = {k[1].a == k[0].dst ? k[1].b : k[1].a};
+    e.fk = (float)k[0].fimm;
+  } else if (k.size() == 3 && k[0].op == EOp::MULF && k[1].op == EOp::MULF && k[2].op == EOp::ADDF &&
+             arg(k[0].a) && arg(k[0].b) && arg(k[1].a) && arg(k[1].b) && k[2].dst == p.result &&
+             ((k[2].a == k[0].dst && k[2].b == k[1].dst) || (k[2].a == k[1].dst && k[2].b == k[0].dst))) {
+    fast = kern::EW_MUL_MUL_ADD;  // a*b + c*d: IEEE addition is commutative, so the product order is free
+    sel = {k[0].a, k[0].b, k[1].a, k[1].b};
+  } else {
+    return;
+  }
+  kern::EwOperand orig[kern::kMaxIn];
+  for (int i = 0; i < e.n_in; ++i) orig[i] = e.in[i];
+  for (size_t i = 0; i < sel.size(); ++i) e.in[i] = orig[sel[i]];
+  e.n_in = (int)sel.size();
+  e.fast = fast;
+}
+
 static void launch_ew(Runtime& rt, const Op& op, cudaStream_t s) {
   const View& out = op.out;
   int r = out.rank();
@@ -291,6 +342,9 @@ static void launch_ew(Runtime& rt, const Op& op, cudaStream_t s) {
     p.in[k].dt = (int8_t)op.ins[k].dt;
   }
   p.prog = to_device(op.prog);
+  bool all_f32 = out.dt == DType::F32;
+  for (const auto& v : op.ins) all_f32 = all_f32 && v.dt == DType::F32;
+  if (all_f32) match_fast_ew(op.prog, p);
   p.status = rt.status();
   kern::launch_elementwise(p, s);
 }

@@ -48,6 +48,19 @@ struct EwOperand {
   int8_t dt;
 };
 
+// Elementwise programs recognised on the host (all f32) and evaluated without
+// the interpreter, with the same IEEE operations in the same order.
+// The host reorders the operands so the fast form reads in[0..3].
+enum FastEw : int {
+  EW_INTERP = 0,
+  EW_COPY = 1,        // in[0]
+  EW_SQR = 2,         // in[0] * in[0]           (powf(x, 2) or x * x)
+  EW_NEG = 3,         // -in[0]
+  EW_ADDC_SQRT = 4,   // sqrt(in[0] + fk)
+  EW_DIV_MUL = 5,     // (in[0] / in[1]) * in[2]
+  EW_MUL_MUL_ADD = 6, // (in[0] * in[1]) + (in[2] * in[3])
+};
+
 struct EwParams {
   int rank;
   int n_in;
@@ -56,6 +69,8 @@ struct EwParams {
   EwOperand out;
   EwOperand in[kMaxIn];
   DProgram prog;
+  int fast;                  // FastEw
+  float fk;                  // its constant
   int* status;
 };
 

@@ -44,6 +44,19 @@ __device__ __forceinline__ void set_status(int* st, int code) {
 // Elementwise: one program run per output element; operands addressed through
 // per-dimension strides over the iteration space (0 = broadcast).
 // ---------------------------------------------------------------------------
+// Evaluates a recognised f32 program (EwParams::fast) on operand values v.
+template <int N>
+__device__ __forceinline__ float eval_fast(const EwParams& p, const float (&v)[kMaxIn][N], int e) {
+  switch (p.fast) {
+    case EW_COPY: return v[0][e];
+    case EW_SQR: return __fmul_rn(v[0][e], v[0][e]);
+    case EW_NEG: return -v[0][e];
+    case EW_ADDC_SQRT: return __fsqrt_rn(__fadd_rn(v[0][e], p.fk));
+    case EW_DIV_MUL: return __fmul_rn(__fdiv_rn(v[0][e], v[1][e]), v[2][e]);
+    default: return __fadd_rn(__fmul_rn(v[0][e], v[1][e]), __fmul_rn(v[2][e], v[3][e]));
+  }
+}
+
 __global__ void __launch_bounds__(kThreads) elementwise_kernel(const __grid_constant__ EwParams p) {
   Reg regs[kMaxRegs];
   int err = 0;
@@ -92,12 +105,25 @@ __global__ void __launch_bounds__(kThreads) elementwise_dense4_kernel(const __gr
     }
     float4 o;
     float* op = reinterpret_cast<float*>(&o);
+    if (p.fast != EW_INTERP) {
+      float w[kMaxIn][4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
+      for (int k = 0; k < kMaxIn; ++k) {
+        w[k][0] = v[k].x;
+        w[k][1] = v[k].y;
+        w[k][2] = v[k].z;
+        w[k][3] = v[k].w;
+      }
 #pragma unroll
-      for (int k = 0; k < kMaxIn; ++k)
-        if (k < p.n_in) regs[k].f = reinterpret_cast<float*>(&v[k])[e];
-      op[e] = run_program(p.prog, regs, &err).f;
+      for (int e = 0; e < 4; ++e) op[e] = eval_fast(p, w, e);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+#pragma unroll
+        for (int k = 0; k < kMaxIn; ++k)
+          if (k < p.n_in) regs[k].f = reinterpret_cast<float*>(&v[k])[e];
+        op[e] = run_program(p.prog, regs, &err).f;
+      }
     }
     reinterpret_cast<float4*>(p.out.ptr)[i] = o;
   }
@@ -162,12 +188,17 @@ __global__ void __launch_bounds__(kThreads) elementwise_rows4_kernel(const __gri
       }
     }
     float o[4];
+    if (p.fast != EW_INTERP) {
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
+      for (int e = 0; e < 4; ++e) o[e] = eval_fast(p, v, e);
+    } else {
 #pragma unroll
-      for (int k = 0; k < kMaxIn; ++k)
-        if (k < p.n_in) regs[k].f = v[k][e];
-      o[e] = run_program(p.prog, regs, &err).f;
+      for (int e = 0; e < 4; ++e) {
+#pragma unroll
+        for (int k = 0; k < kMaxIn; ++k)
+          if (k < p.n_in) regs[k].f = v[k][e];
+        o[e] = run_program(p.prog, regs, &err).f;
+      }
     }
     if (full && (vec_mask & (1u << 31))) {
       *reinterpret_cast<float4*>(op) = make_float4(o[0], o[1], o[2], o[3]);

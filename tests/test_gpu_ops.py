@@ -42,6 +42,29 @@ def test_elementwise_rows_path(cols):
     parity(*build(g_), atol=0.0, rtol=0.0)
 
 
+def test_elementwise_fast_forms():
+    """Programs the host recognises and the kernels evaluate without the
+    interpreter: negate, square (x * x and powf(x, 2)), sqrt(x + eps),
+    x / r * w with broadcast operands, a*b + c*d.  Dense operands take the
+    flat float4 kernel, broadcast ones the row-run kernel.  All are IEEE
+    single operations and match the oracle bit for bit, except powf(x, 2):
+    the device evaluates it as the correctly rounded x * x, while the
+    oracle calls libm powf (as the reference's lowering does), which can
+    be one ulp away; hence the two-ulp relative bound."""
+    def g_(g):
+        x = rand_input(g, (2, 37, 64), 41)
+        y = rand_input(g, (2, 37, 64), 42)
+        r = rand_input(g, (2, 37, 1), 43)
+        w = rand_input(g, (64,), 44)
+        m = g.mul(rand_input(g, (2, 37, 6), 45), rand_input(g, (2, 37, 6), 46))
+        # m is also an output, so sqrt(m + eps) stays a program of its own
+        return [m, g.neg(x), g.mul(y, y), g.pow(x, g.const(2.0, F)),
+                g.sqrt(g.add(m, g.const(1e-5, F))),
+                g.mul(g.div(x, r), w),
+                g.add(g.mul(x, y), g.mul(rand_input(g, (2, 37, 64), 47), w))]
+    parity(*build(g_), atol=0.0, rtol=2.4e-7)
+
+
 def test_unary_activations():
     def g_(g):
         x = rand_input(g, (3, 37, 11), 7, scale=3.0)

@@ -369,9 +369,79 @@ __global__ void __launch_bounds__(kThreads) softmax_kernel(const __grid_constant
   }
 }
 
+// Rows of up to 32 * PER elements: one warp per row holds the row in
+// registers (PER values per lane, float4 loads and stores when the axis is
+// contiguous and aligned), so the row is read once and written once.  Same
+// steps as the multi-pass kernel: max from -FLT_MAX, exp(x - max), sum, divide.
+template <int PER>
+__global__ void __launch_bounds__(kThreads) softmax_reg_kernel(const __grid_constant__ SoftmaxParams p, bool vec) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (kThreads / 32);
+  for (int64_t row = blockIdx.x * (int64_t)(kThreads / 32) + threadIdx.x / 32; row < p.rows; row += warps) {
+    const float* x = p.in + unravel_off(row, p.rank, p.row_shape, p.in_row_st);
+    float* y = p.out + unravel_off(row, p.rank, p.row_shape, p.out_row_st);
+    float v[PER];
+    if (vec) {
+#pragma unroll
+      for (int c = 0; c < PER / 4; ++c) {
+        const int64_t j = ((int64_t)c * 32 + lane) * 4;
+        float4 t = make_float4(-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX);
+        if (j < p.len) t = *reinterpret_cast<const float4*>(x + j);
+        v[4 * c] = t.x;
+        v[4 * c + 1] = t.y;
+        v[4 * c + 2] = t.z;
+        v[4 * c + 3] = t.w;
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < PER; ++c) {
+        const int64_t j = (int64_t)c * 32 + lane;
+        v[c] = j < p.len ? x[j * p.in_axis_st] : -FLT_MAX;
+      }
+    }
+    float m = -FLT_MAX;
+#pragma unroll
+    for (int c = 0; c < PER; ++c) m = fmaxf(m, v[c]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float ssum = 0.0f;
+#pragma unroll
+    for (int c = 0; c < PER; ++c) {
+      const int64_t j = vec ? ((int64_t)(c / 4) * 32 + lane) * 4 + (c & 3) : (int64_t)c * 32 + lane;
+      v[c] = j < p.len ? expf(__fsub_rn(v[c], m)) : 0.0f;
+      ssum += v[c];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
+    if (vec) {
+#pragma unroll
+      for (int c = 0; c < PER / 4; ++c) {
+        const int64_t j = ((int64_t)c * 32 + lane) * 4;
+        if (j < p.len)
+          *reinterpret_cast<float4*>(y + j) = make_float4(__fdiv_rn(v[4 * c], ssum), __fdiv_rn(v[4 * c + 1], ssum),
+                                                          __fdiv_rn(v[4 * c + 2], ssum), __fdiv_rn(v[4 * c + 3], ssum));
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < PER; ++c) {
+        const int64_t j = (int64_t)c * 32 + lane;
+        if (j < p.len) y[j * p.out_axis_st] = __fdiv_rn(v[c], ssum);
+      }
+    }
+  }
+}
+
 void launch_softmax(const SoftmaxParams& p, cudaStream_t s) {
   if (p.rows <= 0) return;
-  if (p.len <= 1024) {
+  // float4 rows: contiguous axis, length a multiple of 4, every row 16-byte aligned
+  bool vec = p.in_axis_st == 1 && p.out_axis_st == 1 && p.len % 4 == 0 &&
+             (reinterpret_cast<uintptr_t>(p.in) & 15) == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
+  for (int d = 0; d < p.rank && vec; ++d) vec = p.in_row_st[d] % 4 == 0 && p.out_row_st[d] % 4 == 0;
+  if (p.len <= 128) {
+    softmax_reg_kernel<4><<<grid_for(p.rows, kThreads / 32), kThreads, 0, s>>>(p, vec);
+  } else if (p.len <= 512) {
+    softmax_reg_kernel<16><<<grid_for(p.rows, kThreads / 32), kThreads, 0, s>>>(p, vec);
+  } else if (p.len <= 1024) {
     softmax_kernel<1><<<grid_for(p.rows, kThreads / 32), kThreads, 0, s>>>(p);
   } else {
     softmax_kernel<8><<<grid_for(p.rows, 1), kThreads, 0, s>>>(p);

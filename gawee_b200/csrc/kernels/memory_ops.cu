@@ -786,9 +786,77 @@ __global__ void __launch_bounds__(kThreads) pack_b_kernel(const __grid_constant_
   }
 }
 
+// Four consecutive k of one (b, n) row per thread, 32-bit indices: the row's
+// source offset is found once per four outputs, a single k dimension needs no
+// division, contiguous k loads as a float4, and both planes store float4s
+// (ldk is a multiple of 4).  Same values as pack_b_kernel.
+__global__ void __launch_bounds__(kThreads) pack_b4_kernel(const __grid_constant__ PackBParams p, bool vec_src) {
+  const uint32_t q4 = (uint32_t)(p.ldk / 4), N = (uint32_t)p.N, K = (uint32_t)p.K;
+  const uint32_t total = (uint32_t)(p.batch * p.N) * q4;
+  for (uint32_t u = blockIdx.x * blockDim.x + threadIdx.x; u < total; u += gridDim.x * blockDim.x) {
+    const uint32_t row = u / q4;
+    const uint32_t k0 = (u - row * q4) * 4;
+    const uint32_t b = row / N, n = row - b * N;
+    int64_t base = (int64_t)n * p.sn;
+    uint32_t rem = b;
+    for (int d = p.batch_rank - 1; d >= 0; --d) {
+      const uint32_t sh = (uint32_t)p.batch_shape[d];
+      const uint32_t qq = rem / sh;
+      base += (int64_t)(rem - qq * sh) * p.batch_st[d];
+      rem = qq;
+    }
+    float x[4] = {0.f, 0.f, 0.f, 0.f};
+    if (vec_src && k0 + 4 <= K) {
+      const float4 t = *reinterpret_cast<const float4*>(p.src + base + k0);
+      x[0] = t.x; x[1] = t.y; x[2] = t.z; x[3] = t.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t k = k0 + e;
+        if (k >= K) continue;
+        if (p.k_rank == 1) {
+          if (k < (uint32_t)p.k_valid[0]) x[e] = p.src[base + (int64_t)k * p.k_st[0]];
+        } else {
+          int64_t off = base;
+          bool valid = true;
+          uint32_t r = k;
+          for (int d = p.k_rank - 1; d >= 0; --d) {
+            const uint32_t sh = (uint32_t)p.k_shape[d];
+            const uint32_t qq = r / sh;
+            const uint32_t c = r - qq * sh;
+            r = qq;
+            if (c >= (uint32_t)p.k_valid[d]) valid = false;
+            off += (int64_t)c * p.k_st[d];
+          }
+          if (valid) x[e] = p.src[off];
+        }
+      }
+    }
+    float h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      h[e] = __uint_as_float(__float_as_uint(x[e]) & 0xffffe000u);
+      l[e] = __fsub_rn(x[e], h[e]);
+    }
+    const int64_t i = (int64_t)u * 4;
+    *reinterpret_cast<float4*>(p.hi + i) = make_float4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<float4*>(p.lo + i) = make_float4(l[0], l[1], l[2], l[3]);
+  }
+}
+
 void launch_pack_b(const PackBParams& p, cudaStream_t s) {
   const int64_t total = p.batch * p.N * p.ldk;
   if (total <= 0) return;
+  const bool fits = total / 4 < (int64_t(1) << 31) && p.batch * p.N < (int64_t(1) << 31) && p.ldk % 4 == 0 &&
+                    (reinterpret_cast<uintptr_t>(p.hi) & 15) == 0 && (reinterpret_cast<uintptr_t>(p.lo) & 15) == 0;
+  if (fits) {
+    // k contiguous in the source, whole float4s valid, rows and batches 16-byte aligned
+    bool vec = p.k_rank == 1 && p.k_st[0] == 1 && p.k_valid[0] >= p.K && p.sn % 4 == 0 &&
+               (reinterpret_cast<uintptr_t>(p.src) & 15) == 0;
+    for (int d = 0; d < p.batch_rank && vec; ++d) vec = p.batch_st[d] % 4 == 0;
+    pack_b4_kernel<<<grid_for(total / 4), kThreads, 0, s>>>(p, vec);
+    return;
+  }
   pack_b_kernel<<<grid_for(total), kThreads, 0, s>>>(p);
 }
 

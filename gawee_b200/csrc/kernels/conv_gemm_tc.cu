@@ -706,6 +706,71 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           continue;
         }
       }
+      if (EPI == EPI_FAST && p.fast != FAST_SIGMOID_MUL) {
+        // One aux operand (residual, mask): each thread loads its row's aux
+        // values one 16-column chunk ahead, computes the chunk, and the warp
+        // stores it through the shared-memory transpose (8 rows x 64 bytes
+        // per store instruction instead of 32 rows x 16 bytes).
+        int64_t abase = 0;
+        {
+          uint32_t rem = (uint32_t)z;
+          for (int d = p.batch_rank - 1; d >= 0; --d) {
+            const uint32_t sh = (uint32_t)p.batch_shape[d];
+            const uint32_t qq = rem / sh;
+            abase += (int64_t)(rem - qq * sh) * p.aux_sb[0][d];
+            rem = qq;
+          }
+        }
+        const int nb0 = n0 + cbase;
+        const bool coal = p.ldc_n == 1 && (p.ldc & 3) == 0 && (c_off & 3) == 0 &&
+                          (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 && p.aux_sn[0] == 1 &&
+                          (p.aux_sm[0] & 3) == 0 && ((reinterpret_cast<uintptr_t>(p.aux[0] + abase) & 15) == 0) &&
+                          p.bias == nullptr && nb0 + HB <= p.N;
+        if (coal && __all_sync(0xffffffffu, ok)) {
+          float* stage = reinterpret_cast<float*>(smem + L::kStageOff) + (warp - 6) * kStageWarpFloats;
+          const int64_t m = m0 + row;
+          const bool mrow = m < p.M;
+          const float* arow = p.aux[0] + abase + (mrow ? m : 0) * p.aux_sm[0] + nb0;
+          float4 an[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) an[j] = mrow ? __ldg(reinterpret_cast<const float4*>(arow) + j) : make_float4(0, 0, 0, 0);
+          const int c4 = lane & 3;
+#pragma unroll
+          for (int c0 = 0; c0 < HB; c0 += 16) {
+            float a[16];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              a[4 * j] = an[j].x; a[4 * j + 1] = an[j].y; a[4 * j + 2] = an[j].z; a[4 * j + 3] = an[j].w;
+            }
+            if (c0 + 16 < HB) {  // next chunk's aux, in flight while this one is finished
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                an[j] = mrow ? __ldg(reinterpret_cast<const float4*>(arow + c0 + 16) + j) : make_float4(0, 0, 0, 0);
+            }
+            float o[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float x = acc[c0 + j];
+              if (p.fast == FAST_ADD) o[j] = __fadd_rn(x, a[j]);
+              else if (p.fast == FAST_DIVC_ADD) o[j] = __fadd_rn(__fdiv_rn(x, p.fast_c), a[j]);
+              else o[j] = __fadd_rn(__fmul_rn(x, p.fast_c), a[j]);
+            }
+            float* srow = stage + lane * kStagePitch;
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4*>(srow + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
+            __syncwarp();
+#pragma unroll
+            for (int it = 0; it < 4; ++it) {
+              const int r = it * 8 + (lane >> 2);
+              const int64_t mm = m0 + q * 32 + r;
+              const float4 v = *reinterpret_cast<const float4*>(stage + r * kStagePitch + c4 * 4);
+              if (mm < p.M) *reinterpret_cast<float4*>(p.out + c_off + mm * p.ldc + nb0 + c0 + c4 * 4) = v;
+            }
+            __syncwarp();
+          }
+          continue;
+        }
+      }
       const int64_t m = m0 + row;
       if (!ok || m >= p.M) continue;
       float* crow = p.out + c_off + m * p.ldc;

@@ -706,18 +706,20 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           continue;
         }
       }
-      if (EPI == EPI_FAST && p.fast != FAST_SIGMOID_MUL) {
-        // One aux operand (residual, mask): each thread loads its row's aux
-        // values one 16-column chunk ahead, computes the chunk, and the warp
-        // stores it through the shared-memory transpose (8 rows x 64 bytes
-        // per store instruction instead of 32 rows x 16 bytes).
-        int64_t abase = 0;
+      if (EPI == EPI_FAST) {
+        // Recognised programs: each thread loads its row's aux values (one
+        // 16-column chunk ahead when there is a single aux operand), computes
+        // the chunk, and the warp stores it through the shared-memory
+        // transpose (8 rows x 64 bytes per store instead of 32 rows x 16 bytes).
+        const bool two = p.fast == FAST_SIGMOID_MUL;
+        int64_t abase = 0, abase1 = 0;
         {
           uint32_t rem = (uint32_t)z;
           for (int d = p.batch_rank - 1; d >= 0; --d) {
             const uint32_t sh = (uint32_t)p.batch_shape[d];
             const uint32_t qq = rem / sh;
             abase += (int64_t)(rem - qq * sh) * p.aux_sb[0][d];
+            if (two) abase1 += (int64_t)(rem - qq * sh) * p.aux_sb[1][d];
             rem = qq;
           }
         }
@@ -725,12 +727,15 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         const bool coal = p.ldc_n == 1 && (p.ldc & 3) == 0 && (c_off & 3) == 0 &&
                           (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 && p.aux_sn[0] == 1 &&
                           (p.aux_sm[0] & 3) == 0 && ((reinterpret_cast<uintptr_t>(p.aux[0] + abase) & 15) == 0) &&
-                          p.bias == nullptr && nb0 + HB <= p.N;
+                          p.bias == nullptr && nb0 + HB <= p.N &&
+                          (!two || (p.aux_sn[1] == 1 && (p.aux_sm[1] & 3) == 0 &&
+                                    ((reinterpret_cast<uintptr_t>(p.aux[1] + abase1) & 15) == 0)));
         if (coal && __all_sync(0xffffffffu, ok)) {
           float* stage = reinterpret_cast<float*>(smem + L::kStageOff) + (warp - 6) * kStageWarpFloats;
           const int64_t m = m0 + row;
           const bool mrow = m < p.M;
           const float* arow = p.aux[0] + abase + (mrow ? m : 0) * p.aux_sm[0] + nb0;
+          const float* arow1 = two ? p.aux[1] + abase1 + (mrow ? m : 0) * p.aux_sm[1] + nb0 : arow;
           float4 an[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) an[j] = mrow ? __ldg(reinterpret_cast<const float4*>(arow) + j) : make_float4(0, 0, 0, 0);
@@ -742,18 +747,37 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             for (int j = 0; j < 4; ++j) {
               a[4 * j] = an[j].x; a[4 * j + 1] = an[j].y; a[4 * j + 2] = an[j].z; a[4 * j + 3] = an[j].w;
             }
-            if (c0 + 16 < HB) {  // next chunk's aux, in flight while this one is finished
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                an[j] = mrow ? __ldg(reinterpret_cast<const float4*>(arow + c0 + 16) + j) : make_float4(0, 0, 0, 0);
-            }
             float o[16];
+            if (two) {  // this chunk's second operand now; no prefetch (registers)
+              float b1[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const float x = acc[c0 + j];
-              if (p.fast == FAST_ADD) o[j] = __fadd_rn(x, a[j]);
-              else if (p.fast == FAST_DIVC_ADD) o[j] = __fadd_rn(__fdiv_rn(x, p.fast_c), a[j]);
-              else o[j] = __fadd_rn(__fmul_rn(x, p.fast_c), a[j]);
+              for (int j = 0; j < 4; ++j) {
+                const float4 t = mrow ? __ldg(reinterpret_cast<const float4*>(arow1 + c0) + j) : make_float4(0, 0, 0, 0);
+                b1[4 * j] = t.x; b1[4 * j + 1] = t.y; b1[4 * j + 2] = t.z; b1[4 * j + 3] = t.w;
+              }
+              if (c0 + 16 < HB) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                  an[j] = mrow ? __ldg(reinterpret_cast<const float4*>(arow + c0 + 16) + j) : make_float4(0, 0, 0, 0);
+              }
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-b1[j])));
+                o[j] = __fmul_rn(__fmul_rn(a[j], sg), acc[c0 + j]);
+              }
+            } else {
+              if (c0 + 16 < HB) {  // next chunk's aux, in flight while this one is finished
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                  an[j] = mrow ? __ldg(reinterpret_cast<const float4*>(arow + c0 + 16) + j) : make_float4(0, 0, 0, 0);
+              }
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const float x = acc[c0 + j];
+                if (p.fast == FAST_ADD) o[j] = __fadd_rn(x, a[j]);
+                else if (p.fast == FAST_DIVC_ADD) o[j] = __fadd_rn(__fdiv_rn(x, p.fast_c), a[j]);
+                else o[j] = __fadd_rn(__fmul_rn(x, p.fast_c), a[j]);
+              }
             }
             float* srow = stage + lane * kStagePitch;
 #pragma unroll

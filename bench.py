@@ -162,9 +162,10 @@ def run_reference(a):
     sample = (f"each step: a batch-1 slice of the {a.workload} workload on the C++ oracle "
               f"(the reference's lowering semantics; its own MLIR/LLVM AOT toolchain is absent), {threads} threads")
     line = {"metric": metric, "value": value, "unit": unit, "impl": "reference", "n_gpus": a.gpus, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": dt / a.steps * 1e3, "higher_is_better": True, "scaling": "strong",
+            "warmup": a.warmup, "ms_per_step": dt / a.steps * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": a.workload, "batch_per_step": 1},
+            "config": {"workload": a.workload, "global_batch": total,
+                       "sample_per_step": "a batch-1 slice; throughput extrapolates linearly over the batch"},
             "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)

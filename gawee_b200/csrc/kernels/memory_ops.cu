@@ -142,24 +142,30 @@ __global__ void __launch_bounds__(kThreads) elementwise_dense4_kernel(const __gr
 // consecutive elements of one row (coordinates unravelled once per run),
 // loads each operand as a float4 when its inner stride is 1 (and aligned),
 // broadcasts it when the stride is 0, and stores a float4.
+// Idx: type of the run index and coordinates (32-bit when the iteration
+// space has < 2^31 elements: its divisions cost a fraction of 64-bit ones).
+template <typename Idx>
 __global__ void __launch_bounds__(kThreads) elementwise_rows4_kernel(const __grid_constant__ EwParams p,
                                                                      unsigned vec_mask, unsigned bcast_mask,
                                                                      int64_t rows, int64_t cols) {
   Reg regs[kMaxRegs];
   int err = 0;
-  const int64_t runs_per_row = (cols + 3) / 4;
-  const int64_t runs = rows * runs_per_row;
+  const Idx runs_per_row = (Idx)((cols + 3) / 4);
+  const Idx runs = (Idx)rows * runs_per_row;
   const int inner = p.rank - 1;
-  for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < runs; u += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = u / runs_per_row;
-    const int64_t c0 = (u - row * runs_per_row) * 4;
-    int64_t rem = row, off_out = 0;
+  for (Idx u = blockIdx.x * (Idx)blockDim.x + threadIdx.x; u < runs; u += (Idx)gridDim.x * blockDim.x) {
+    const Idx row = u / runs_per_row;
+    const int64_t c0 = (int64_t)(u - row * runs_per_row) * 4;
+    Idx rem = row;
+    int64_t off_out = 0;
     int64_t off_in[kMaxIn];
 #pragma unroll
     for (int k = 0; k < kMaxIn; ++k) off_in[k] = 0;
     for (int d = inner - 1; d >= 0; --d) {
-      const int64_t c = rem % p.shape[d];
-      rem /= p.shape[d];
+      const Idx sh = (Idx)p.shape[d];
+      const Idx qq = rem / sh;
+      const int64_t c = (int64_t)(rem - qq * sh);
+      rem = qq;
       off_out += c * p.out.st[d];
 #pragma unroll
       for (int k = 0; k < kMaxIn; ++k)
@@ -235,7 +241,10 @@ void launch_elementwise(const EwParams& p, cudaStream_t s) {
     if (ok && cols >= 4) {
       const int64_t rows = p.numel / cols;
       const int64_t runs = rows * ((cols + 3) / 4);
-      elementwise_rows4_kernel<<<grid_for(runs), kThreads, 0, s>>>(p, vec_mask, bcast_mask, rows, cols);
+      if (p.numel < (int64_t(1) << 31))
+        elementwise_rows4_kernel<uint32_t><<<grid_for(runs), kThreads, 0, s>>>(p, vec_mask, bcast_mask, rows, cols);
+      else
+        elementwise_rows4_kernel<int64_t><<<grid_for(runs), kThreads, 0, s>>>(p, vec_mask, bcast_mask, rows, cols);
       return;
     }
   }

@@ -35,6 +35,33 @@ def test_resnet18_b2_small_image():
     _check(synth.resnet18(2, image=96))
 
 
+def test_resnet18_full_batch_rows_match_oracle():
+    """The bench workload at its full size: ResNet-18, batch 256 of 3x224x224.
+    Batch rows are independent, so rows of the full-batch GPU forward (two
+    runs: eager, then the replayed CUDA graph) must match the oracle's
+    forward of those single images with the same weights; the first, a
+    middle and the last row are checked at the reference ResNet tolerance."""
+    import os
+
+    import oracle
+    from gawee_b200.runtime import Model
+
+    big = synth.resnet18(256)
+    args = big.make_args()
+    m = Model(big.mlir)
+    try:
+        got = [m.run(args)[0] for _ in range(2)]
+    finally:
+        m.close()
+    one = synth.resnet18(1)  # same weights: they do not depend on the batch size
+    o = oracle.Oracle(one.mlir)
+    for r in (0, 129, 255):
+        a1 = [np.ascontiguousarray(args[0][r:r + 1])] + list(args[1:])
+        want = o.run(a1, threads=os.cpu_count() or 1)[0]
+        for k, g in enumerate(got):
+            compare(g[r:r + 1], want, big.atol, 1e-4, f"resnet18 b256 row {r} run {k}")
+
+
 def test_bert_tiny_s128():
     _check(synth.bert_tiny())
 

@@ -29,6 +29,7 @@ MLIR/LLVM toolchain is not available, so its AOT binary cannot be built).
 from __future__ import annotations
 
 import argparse
+import atexit
 import json
 import os
 import statistics
@@ -73,12 +74,24 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """nvidia-smi clock / throttle sampling during the timed regions.
+
+    nvidia-smi is started and its first row awaited before the region opens
+    (that row, taken right after the warm-up, is dropped), so a timed region
+    of a few hundred milliseconds still gets samples at the 100 ms period."""
 
     def __init__(self, gpu: int):
         self.gpu = gpu
         self.proc = None
+        self.skip = 0
         self.path = os.path.join("/tmp", f"gawee_clocks_{os.getpid()}.csv")
+
+    def _rows(self):
+        try:
+            with open(self.path) as f:
+                return [ln for ln in f if ln.strip()]
+        except OSError:
+            return []
 
     def __enter__(self):
         try:
@@ -86,25 +99,32 @@ class ClockSampler:
                 ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=clocks.sm,clocks.max.sm,power.draw,"
                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return self
+        atexit.register(self.__exit__, None, None, None)
+        t0 = time.perf_counter()
+        while not self._rows() and time.perf_counter() - t0 < 10.0 and self.proc.poll() is None:
+            time.sleep(0.01)
+        self.skip = len(self._rows())
         return self
 
     def __exit__(self, *a):
         if self.proc:
-            self.proc.terminate()
+            proc, self.proc = self.proc, None
+            proc.terminate()
             try:
-                self.proc.wait(5)
+                proc.wait(5)
             except Exception:
-                self.proc.kill()
+                proc.kill()
 
     def summary(self):
         if not os.path.exists(self.path):
             return None
         rows = []
-        for line in open(self.path):
+        for line in self._rows()[self.skip:]:
             parts = [x.strip() for x in line.split(",")]
             if len(parts) < 7:
                 continue
@@ -243,10 +263,9 @@ def main():
             ms = float(t.item())
         return ms
 
-    with ClockSampler(local) as clk:
-        ms = timed(step, a.steps)
+    clk = ClockSampler(local).__enter__()
+    ms = timed(step, a.steps)
     m.synchronize(sp)
-    clocks = clk.summary()
     value = total_batch * items * a.steps / (ms / 1e3)
 
     # End to end through the C ABI, every step: the step's input from pinned
@@ -304,6 +323,8 @@ def main():
     e1.record(down)                              # after the last step's download
     torch.cuda.synchronize(local)
     ms_e2e = e0.elapsed_time(e1)
+    clk.__exit__(None, None, None)
+    clocks = clk.summary()
     if world > 1:
         t = torch.tensor([ms_e2e], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

@@ -26,6 +26,22 @@ int sm_count() {
   return n;
 }
 
+// One wave of the blocks that fit on the SMs at once (a grid-stride kernel
+// then has no partial last wave), or fewer when the work is smaller.
+template <auto Kernel>
+unsigned resident_grid(int64_t work) {
+  static const int per_sm = [] {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, Kernel, kThreads, 0) != cudaSuccess || n < 1) n = 1;
+    return n;
+  }();
+  int64_t g = (work + kThreads - 1) / kThreads;
+  const int64_t cap = (int64_t)sm_count() * per_sm;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return (unsigned)g;
+}
+
 unsigned grid_for(int64_t work, int per_block = kThreads, int waves = 8) {
   int64_t g = (work + per_block - 1) / per_block;
   int64_t cap = (int64_t)sm_count() * waves;
@@ -653,6 +669,23 @@ __global__ void __launch_bounds__(kThreads) pool_kernel(const __grid_constant__ 
 // its divisions cost a fraction of 64-bit ones).
 // KW > 0 fixes the window at compile time (KW x KW), so the window's loads are
 // all issued before the first is used.
+// arith.maximumf in one instruction: max.NaN.f32 (PTX ISA 7.0+, sm_80+)
+// returns NaN when either input is NaN and orders -0 < +0.  Its NaN is
+// canonicalised per output (nan_canon_) to the 0x7fc00000 that maximumf_
+// returns, so the pool results keep the same bits.
+__device__ __forceinline__ float max_nan_(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float nan_canon_(float x) { return isnan(x) ? __int_as_float(0x7fc00000) : x; }
+__device__ __forceinline__ float4 max_nan4_(float4 a, float4 b) {
+  return make_float4(max_nan_(a.x, b.x), max_nan_(a.y, b.y), max_nan_(a.z, b.z), max_nan_(a.w, b.w));
+}
+__device__ __forceinline__ float4 nan_canon4_(float4 a) {
+  return make_float4(nan_canon_(a.x), nan_canon_(a.y), nan_canon_(a.z), nan_canon_(a.w));
+}
+
 template <typename Idx, int KW>
 __global__ void __launch_bounds__(kThreads) pool_nhwc4_kernel(const __grid_constant__ PoolParams p) {
   const Idx cg = (Idx)(p.C / 4);
@@ -679,19 +712,88 @@ __global__ void __launch_bounds__(kThreads) pool_nhwc4_kernel(const __grid_const
         if (in) v = __ldg(reinterpret_cast<const float4*>(base + ih * p.in_st[2] + iw * p.in_st[3]));
         else v = p.mode == 0 ? make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY) : make_float4(0.f, 0.f, 0.f, 0.f);
         if (p.mode == 0) {
-          acc.x = maximumf_(acc.x, v.x); acc.y = maximumf_(acc.y, v.y);
-          acc.z = maximumf_(acc.z, v.z); acc.w = maximumf_(acc.w, v.w);
+          acc = max_nan4_(acc, v);
         } else {
           acc.x = __fadd_rn(acc.x, v.x); acc.y = __fadd_rn(acc.y, v.y);
           acc.z = __fadd_rn(acc.z, v.z); acc.w = __fadd_rn(acc.w, v.w);
         }
       }
     }
+    if (p.mode == 0) acc = nan_canon4_(acc);
     if (p.mode == 1) {
       acc.x = __fdiv_rn(acc.x, p.count); acc.y = __fdiv_rn(acc.y, p.count);
       acc.z = __fdiv_rn(acc.z, p.count); acc.w = __fdiv_rn(acc.w, p.count);
     }
     *reinterpret_cast<float4*>(p.out + n * p.out_st[0] + (int64_t)oh * p.out_st[2] + (int64_t)ow * p.out_st[3] + g * 4) = acc;
+  }
+}
+
+// 3x3 window, stride 2, dilation 1 (the ResNet stem pool), dense NHWC,
+// C % 4 == 0: one thread per 4 channels of a 2x2 block of outputs, which
+// share a 5x5 input patch (25 loads instead of 36).  Each output still folds
+// its window in (kh, kw) order with the same padding values.
+__global__ void __launch_bounds__(kThreads) pool_nhwc4_3x3s2_kernel(const __grid_constant__ PoolParams p) {
+  const uint32_t cg = (uint32_t)(p.C / 4);
+  const uint32_t OW = (uint32_t)p.OW, OH = (uint32_t)p.OH;
+  const uint32_t OW2 = (OW + 1) / 2, OH2 = (OH + 1) / 2;
+  const uint32_t total = (uint32_t)p.N * OH2 * OW2 * cg;
+  const float pad = p.mode == 0 ? -INFINITY : 0.f;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const uint32_t g = i % cg;
+    uint32_t r = i / cg;
+    const uint32_t ow2 = r % OW2;
+    r /= OW2;
+    const uint32_t oh2 = r % OH2;
+    const int64_t n = r / OH2;
+    const int oh = 2 * (int)oh2, ow = 2 * (int)ow2;
+    const float* base = p.in + n * p.in_st[0] + g * 4;
+    float4 acc[2][2];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int b = 0; b < 2; ++b) acc[a][b] = make_float4(pad, pad, pad, pad);
+#pragma unroll
+    for (int dy = 0; dy < 5; ++dy) {
+      const int ih = oh * 2 - p.ph + dy;
+#pragma unroll
+      for (int dx = 0; dx < 5; ++dx) {
+        const int iw = ow * 2 - p.pw + dx;
+        float4 v = make_float4(pad, pad, pad, pad);
+        if (ih >= 0 && ih < p.H && iw >= 0 && iw < p.W)
+          v = __ldg(reinterpret_cast<const float4*>(base + ih * p.in_st[2] + iw * p.in_st[3]));
+#pragma unroll
+        for (int a = 0; a < 2; ++a) {
+          const int kh = dy - 2 * a;
+          if (kh < 0 || kh > 2) continue;
+#pragma unroll
+          for (int b = 0; b < 2; ++b) {
+            const int kw = dx - 2 * b;
+            if (kw < 0 || kw > 2) continue;
+            float4& o = acc[a][b];
+            if (p.mode == 0) {
+              o = max_nan4_(o, v);
+            } else {
+              o.x = __fadd_rn(o.x, v.x); o.y = __fadd_rn(o.y, v.y);
+              o.z = __fadd_rn(o.z, v.z); o.w = __fadd_rn(o.w, v.w);
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int b = 0; b < 2; ++b) {
+        if ((uint32_t)(oh + a) >= OH || (uint32_t)(ow + b) >= OW) continue;
+        float4 o = acc[a][b];
+        if (p.mode == 0) o = nan_canon4_(o);
+        if (p.mode == 1) {
+          o.x = __fdiv_rn(o.x, p.count); o.y = __fdiv_rn(o.y, p.count);
+          o.z = __fdiv_rn(o.z, p.count); o.w = __fdiv_rn(o.w, p.count);
+        }
+        *reinterpret_cast<float4*>(p.out + n * p.out_st[0] + (int64_t)(oh + a) * p.out_st[2] +
+                                   (int64_t)(ow + b) * p.out_st[3] + g * 4) = o;
+      }
   }
 }
 
@@ -703,7 +805,9 @@ void launch_pool(const PoolParams& p, cudaStream_t s) {
                      p.out_st[0] % 4 == 0 && (reinterpret_cast<uintptr_t>(p.in) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
   const bool small = total / 4 < (int64_t(1) << 31);
-  if (nhwc4 && small && p.kh == 3 && p.kw == 3)
+  if (nhwc4 && small && p.kh == 3 && p.kw == 3 && p.sh == 2 && p.sw == 2 && p.dh == 1 && p.dw == 1)
+    pool_nhwc4_3x3s2_kernel<<<resident_grid<pool_nhwc4_3x3s2_kernel>(total / 16 + 1), kThreads, 0, s>>>(p);
+  else if (nhwc4 && small && p.kh == 3 && p.kw == 3)
     pool_nhwc4_kernel<uint32_t, 3><<<grid_for(total / 4), kThreads, 0, s>>>(p);
   else if (nhwc4 && small) pool_nhwc4_kernel<uint32_t, 0><<<grid_for(total / 4), kThreads, 0, s>>>(p);
   else if (nhwc4) pool_nhwc4_kernel<int64_t, 0><<<grid_for(total / 4), kThreads, 0, s>>>(p);

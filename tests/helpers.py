@@ -44,11 +44,12 @@ def compare(got: np.ndarray, want: np.ndarray, atol: float, rtol: float, what: s
         g64, w64 = got[ok].astype(np.float64), want[ok].astype(np.float64)
         with np.errstate(invalid="ignore"):
             diff = np.where(g64 == w64, 0.0, np.abs(g64 - w64))
-        bound = atol + rtol * np.abs(w64)
+            bound = atol + rtol * np.abs(w64)  # NaN for an infinite want with rtol 0: equality decides there
+            within = (g64 == w64) | (diff <= bound)
         if diff.size:
-            k = int(np.argmax(diff - bound))
-            assert np.all(diff <= bound), (f"{what}: max_abs_diff={diff.max():.3e} worst at flat {k}: "
-                                           f"got {got[ok].ravel()[k]!r} want {want[ok].ravel()[k]!r}")
+            k = int(np.argmin(within))
+            assert np.all(within), (f"{what}: max_abs_diff={diff.max():.3e} worst at flat {k}: "
+                                    f"got {got[ok].ravel()[k]!r} want {want[ok].ravel()[k]!r}")
         return float(diff.max()) if diff.size else 0.0
     assert np.array_equal(got, want), f"{what}: integer/bool outputs differ at {np.argwhere(got != want)[:5]}"
     return 0.0

@@ -178,6 +178,57 @@ def test_pools():
     parity(*build(g_), atol=1e-6, rtol=1e-6)
 
 
+def test_pools_channels_last():
+    """Pools over a convolution's output, which the plan keeps channels-last,
+    with C % 4 == 0: the float4 kernels, including the 3x3 stride-2 one that
+    computes 2x2 output blocks, here with odd output extents (ragged blocks)
+    and with and without padding."""
+    def g_(g):
+        x = rand_input(g, (2, 3, 15, 13), 72)
+        wt = rand_input(g, (8, 3, 3, 3), 73, scale=0.3)
+        b = rand_input(g, (8,), 74, scale=0.1)
+        y = g.op("conv", [x, wt, b], {"strides": _arr([1, 1]), "padding": _arr([1, 1]), "dilation": _arr([1, 1])},
+                 F, (2, 8, 15, 13))
+        mp = g.op("max_pool", [y], {"kernelSize": _arr([3, 3]), "strides": _arr([2, 2]), "padding": _arr([1, 1]),
+                                    "dilation": _arr([1, 1]), "ceilMode": "false"}, F, (2, 8, 8, 7))
+        m0 = g.op("max_pool", [y], {"kernelSize": _arr([3, 3]), "strides": _arr([2, 2]), "padding": _arr([0, 0]),
+                                    "dilation": _arr([1, 1]), "ceilMode": "false"}, F, (2, 8, 7, 6))
+        ap = g.op("average_pool", [y], {"kernelSize": _arr([3, 3]), "strides": _arr([2, 2]), "padding": _arr([1, 1]),
+                                        "ceilMode": "false", "countIncludePad": "true"}, F, (2, 8, 8, 7))
+        m1 = g.op("max_pool", [y], {"kernelSize": _arr([3, 3]), "strides": _arr([1, 1]), "padding": _arr([1, 1]),
+                                    "dilation": _arr([1, 1]), "ceilMode": "false"}, F, (2, 8, 15, 13))
+        return [mp, m0, ap, m1]
+    parity(*build(g_), atol=1e-6, rtol=1e-6)
+
+
+def test_max_pool_signed_zero_and_nan_bits():
+    """max_pool folds with arith.maximumf (GaweeToLinalg.cpp:565-706): NaN
+    propagates and -0 < +0.  A channels-last input (an NHWC argument seen
+    through a transpose view) holding mostly signed zeros, negatives, infs
+    and a few NaNs; every non-NaN output must match the oracle bit for bit
+    (the sign of zero included) and NaNs must sit in the same places."""
+    rng = np.random.default_rng(91)
+    vals = np.array([-0.0, 0.0, -1.0, -2.0, np.nan, -np.inf, np.inf], np.float32)
+    p_lo = [0.55, 0.05, 0.2, 0.18, 0.01, 0.01, 0.0]   # channels 0-3: windows of only -0 and negatives
+    p_hi = [0.3, 0.3, 0.15, 0.15, 0.03, 0.04, 0.03]   # channels 4-7
+    x = np.concatenate([rng.choice(vals, (2, 9, 11, 4), p=p_lo), rng.choice(vals, (2, 9, 11, 4), p=p_hi)], axis=3)
+
+    def g_(g):
+        xi = g.input(F, (2, 9, 11, 8), lambda: x.astype(np.float32))
+        xt = g.transpose(xi, [0, 3, 1, 2])
+        outs = []
+        for pad, (oh, ow), st in (((1, 1), (5, 6), 2), ((0, 0), (4, 5), 2), ((1, 1), (9, 11), 1)):
+            outs.append(g.op("max_pool", [xt], {"kernelSize": _arr([3, 3]), "strides": _arr([st, st]),
+                                                "padding": _arr(list(pad)), "dilation": _arr([1, 1]),
+                                                "ceilMode": "false"}, F, (2, 8, oh, ow)))
+        return outs
+    got, want = parity(*build(g_), atol=0, rtol=0)
+    for k, (a, b) in enumerate(zip(got, want)):
+        ok = ~np.isnan(b)
+        assert np.array_equal(a[ok].view(np.uint32), b[ok].view(np.uint32)), f"output{k}: bits differ"
+        assert np.any(b[ok].view(np.uint32) == 0x80000000), f"output{k}: no -0 window in the case"
+
+
 def test_range_shape_topk():
     def g_(g):
         r1 = g.range_(3, 40, 4)

@@ -314,9 +314,36 @@ __global__ void __launch_bounds__(kThreads) reduce_f32_kernel(const __grid_const
   }
 }
 
+// Rows that sit next to each other in memory while each row's elements are
+// strided (a spatial mean over channels-last data): one thread per row, so
+// the lanes of a warp read adjacent rows and every load is coalesced.  Each
+// row is summed sequentially from 0 in row-major order over the reduced
+// dimensions, the order of the reference's loop.
+__global__ void __launch_bounds__(kThreads) reduce_f32_strided_kernel(const __grid_constant__ ReduceParams p) {
+  const int64_t n0 = p.red_shape[0], s0 = p.red_st[0];
+  const int64_t n1 = p.red_rank == 2 ? p.red_shape[1] : 1, s1 = p.red_rank == 2 ? p.red_st[1] : 0;
+  for (int64_t row = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; row < p.rows;
+       row += (int64_t)gridDim.x * blockDim.x) {
+    const float* rp = p.in + unravel_off(row, p.kept_rank, p.kept_shape, p.kept_st);
+    float acc = 0.0f;
+    for (int64_t a = 0; a < n0; ++a) {
+      const float* ra = rp + a * s0;
+#pragma unroll 7
+      for (int64_t b = 0; b < n1; ++b) acc = __fadd_rn(acc, __ldg(ra + b * s1));
+    }
+    p.out[unravel_off(row, p.kept_rank, p.kept_shape, p.out_st)] = p.mode == 1 ? __fdiv_rn(acc, p.count) : acc;
+  }
+}
+
 void launch_reduce_f32(const ReduceParams& p, cudaStream_t s) {
   if (p.rows <= 0) return;
-  reduce_f32_kernel<<<grid_for(p.rows, kThreads / 32), kThreads, 0, s>>>(p);
+  const bool strided_rows = p.kept_rank >= 1 && p.kept_st[p.kept_rank - 1] == 1 && p.red_rank >= 1 &&
+                            p.red_rank <= 2 && p.red_st[p.red_rank - 1] != 1 && p.cols <= 4096 &&
+                            p.rows >= 32;
+  if (strided_rows)
+    reduce_f32_strided_kernel<<<grid_for(p.rows), kThreads, 0, s>>>(p);
+  else
+    reduce_f32_kernel<<<grid_for(p.rows, kThreads / 32), kThreads, 0, s>>>(p);
 }
 
 __global__ void __launch_bounds__(kThreads) generic_reduce_kernel(const __grid_constant__ GenericReduceParams p) {

@@ -197,8 +197,25 @@ def test_pools_channels_last():
                                         "ceilMode": "false", "countIncludePad": "true"}, F, (2, 8, 8, 7))
         m1 = g.op("max_pool", [y], {"kernelSize": _arr([3, 3]), "strides": _arr([1, 1]), "padding": _arr([1, 1]),
                                     "dilation": _arr([1, 1]), "ceilMode": "false"}, F, (2, 8, 15, 13))
-        return [mp, m0, ap, m1]
+        gp = g.op("global_average_pool", [y], None, F, (2, 8, 1, 1))
+        return [mp, m0, ap, m1, gp]
     parity(*build(g_), atol=1e-6, rtol=1e-6)
+
+
+def test_global_average_pool_channels_last_bits():
+    """global_average_pool and ad_avg_pool over channels-last data (an NHWC
+    argument seen through a transpose view): one thread per (n, c) row, summed
+    in the reference's order (GaweeToLinalg.cpp:1327-1375: h, then w, from
+    0, then divided by h*w), so the results match the oracle bit for bit."""
+    def g_(g):
+        xi = rand_input(g, (3, 7, 9, 40), 75)
+        xt = g.transpose(xi, [0, 3, 1, 2])
+        gp = g.op("global_average_pool", [xt], None, F, (3, 40, 1, 1))
+        ad = g.op("ad_avg_pool", [xt], {"outputSize": _arr([1, 1])}, F, (3, 40, 1, 1))
+        return [gp, ad]
+    got, want = parity(*build(g_), atol=0, rtol=0)
+    for k, (a, b) in enumerate(zip(got, want)):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), f"output{k}: bits differ"
 
 
 def test_max_pool_signed_zero_and_nan_bits():

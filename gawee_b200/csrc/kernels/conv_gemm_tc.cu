@@ -352,6 +352,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     int ih0[8], iw0[8];
     int kc = 0, kr = 0, ks = 0;
     const int H = (int)p.H, W = (int)p.W, C = (int)p.C;
+    // When C divides kBK (the 7x7 stem's four padded channels), a k-block
+    // moves kBK / C whole filter taps and the channel offset stays put.
+    const int tap_step = (C < kBK && kBK % C == 0) ? kBK / C : 0;
     auto decompose = [&](int k) {
       const int rs = k / C;
       kc = k - rs * C;
@@ -404,6 +407,12 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         } else if (++lka == num_kb) {
           lka = 0;
           decompose(chunk * 4);
+        } else if (tap_step) {
+          ks += tap_step;
+          while (ks >= p.S) {
+            ks -= p.S;
+            ++kr;
+          }
         } else if (C < kBK) {
           decompose(lka * kBK + chunk * 4);  // k crosses several (r, s) positions: divide directly
         } else {

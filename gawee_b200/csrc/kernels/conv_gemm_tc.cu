@@ -758,11 +758,15 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             }
             float o[16];
             if (two) {  // this chunk's second operand now; no prefetch (registers)
-              float b1[16];
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
+              for (int j = 0; j < 4; ++j) {  // four values of the second operand live at a time
                 const float4 t = mrow ? __ldg(reinterpret_cast<const float4*>(arow1 + c0) + j) : make_float4(0, 0, 0, 0);
-                b1[4 * j] = t.x; b1[4 * j + 1] = t.y; b1[4 * j + 2] = t.z; b1[4 * j + 3] = t.w;
+                const float b1[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-b1[e])));
+                  acc[c0 + 4 * j + e] = __fmul_rn(__fmul_rn(a[4 * j + e], sg), acc[c0 + 4 * j + e]);
+                }
               }
               if (c0 + 16 < HB) {
 #pragma unroll
@@ -770,23 +774,25 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                   an[j] = mrow ? __ldg(reinterpret_cast<const float4*>(arow + c0 + 16) + j) : make_float4(0, 0, 0, 0);
               }
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-b1[j])));
-                o[j] = __fmul_rn(__fmul_rn(a[j], sg), acc[c0 + j]);
-              }
+              for (int j = 0; j < 16; ++j) o[j] = acc[c0 + j];
             } else {
-              if (c0 + 16 < HB) {  // next chunk's aux, in flight while this one is finished
+              // computed in place: this chunk's accumulators are not needed
+              // afterwards, and the aux registers are free for the next chunk,
+              // whose loads are then in flight while this one is stored
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const float x = acc[c0 + j];
+                if (p.fast == FAST_ADD) acc[c0 + j] = __fadd_rn(x, a[j]);
+                else if (p.fast == FAST_DIVC_ADD) acc[c0 + j] = __fadd_rn(__fdiv_rn(x, p.fast_c), a[j]);
+                else acc[c0 + j] = __fadd_rn(__fmul_rn(x, p.fast_c), a[j]);
+              }
+              if (c0 + 16 < HB) {
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
                   an[j] = mrow ? __ldg(reinterpret_cast<const float4*>(arow + c0 + 16) + j) : make_float4(0, 0, 0, 0);
               }
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const float x = acc[c0 + j];
-                if (p.fast == FAST_ADD) o[j] = __fadd_rn(x, a[j]);
-                else if (p.fast == FAST_DIVC_ADD) o[j] = __fadd_rn(__fdiv_rn(x, p.fast_c), a[j]);
-                else o[j] = __fadd_rn(__fmul_rn(x, p.fast_c), a[j]);
-              }
+              for (int j = 0; j < 16; ++j) o[j] = acc[c0 + j];
             }
             float* srow = stage + lane * kStagePitch;
 #pragma unroll

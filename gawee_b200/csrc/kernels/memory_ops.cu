@@ -631,11 +631,40 @@ __global__ void __launch_bounds__(kThreads) nchw_to_nhwc4_kernel(const float* __
   }
 }
 
+// C <= 4 (an image input): four consecutive pixels per thread, one float4
+// load per channel plane and four float4 stores (64 contiguous bytes);
+// 32-bit indices.  Strides are in float4 units.
+__global__ void __launch_bounds__(kThreads) nchw_to_nhwc4_px4_kernel(const float4* __restrict__ in,
+                                                                     float4* __restrict__ out, uint32_t N, int C,
+                                                                     uint32_t HW4, uint32_t in_sn4, uint32_t in_sc4) {
+  const uint32_t total = N * HW4;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const uint32_t n = i / HW4, q = i - n * HW4;
+    const float4* src = in + (size_t)n * in_sn4 + q;
+    float4 c[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) c[k] = k < C ? __ldg(src + (size_t)k * in_sc4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float4* dst = out + (size_t)i * 4;
+    dst[0] = make_float4(c[0].x, c[1].x, c[2].x, c[3].x);
+    dst[1] = make_float4(c[0].y, c[1].y, c[2].y, c[3].y);
+    dst[2] = make_float4(c[0].z, c[1].z, c[2].z, c[3].z);
+    dst[3] = make_float4(c[0].w, c[1].w, c[2].w, c[3].w);
+  }
+}
+
 void launch_nchw_to_nhwc4(const float* in, float* out, int64_t N, int C, int C4, int64_t HW, int64_t in_sn,
                           int64_t in_sc, cudaStream_t s) {
   const int64_t total = N * HW * (C4 / 4);
   if (total <= 0) return;
-  nchw_to_nhwc4_kernel<<<grid_for(total), kThreads, 0, s>>>(in, out, N, C, C4, HW, in_sn, in_sc);
+  const bool px4 = C4 == 4 && HW % 4 == 0 && in_sn % 4 == 0 && in_sc % 4 == 0 && in_sn / 4 < (int64_t(1) << 32) &&
+                   in_sc / 4 < (int64_t(1) << 32) && N * HW / 4 < (int64_t(1) << 31) &&
+                   (reinterpret_cast<uintptr_t>(in) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+  if (px4)
+    nchw_to_nhwc4_px4_kernel<<<grid_for(N * HW / 4), kThreads, 0, s>>>(
+        reinterpret_cast<const float4*>(in), reinterpret_cast<float4*>(out), (uint32_t)N, C, (uint32_t)(HW / 4),
+        (uint32_t)(in_sn / 4), (uint32_t)(in_sc / 4));
+  else
+    nchw_to_nhwc4_kernel<<<grid_for(total), kThreads, 0, s>>>(in, out, N, C, C4, HW, in_sn, in_sc);
 }
 
 __global__ void range_kernel(const __grid_constant__ RangeParams p) {

@@ -785,13 +785,15 @@ __global__ void __launch_bounds__(kThreads) pool_nhwc4_kernel(const __grid_const
 }
 
 // 3x3 window, stride 2, dilation 1 (the ResNet stem pool), dense NHWC,
-// C % 4 == 0: one thread per 4 channels of a 2x2 block of outputs, which
-// share a 5x5 input patch (25 loads instead of 36).  Each output still folds
-// its window in (kh, kw) order with the same padding values.
+// C % 4 == 0: one thread per 4 channels of a BH x BW block of outputs, which
+// share a (2BH+1) x (2BW+1) input patch (a 1x2 block: 15 loads instead of
+// 18).  Each output still folds its window in (kh, kw) order with the same
+// padding values.
+template <int BH, int BW>
 __global__ void __launch_bounds__(kThreads) pool_nhwc4_3x3s2_kernel(const __grid_constant__ PoolParams p) {
   const uint32_t cg = (uint32_t)(p.C / 4);
   const uint32_t OW = (uint32_t)p.OW, OH = (uint32_t)p.OH;
-  const uint32_t OW2 = (OW + 1) / 2, OH2 = (OH + 1) / 2;
+  const uint32_t OW2 = (OW + BW - 1) / BW, OH2 = (OH + BH - 1) / BH;
   const uint32_t total = (uint32_t)p.N * OH2 * OW2 * cg;
   const float pad = p.mode == 0 ? -INFINITY : 0.f;
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
@@ -801,28 +803,28 @@ __global__ void __launch_bounds__(kThreads) pool_nhwc4_3x3s2_kernel(const __grid
     r /= OW2;
     const uint32_t oh2 = r % OH2;
     const int64_t n = r / OH2;
-    const int oh = 2 * (int)oh2, ow = 2 * (int)ow2;
+    const int oh = BH * (int)oh2, ow = BW * (int)ow2;
     const float* base = p.in + n * p.in_st[0] + g * 4;
-    float4 acc[2][2];
+    float4 acc[BH][BW];
 #pragma unroll
-    for (int a = 0; a < 2; ++a)
+    for (int a = 0; a < BH; ++a)
 #pragma unroll
-      for (int b = 0; b < 2; ++b) acc[a][b] = make_float4(pad, pad, pad, pad);
+      for (int b = 0; b < BW; ++b) acc[a][b] = make_float4(pad, pad, pad, pad);
 #pragma unroll
-    for (int dy = 0; dy < 5; ++dy) {
+    for (int dy = 0; dy < 2 * BH + 1; ++dy) {
       const int ih = oh * 2 - p.ph + dy;
 #pragma unroll
-      for (int dx = 0; dx < 5; ++dx) {
+      for (int dx = 0; dx < 2 * BW + 1; ++dx) {
         const int iw = ow * 2 - p.pw + dx;
         float4 v = make_float4(pad, pad, pad, pad);
         if (ih >= 0 && ih < p.H && iw >= 0 && iw < p.W)
           v = __ldg(reinterpret_cast<const float4*>(base + ih * p.in_st[2] + iw * p.in_st[3]));
 #pragma unroll
-        for (int a = 0; a < 2; ++a) {
+        for (int a = 0; a < BH; ++a) {
           const int kh = dy - 2 * a;
           if (kh < 0 || kh > 2) continue;
 #pragma unroll
-          for (int b = 0; b < 2; ++b) {
+          for (int b = 0; b < BW; ++b) {
             const int kw = dx - 2 * b;
             if (kw < 0 || kw > 2) continue;
             float4& o = acc[a][b];
@@ -837,9 +839,9 @@ __global__ void __launch_bounds__(kThreads) pool_nhwc4_3x3s2_kernel(const __grid
       }
     }
 #pragma unroll
-    for (int a = 0; a < 2; ++a)
+    for (int a = 0; a < BH; ++a)
 #pragma unroll
-      for (int b = 0; b < 2; ++b) {
+      for (int b = 0; b < BW; ++b) {
         if ((uint32_t)(oh + a) >= OH || (uint32_t)(ow + b) >= OW) continue;
         float4 o = acc[a][b];
         if (p.mode == 0) o = nan_canon4_(o);
@@ -862,7 +864,7 @@ void launch_pool(const PoolParams& p, cudaStream_t s) {
                      (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
   const bool small = total / 4 < (int64_t(1) << 31);
   if (nhwc4 && small && p.kh == 3 && p.kw == 3 && p.sh == 2 && p.sw == 2 && p.dh == 1 && p.dw == 1)
-    pool_nhwc4_3x3s2_kernel<<<resident_grid<pool_nhwc4_3x3s2_kernel>(total / 16 + 1), kThreads, 0, s>>>(p);
+    pool_nhwc4_3x3s2_kernel<1, 2><<<resident_grid<pool_nhwc4_3x3s2_kernel<1, 2>>(total / 8 + 1), kThreads, 0, s>>>(p);
   else if (nhwc4 && small && p.kh == 3 && p.kw == 3)
     pool_nhwc4_kernel<uint32_t, 3><<<grid_for(total / 4), kThreads, 0, s>>>(p);
   else if (nhwc4 && small) pool_nhwc4_kernel<uint32_t, 0><<<grid_for(total / 4), kThreads, 0, s>>>(p);

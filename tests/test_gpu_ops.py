@@ -181,7 +181,7 @@ def test_pools():
 def test_pools_channels_last():
     """Pools over a convolution's output, which the plan keeps channels-last,
     with C % 4 == 0: the float4 kernels, including the 3x3 stride-2 one that
-    computes 2x2 output blocks, here with odd output extents (ragged blocks)
+    computes 1x2 output blocks, here with odd output extents (ragged blocks)
     and with and without padding."""
     def g_(g):
         x = rand_input(g, (2, 3, 15, 13), 72)

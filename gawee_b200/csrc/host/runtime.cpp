@@ -26,6 +26,8 @@
 
 namespace gawee {
 
+int noalloc_take_status(cudaStream_t s);  // noalloc_gemm.cu
+
 struct CudaError : std::runtime_error {
   using std::runtime_error::runtime_error;
 };
@@ -55,6 +57,7 @@ struct NcclApi {
   ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*groupStart)() = nullptr;
   ncclResult_t (*groupEnd)() = nullptr;
+  ncclResult_t (*allGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   const char* (*errorString)(ncclResult_t) = nullptr;
   bool ok = false;
 };
@@ -73,9 +76,10 @@ static NcclApi& nccl() {
     api.recv = (decltype(api.recv))dlsym(h, "ncclRecv");
     api.groupStart = (decltype(api.groupStart))dlsym(h, "ncclGroupStart");
     api.groupEnd = (decltype(api.groupEnd))dlsym(h, "ncclGroupEnd");
+    api.allGather = (decltype(api.allGather))dlsym(h, "ncclAllGather");
     api.errorString = (decltype(api.errorString))dlsym(h, "ncclGetErrorString");
     api.ok = api.getUniqueId && api.commInitRank && api.commDestroy && api.send && api.recv && api.groupStart &&
-             api.groupEnd && api.errorString;
+             api.groupEnd && api.allGather && api.errorString;
   });
   return api;
 }
@@ -104,6 +108,10 @@ struct Runtime {
   std::vector<std::array<TMap, 2>> tmaps;  // per op (TC only)
   ncclComm_t comm = nullptr;
   int world = 1, rank = 0;
+  // output bytes of every rank (rank-major, one entry per output), exchanged
+  // at gawee_dp_init: shards may differ by a row, so rank 0 receives each
+  // peer's own count at the running offset
+  std::vector<int64_t> peer_bytes;
 
   char* ptr(const View& v) const {
     const Buf& b = plan->bufs[v.buf];
@@ -715,6 +723,23 @@ gawee_status guard(gawee_ctx* ctx, F&& f) {
   }
 }
 
+const char* device_status_name(int st) {
+  static const char* names[] = {"ok", "gather index out of range", "tensor-core barrier wait timed out",
+                                "invalid scalar program", "integer division by zero", "slice out of bounds"};
+  return st >= 0 && st < 6 ? names[st] : "error";
+}
+
+// Reads and clears a device status word (after the work that writes it has
+// completed); a non-zero code becomes GAWEE_ERR_DEVICE with its meaning.
+void check_device_status(int* d_status) {
+  int st = 0;
+  GCHECK(cudaMemcpy(&st, d_status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (st) {
+    GCHECK(cudaMemset(d_status, 0, sizeof(int)));
+    throw gawee::StatusError(GAWEE_ERR_DEVICE, std::string("device reported: ") + device_status_name(st));
+  }
+}
+
 cudaStream_t stream_of(gawee_ctx* ctx, void* s) {
   return s ? static_cast<cudaStream_t>(s) : ctx->rt.own_stream;
 }
@@ -862,17 +887,19 @@ gawee_status gawee_output_device_ptr(gawee_ctx* ctx, int i, void** ptr) {
 }
 
 gawee_status gawee_synchronize(gawee_ctx* ctx, void* stream) {
-  if (!ctx) return GAWEE_ERR_INVALID;
+  if (!ctx) {
+    // the allocation-free entry point's status word on the current device
+    const int st = gawee::noalloc_take_status(static_cast<cudaStream_t>(stream));
+    if (st < 0) return GAWEE_ERR_CUDA;
+    if (st > 0) {
+      g_create_error = std::string("device reported: ") + device_status_name(st);
+      return GAWEE_ERR_DEVICE;
+    }
+    return GAWEE_OK;
+  }
   return guard(ctx, [&] {
     GCHECK(cudaStreamSynchronize(stream_of(ctx, stream)));
-    int st = 0;
-    GCHECK(cudaMemcpy(&st, ctx->rt.d_status, sizeof(int), cudaMemcpyDeviceToHost));
-    if (st) {
-      GCHECK(cudaMemset(ctx->rt.d_status, 0, sizeof(int)));
-      static const char* names[] = {"ok", "gather index out of range", "tensor-core barrier wait timed out",
-                                    "invalid scalar program", "integer division by zero", "slice out of bounds"};
-      throw gawee::StatusError(GAWEE_ERR_DEVICE, std::string("device reported: ") + (st >= 0 && st < 6 ? names[st] : "error"));
-    }
+    check_device_status(ctx->rt.d_status);
   });
 }
 
@@ -982,7 +1009,13 @@ gawee_status gawee_ciface_forward(gawee_ctx* ctx, void* result_desc, void* const
     void* host = std::malloc(nb ? nb : 1);  // owned by the caller, as in the reference ABI
     if (!host) throw gawee::StatusError(GAWEE_ERR_OOM, "malloc of the result failed");
     GCHECK(cudaMemcpyAsync(host, rt.ptr(v), nb, cudaMemcpyDeviceToHost, s));
-    GCHECK(cudaStreamSynchronize(s));
+    try {
+      GCHECK(cudaStreamSynchronize(s));
+      check_device_status(rt.d_status);
+    } catch (...) {
+      std::free(host);
+      throw;
+    }
     char* r = static_cast<char*>(result_desc);
     const auto& rtype = g.values[g.results[0]].type;
     int64_t zero = 0;
@@ -1019,7 +1052,10 @@ gawee_status gawee_embedded_forward(const char* mlir_text, int device, void* res
       cache->ctxs.push_back({{mlir_text, device}, ctx});
     }
   }
-  return gawee_ciface_forward(ctx, result_desc, arg_descs, nargs);
+  gawee_status st = gawee_ciface_forward(ctx, result_desc, arg_descs, nargs);
+  // the caller holds no context: its message goes where gawee_last_error(NULL, ...) reads
+  if (st != GAWEE_OK) g_create_error = ctx->err;
+  return st;
 }
 
 gawee_status gawee_dp_unique_id(void* id) {
@@ -1038,9 +1074,59 @@ gawee_status gawee_dp_init(gawee_ctx* ctx, int world, int rank, const void* id) 
     if (!gawee::nccl().ok) throw gawee::StatusError(GAWEE_ERR_NCCL, "libnccl.so.2 could not be loaded");
     ncclUniqueId u;
     std::memcpy(&u, id, sizeof(u));
-    gawee::nccl_check(gawee::nccl().commInitRank(&ctx->rt.comm, world, u, rank), "ncclCommInitRank");
-    ctx->rt.world = world;
-    ctx->rt.rank = rank;
+    auto& rt = ctx->rt;
+    gawee::nccl_check(gawee::nccl().commInitRank(&rt.comm, world, u, rank), "ncclCommInitRank");
+    rt.world = world;
+    rt.rank = rank;
+    // every rank learns every rank's output sizes (one all-gather of a few
+    // int64s, once): the gather then moves each peer's own byte count
+    const size_t nout = rt.plan->result_view.size();
+    std::vector<int64_t> mine(nout);
+    for (size_t i = 0; i < nout; ++i) {
+      const gawee::View& v = rt.plan->result_view[i];
+      mine[i] = v.numel() * (int64_t)gawee::dtype_size(v.dt);
+    }
+    rt.peer_bytes.assign((size_t)world * nout, 0);
+    if (nout) {
+      int64_t* d = nullptr;
+      GCHECK(cudaMalloc(&d, sizeof(int64_t) * nout * (world + 1)));
+      try {
+        GCHECK(cudaMemcpyAsync(d, mine.data(), sizeof(int64_t) * nout, cudaMemcpyHostToDevice, rt.own_stream));
+        gawee::nccl_check(gawee::nccl().allGather(d, d + nout, nout * sizeof(int64_t), ncclInt8, rt.comm,
+                                                  rt.own_stream), "ncclAllGather");
+        GCHECK(cudaMemcpyAsync(rt.peer_bytes.data(), d + nout, sizeof(int64_t) * nout * world,
+                               cudaMemcpyDeviceToHost, rt.own_stream));
+        GCHECK(cudaStreamSynchronize(rt.own_stream));
+      } catch (...) {
+        cudaFree(d);
+        throw;
+      }
+      GCHECK(cudaFree(d));
+    }
+    for (int r = 0; r < world; ++r)
+      for (size_t i = 0; i < nout; ++i) {
+        const int64_t b = rt.peer_bytes[(size_t)r * nout + i];
+        // every rank plans the same graph up to its batch size: a rank whose
+        // row size differs from rank 0's cannot be gathered row-wise
+        const int64_t rows0 = rt.plan->result_view[i].shape.empty() ? 1 : rt.plan->result_view[i].shape[0];
+        const int64_t row_bytes = rows0 ? mine[i] / rows0 : 0;
+        if (b < 0 || (row_bytes && b % row_bytes != 0))
+          throw gawee::StatusError(GAWEE_ERR_INVALID, "rank " + std::to_string(r) + " output " + std::to_string(i) +
+                                                          " is not a whole number of this rank's rows");
+      }
+  });
+}
+
+gawee_status gawee_dp_output_bytes(gawee_ctx* ctx, int i, size_t* total) {
+  if (!ctx || !total) return GAWEE_ERR_INVALID;
+  return guard(ctx, [&] {
+    auto& rt = ctx->rt;
+    if (!rt.comm) throw gawee::StatusError(GAWEE_ERR_INVALID, "gawee_dp_init was not called");
+    const size_t nout = rt.plan->result_view.size();
+    if (i < 0 || i >= (int)nout) throw gawee::StatusError(GAWEE_ERR_INVALID, "output index out of range");
+    size_t t = 0;
+    for (int r = 0; r < rt.world; ++r) t += (size_t)rt.peer_bytes[(size_t)r * nout + i];
+    *total = t;
   });
 }
 
@@ -1052,16 +1138,24 @@ gawee_status gawee_dp_gather_output(gawee_ctx* ctx, int i, void* dst, void* stre
     if (i < 0 || i >= (int)rt.plan->result_view.size()) throw gawee::StatusError(GAWEE_ERR_INVALID, "output index out of range");
     const gawee::View& v = rt.plan->result_view[i];
     size_t nb = (size_t)v.numel() * gawee::dtype_size(v.dt);
+    const size_t nout = rt.plan->result_view.size();
+    if ((int64_t)nb != rt.peer_bytes[(size_t)rt.rank * nout + i])
+      throw gawee::StatusError(GAWEE_ERR_INVALID, "output size changed since gawee_dp_init");
     cudaStream_t s = stream_of(ctx, stream);
     auto& api = gawee::nccl();
     if (rt.rank == 0) {
       if (!dst) throw gawee::StatusError(GAWEE_ERR_INVALID, "rank 0 needs a destination buffer");
       GCHECK(cudaMemcpyAsync(dst, rt.ptr(v), nb, cudaMemcpyDeviceToDevice, s));
+      size_t off = nb;
       gawee::nccl_check(api.groupStart(), "ncclGroupStart");
-      for (int r = 1; r < rt.world; ++r)
-        gawee::nccl_check(api.recv(static_cast<char*>(dst) + (size_t)r * nb, nb, ncclInt8, r, rt.comm, s), "ncclRecv");
+      for (int r = 1; r < rt.world; ++r) {
+        const size_t rb = (size_t)rt.peer_bytes[(size_t)r * nout + i];
+        if (rb)
+          gawee::nccl_check(api.recv(static_cast<char*>(dst) + off, rb, ncclInt8, r, rt.comm, s), "ncclRecv");
+        off += rb;
+      }
       gawee::nccl_check(api.groupEnd(), "ncclGroupEnd");
-    } else {
+    } else if (nb) {
       gawee::nccl_check(api.send(rt.ptr(v), nb, ncclInt8, 0, rt.comm, s), "ncclSend");
     }
   });

@@ -2,6 +2,7 @@
 // reductions, softmax, gather, index remaps, pooling, top-k and the packing of
 // tensor-core B operands.  Grids are sized as multiples of the SM count and
 // use grid-stride loops.
+#include <algorithm>
 #include <cfloat>
 #include <cstdio>
 
@@ -1015,9 +1016,58 @@ __global__ void __launch_bounds__(kThreads) pack_b4_kernel(const __grid_constant
   }
 }
 
+// Sources stored k-outer, n-contiguous ([k][n] rows, the layout of a
+// gawee.matmul right operand): a 32 x 32 block of (k, n) goes through shared
+// memory, so the loads run along n and the plane stores along k, both
+// coalesced.  One k dimension; batch offsets as in pack_b_kernel.  Same values.
+constexpr int kPackT = 32;
+__global__ void __launch_bounds__(256) pack_b_kn_kernel(const __grid_constant__ PackBParams p) {
+  __shared__ float tile[kPackT][kPackT + 1];
+  const int64_t kt = (p.ldk + kPackT - 1) / kPackT, nt = (p.N + kPackT - 1) / kPackT;
+  const int64_t tiles = p.batch * nt * kt;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
+  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int64_t k0 = (t % kt) * kPackT;
+    const int64_t n0 = ((t / kt) % nt) * kPackT;
+    const int64_t b = t / (kt * nt);
+    int64_t base = 0, rem = b;
+    for (int d = p.batch_rank - 1; d >= 0; --d) {
+      base += (rem % p.batch_shape[d]) * p.batch_st[d];
+      rem /= p.batch_shape[d];
+    }
+    const int64_t n = n0 + tx;
+#pragma unroll
+    for (int j = 0; j < kPackT; j += 8) {
+      const int64_t k = k0 + ty + j;
+      float x = 0.f;
+      if (n < p.N && k < p.K && k < p.k_valid[0]) x = p.src[base + k * p.k_st[0] + n];
+      tile[ty + j][tx] = x;
+    }
+    __syncthreads();
+    const int64_t k = k0 + tx;
+#pragma unroll
+    for (int j = 0; j < kPackT; j += 8) {
+      const int64_t nn = n0 + ty + j;
+      if (nn < p.N && k < p.ldk) {
+        const float x = tile[tx][ty + j];
+        const float hi = __uint_as_float(__float_as_uint(x) & 0xffffe000u);
+        const int64_t i = (b * p.N + nn) * p.ldk + k;
+        p.hi[i] = hi;
+        p.lo[i] = __fsub_rn(x, hi);
+      }
+    }
+    __syncthreads();
+  }
+}
+
 void launch_pack_b(const PackBParams& p, cudaStream_t s) {
   const int64_t total = p.batch * p.N * p.ldk;
   if (total <= 0) return;
+  if (p.k_rank == 1 && p.sn == 1 && p.k_st[0] != 1) {
+    const int64_t tiles = p.batch * ((p.N + kPackT - 1) / kPackT) * ((p.ldk + kPackT - 1) / kPackT);
+    pack_b_kn_kernel<<<(unsigned)std::min<int64_t>(tiles, 148 * 8), 256, 0, s>>>(p);
+    return;
+  }
   const bool fits = total / 4 < (int64_t(1) << 31) && p.batch * p.N < (int64_t(1) << 31) && p.ldk % 4 == 0 &&
                     (reinterpret_cast<uintptr_t>(p.hi) & 15) == 0 && (reinterpret_cast<uintptr_t>(p.lo) & 15) == 0;
   if (fits) {

@@ -56,15 +56,40 @@ def share_nccl_id(uid: bytes, rank: int, group=None) -> bytes:
     return bytes(t.cpu().numpy().tobytes())
 
 
+def gather_offsets(rows: Sequence[int]) -> List[int]:
+    """Row offset of each rank's block in the gathered output (rank order);
+    what libgawee_cuda computes from the sizes exchanged at gawee_dp_init."""
+    out, acc = [], 0
+    for r in rows:
+        if r < 0:
+            raise ValueError("negative row count")
+        out.append(acc)
+        acc += r
+    return out
+
+
 def gather_rows_host(local: np.ndarray, rank: int, world: int, group=None):
-    """Host-side gather of equal-size row blocks to rank 0 (gloo); returns the
-    assembled array on rank 0 and None elsewhere.  Used where no GPU exists."""
+    """Host-side gather of row blocks to rank 0 (gloo), in rank order; the
+    blocks may differ in length (shards of an uneven batch).  Returns the
+    assembled array on rank 0 and None elsewhere.  Used where no GPU exists.
+    Like gawee_dp_init / gawee_dp_gather_output, the ranks first exchange
+    their row counts, then rank 0 places each block at its offset."""
     import torch
     import torch.distributed as dist
 
-    t = torch.from_numpy(np.ascontiguousarray(local))
+    local = np.ascontiguousarray(local)
+    counts = [torch.zeros(1, dtype=torch.int64) for _ in range(world)]
+    dist.all_gather(counts, torch.tensor([local.shape[0]], dtype=torch.int64), group=group)
+    rows = [int(c.item()) for c in counts]
+    width = max(rows)
+    padded = np.zeros((width,) + local.shape[1:], local.dtype)
+    padded[:local.shape[0]] = local
+    t = torch.from_numpy(padded)
     parts = [torch.empty_like(t) for _ in range(world)] if rank == 0 else None
     dist.gather(t, gather_list=parts, dst=0, group=group)
-    if rank == 0:
-        return assemble([p.numpy() for p in parts])
-    return None
+    if rank != 0:
+        return None
+    out = np.empty((sum(rows),) + local.shape[1:], local.dtype)
+    for r, off in enumerate(gather_offsets(rows)):
+        out[off:off + rows[r]] = parts[r].numpy()[:rows[r]]
+    return out

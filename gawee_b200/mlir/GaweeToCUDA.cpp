@@ -3,8 +3,9 @@
 // whose `_mlir_ciface_forward` runs the graph on a B200 through libgawee_cuda.
 //
 // Drop-in for middle/mlir/lib/Conversion/ of fwangdo/Gawee, registered in
-// middle/mlir/tools/gawee-opt.cpp next to `--gawee-to-llvm` (see
-// INTEGRATION.md).  It replaces the CPU pipeline of gawee-opt.cpp:120-184:
+// middle/mlir/tools/gawee-opt.cpp next to `--gawee-to-llvm` (a
+// PassPipelineRegistration beside the one at gawee-opt.cpp:120-184).  It
+// replaces the CPU pipeline of gawee-opt.cpp:120-184:
 // instead of lowering every op to loops, the pass keeps the gawee-level
 // `forward` as text in a global constant and emits
 //
@@ -61,13 +62,21 @@ struct GaweeToCUDAPass : public PassWrapper<GaweeToCUDAPass, OperationPass<Modul
     }
     const unsigned nargs = forward.getNumArguments();
 
-    // 1. The gawee-level text libgawee_cuda plans (generic op form is what
-    //    its parser reads; the printed module includes #map aliases).
+    // 1. The gawee-level text libgawee_cuda plans, printed the way
+    //    gawee-onnx-translate prints it: the default (custom) form.  gawee
+    //    ops declare no assembly format, so they print in the generic form
+    //    `"gawee.conv"(%0, %1) <{...}> : (...) -> ...`; func.func, return,
+    //    arith.constant, tensor.empty, linalg.fill / generic / reduce print in
+    //    their custom forms, with `#map = affine_map<...>` aliases at the top
+    //    of the module.  That is the form the planner's parser reads
+    //    (csrc/host/ir.cpp).  The full generic form (printGenericOpForm(true))
+    //    would also print func.func and the module generically, which the
+    //    parser does not accept, so it is not used.
     std::string text;
     {
       llvm::raw_string_ostream os(text);
-      OpPrintingFlags flags;
-      flags.printGenericOpForm(false);
+      OpPrintingFlags flags;  // defaults: custom form where an op has one
+      flags.elideLargeElementsAttrs(false);
       module.print(os, flags);
     }
     text.push_back('\0');
@@ -88,6 +97,12 @@ struct GaweeToCUDAPass : public PassWrapper<GaweeToCUDAPass, OperationPass<Modul
 
     auto calleeTy = LLVM::LLVMFunctionType::get(i32, {ptr, i32, ptr, ptr, i32});
     LLVM::LLVMFuncOp::create(b, loc, "gawee_embedded_forward", calleeTy);
+    // Failure path: the reference's lowered code has no status, and its
+    // launcher reports errors by exiting non-zero (back/gawee_aot.cpp:435-438),
+    // so the shim prints gawee_last_error() and exits with status 1.
+    LLVM::LLVMFuncOp::create(b, loc, "gawee_last_error", LLVM::LLVMFunctionType::get(i32, {ptr, ptr, i64}));
+    LLVM::LLVMFuncOp::create(b, loc, "puts", LLVM::LLVMFunctionType::get(i32, {ptr}));
+    LLVM::LLVMFuncOp::create(b, loc, "exit", LLVM::LLVMFunctionType::get(voidTy, {i32}));
 
     SmallVector<Type> params(nargs + 1, ptr);  // result descriptor, then one per argument
     auto shimTy = LLVM::LLVMFunctionType::get(voidTy, params);
@@ -104,8 +119,26 @@ struct GaweeToCUDAPass : public PassWrapper<GaweeToCUDAPass, OperationPass<Modul
     Value textPtr = LLVM::AddressOfOp::create(b, loc, ptr, "gawee_forward_text");
     Value device = LLVM::ConstantOp::create(b, loc, i32, b.getI32IntegerAttr(0));
     Value n = LLVM::ConstantOp::create(b, loc, i32, b.getI32IntegerAttr(nargs));
-    LLVM::CallOp::create(b, loc, TypeRange{i32}, "gawee_embedded_forward",
-                         ValueRange{textPtr, device, entry->getArgument(0), array, n});
+    Value status = LLVM::CallOp::create(b, loc, TypeRange{i32}, "gawee_embedded_forward",
+                                        ValueRange{textPtr, device, entry->getArgument(0), array, n})
+                       .getResult();
+    Value zero = LLVM::ConstantOp::create(b, loc, i32, b.getI32IntegerAttr(0));
+    Value failed = LLVM::ICmpOp::create(b, loc, LLVM::ICmpPredicate::ne, status, zero);
+    Block *okBlock = shim.addBlock();
+    Block *failBlock = shim.addBlock();
+    LLVM::CondBrOp::create(b, loc, failed, failBlock, okBlock);
+
+    b.setInsertionPointToStart(failBlock);
+    Value msgLen = LLVM::ConstantOp::create(b, loc, i64, b.getI64IntegerAttr(1024));
+    Value msg = LLVM::AllocaOp::create(b, loc, ptr, b.getI8Type(), msgLen, /*alignment=*/1);
+    Value null = LLVM::ZeroOp::create(b, loc, ptr);
+    LLVM::CallOp::create(b, loc, TypeRange{i32}, "gawee_last_error", ValueRange{null, msg, msgLen});
+    LLVM::CallOp::create(b, loc, TypeRange{i32}, "puts", ValueRange{msg});
+    Value one = LLVM::ConstantOp::create(b, loc, i32, b.getI32IntegerAttr(1));
+    LLVM::CallOp::create(b, loc, TypeRange{}, "exit", ValueRange{one});
+    LLVM::UnreachableOp::create(b, loc);
+
+    b.setInsertionPointToStart(okBlock);
     LLVM::ReturnOp::create(b, loc, ValueRange{});
   }
 };

@@ -75,6 +75,7 @@ def load_library(path: str = LIB_PATH):
             "gawee_dp_unique_id": (c.c_int, [P]),
             "gawee_dp_init": (c.c_int, [P, c.c_int, c.c_int, P]),
             "gawee_dp_gather_output": (c.c_int, [P, c.c_int, P, P]),
+            "gawee_dp_output_bytes": (c.c_int, [P, c.c_int, c.POINTER(c.c_size_t)]),
         }
         for name, (res, args) in sig.items():
             f = getattr(lib, name)
@@ -235,6 +236,12 @@ class Model:
     def dp_init(self, world: int, rank: int, uid: bytes):
         buf = ctypes.create_string_buffer(uid, 128)
         self._check(self._lib.gawee_dp_init(self._h, world, rank, buf))
+
+    def dp_output_bytes(self, i: int = 0) -> int:
+        """Bytes of output i over every rank (rank 0's gather destination size)."""
+        n = ctypes.c_size_t()
+        self._check(self._lib.gawee_dp_output_bytes(self._h, i, ctypes.byref(n)))
+        return n.value
 
     def dp_gather_output(self, i: int, dst_ptr: Optional[int], stream=None):
         self._check(self._lib.gawee_dp_gather_output(self._h, i, dst_ptr, _stream_ptr(stream)))

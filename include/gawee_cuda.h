@@ -99,7 +99,9 @@ gawee_status gawee_get_output(gawee_ctx* ctx, int i, void* host, size_t bytes, v
 gawee_status gawee_output_device_ptr(gawee_ctx* ctx, int i, void** ptr);
 
 /* Wait for `stream` and check the device status word: returns
- * GAWEE_ERR_DEVICE if a kernel flagged an error since the last check. */
+ * GAWEE_ERR_DEVICE if a kernel flagged an error since the last check.  With
+ * ctx NULL it checks the status word of gawee_matmul_f32_noalloc on the
+ * current device instead (message via gawee_last_error(NULL, ...)). */
 gawee_status gawee_synchronize(gawee_ctx* ctx, void* stream);
 
 /* Capture the forward sequence into a CUDA graph on the next forward
@@ -144,7 +146,8 @@ gawee_status gawee_ciface_forward(gawee_ctx* ctx, void* result_desc, void* const
  * lowered module keeps the gawee-level `forward` text as a global string and
  * its `_mlir_ciface_forward` calls this.  The first call on a thread plans the
  * text for `device` and caches the context (keyed by the string's address);
- * later calls reuse it.  Semantics as gawee_ciface_forward. */
+ * later calls reuse it.  Semantics as gawee_ciface_forward; on failure the
+ * message is read with gawee_last_error(NULL, ...). */
 gawee_status gawee_embedded_forward(const char* mlir_text, int device, void* result_desc, void* const* arg_descs,
                                     int nargs);
 
@@ -155,18 +158,28 @@ gawee_status gawee_embedded_forward(const char* mlir_text, int device, void* res
  * caller, computed on the tensor-core kernel with split-precision TF32
  * (the same arithmetic as gawee.matmul in a planned graph), enqueued on
  * `stream`.  For callers that cannot allocate device memory when they need
- * the product: inside CUDA stream capture, under a fixed memory budget or
- * pool, or on an error path.  It calls no cudaMalloc/cudaFree: the packed
- * TF32 planes of B use a 16 MiB array in the library's static device memory,
- * which every GPU that loads the library holds until the process exits.
+ * the product: a host framework whose own caching allocator owns the device
+ * memory (an allocation behind its back can fail or fragment its pool), a
+ * caller working within a fixed memory budget, or an error-recovery path
+ * after an allocation has already failed; cudaMalloc and cudaFree can also
+ * wait for the whole device.  It calls no cudaMalloc/cudaFree and no
+ * allocating library routine: the packed TF32 planes of B use a 16 MiB array
+ * in the library's static device memory, which every GPU that loads the
+ * library holds until the process exits.
  *   - Limits: k a multiple of 4, A 16-byte aligned, n * k <= 2,097,152
  *     (two planes of n x k floats in 16 MiB); larger shapes return
  *     GAWEE_ERR_INVALID with a message for gawee_last_error(NULL, ...).
- *   - The first call on a device looks up the array's device address
- *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - The first call on a device looks up the device addresses of the array
+ *     and of a status word (cudaGetSymbolAddress); make that first call
+ *     before any stream capture.
  *   - Every call shares the one array: calls that overlap on the GPU (on
  *     different streams, or from several threads) race.  Each call rewrites
  *     all of the scratch it reads, so nothing needs clearing between calls.
+ *   - Errors inside the kernel (a bounded wait that gave up, leaving C
+ *     partly written) are recorded in the shared status word:
+ *     gawee_synchronize(NULL, stream) waits for `stream`, then returns
+ *     GAWEE_ERR_DEVICE and clears the word if any call since the last check
+ *     reported one.
  * ------------------------------------------------------------------------- */
 gawee_status gawee_matmul_f32_noalloc(const float* a, const float* b, float* c, int64_t m, int64_t n, int64_t k,
                                       void* stream);
@@ -181,11 +194,19 @@ gawee_status gawee_matmul_f32_noalloc(const float* a, const float* b, float* c, 
 /* Fill `id` (GAWEE_NCCL_ID_BYTES) on rank 0; share it with the other ranks. */
 gawee_status gawee_dp_unique_id(void* id);
 
-/* Join a communicator of `world` ranks on the context's device. */
+/* Join a communicator of `world` ranks on the context's device.  Collective:
+ * the ranks also exchange their output sizes (shards may differ by a row,
+ * e.g. 5 rows over 2 ranks as 3 + 2). */
 gawee_status gawee_dp_init(gawee_ctx* ctx, int world, int rank, const void* id);
 
-/* Gather output i of every rank (rows of equal size) into `dst` on rank 0
- * (a device buffer of world * output-size bytes; ignored on other ranks). */
+/* Bytes of output i summed over every rank: the size of rank 0's
+ * destination buffer for gawee_dp_gather_output. */
+gawee_status gawee_dp_output_bytes(gawee_ctx* ctx, int i, size_t* total);
+
+/* Gather output i of every rank, in rank order, into `dst` on rank 0 (a
+ * device buffer of gawee_dp_output_bytes bytes; ignored on other ranks).
+ * Each rank contributes its own output size, as exchanged at init.
+ * Collective: every rank calls it, in the same order. */
 gawee_status gawee_dp_gather_output(gawee_ctx* ctx, int i, void* dst, void* stream);
 
 #ifdef __cplusplus

@@ -1,10 +1,8 @@
-"""Data parallelism on two GPUs: each rank runs its batch slice of ResNet-18,
-rank 0 gathers the output rows over NCCL (gawee_dp_gather_output), and the
-result matches the single-GPU full-batch forward.  Batch rows are
-independent, but a row's 128-row tile position differs between the sharded
-and the full batch, and the tensor-core kernel starts each tile's k loop at a
-rotation that depends on that position, so the fp32 sums are ordered
-differently: the comparison uses the reference's ResNet tolerance."""
+"""Data parallelism on two GPUs: each rank runs its batch slice of ResNet-18
+(7 images over 2 ranks: 4 + 3, an uneven split), rank 0 gathers the output
+rows over NCCL (gawee_dp_gather_output, sized by gawee_dp_output_bytes), and
+the gathered rows match the oracle's forward of the full batch at the
+reference's ResNet tolerance."""
 import os
 import socket
 import subprocess
@@ -12,6 +10,9 @@ import sys
 
 import numpy as np
 import pytest
+
+import oracle
+from tests.helpers import compare
 
 pytestmark = pytest.mark.gpu
 
@@ -26,15 +27,17 @@ from gawee_b200.runtime import Model
 rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
 torch.cuda.set_device(rank)
 dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", rank))
-full = synth.resnet18(6, image=64)
+full = synth.resnet18(7, image=64)
 args = full.make_args()
-s0, s1 = dp.shard_range(6, world, rank)
+s0, s1 = dp.shard_range(7, world, rank)
 shard = synth.resnet18(s1 - s0, image=64)
 m = Model(shard.mlir, device=rank)
 m.set_args(dp.shard_args(args, [True] + [False] * (len(args) - 1), world, rank))
 uid = dp.share_nccl_id(Model.dp_unique_id() if rank == 0 else bytes(128), rank)
 m.dp_init(world, rank, uid)
-out = torch.empty((6, 1000), device=f"cuda:{rank}") if rank == 0 else None
+total = m.dp_output_bytes(0)
+assert total == 7 * 1000 * 4, total
+out = torch.empty((7, 1000), device=f"cuda:{rank}") if rank == 0 else None
 stream = torch.cuda.current_stream().cuda_stream
 m.forward(stream)
 m.dp_gather_output(0, out.data_ptr() if rank == 0 else None, stream)
@@ -48,12 +51,11 @@ dist.destroy_process_group()
 """
 
 
-def test_two_gpu_batch_sharding_matches_one_gpu(tmp_path):
+def test_two_gpu_uneven_batch_sharding_matches_oracle(tmp_path):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     from gawee_b200 import synth
-    from gawee_b200.runtime import Model
 
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -69,11 +71,6 @@ def test_two_gpu_batch_sharding_matches_one_gpu(tmp_path):
     codes = [p.wait(timeout=600) for p in procs]
     assert codes == [0, 0]
     gathered = np.load(out)
-    full = synth.resnet18(6, image=64)
-    args = full.make_args()
-    m = Model(full.mlir, device=0)
-    try:
-        want = m.run(args)[0]
-    finally:
-        m.close()
-    np.testing.assert_allclose(gathered, want, atol=1e-4, rtol=1e-4)
+    full = synth.resnet18(7, image=64)
+    want = oracle.run(full.mlir, full.make_args())[0]
+    compare(gathered, want, 1e-4, 1e-4, "gathered rows vs oracle")

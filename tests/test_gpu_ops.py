@@ -289,3 +289,46 @@ module {
 """
     x = np.random.default_rng(3).standard_normal((4, 9)).astype(np.float32)
     parity(mlir, [x])
+
+
+def test_batch_norm_and_flatten():
+    """BatchNormOpLowering (GaweeToLinalg.cpp:1122-1173) per channel with the
+    reference's operation order; FlattenOpLowering (813-870) as a view and as
+    a copy of a transposed source."""
+    def g_(g):
+        x = rand_input(g, (2, 5, 7, 3), 81)
+        w = g.weight((5,), lambda: np.random.default_rng(82).standard_normal(5).astype(np.float32))
+        b = g.weight((5,), lambda: np.random.default_rng(83).standard_normal(5).astype(np.float32))
+        mean = g.weight((5,), lambda: np.random.default_rng(84).standard_normal(5).astype(np.float32))
+        var = g.weight((5,), lambda: np.random.default_rng(85).uniform(0.1, 2.0, 5).astype(np.float32))
+        bn = g.op("batch_norm", [x, w, b, mean, var], {"affine": "true", "eps": "1.000000e-05 : f64"}, F,
+                  (2, 5, 7, 3))
+        f1 = g.op("flatten", [bn], {"startDim": "1 : i64", "endDim": "-1 : i64"}, F, (2, 105))
+        t = g.transpose(x, [0, 2, 3, 1])
+        f2 = g.op("flatten", [t], {"startDim": "1 : i64", "endDim": "2 : i64"}, F, (2, 21, 5))
+        return [bn, f1, g.relu(f2)]
+    got, want = parity(*build(g_), atol=0.0, rtol=0.0)  # same IEEE operations, same order: bit-exact
+
+
+def test_golden_fixtures_on_cuda():
+    """The committed torch-computed fixtures (tests/golden/) through the CUDA
+    path, at the tolerance each fixture states."""
+    import os
+
+    from gawee_b200.runtime import Model
+    from tests.helpers import compare
+    gold = os.path.join(os.path.dirname(__file__), "golden")
+    names = sorted(f[:-4] for f in os.listdir(gold) if f.endswith(".npz"))
+    assert names
+    for name in names:
+        with open(os.path.join(gold, name + ".mlir")) as f:
+            mlir = f.read()
+        data = np.load(os.path.join(gold, name + ".npz"))
+        args = [data[f"arg{i}"] for i in range(sum(k.startswith("arg") for k in data.files))]
+        m = Model(mlir)
+        try:
+            outs = m.run(args)
+        finally:
+            m.close()
+        for k, o in enumerate(outs):
+            compare(o, data[f"out{k}"], atol=float(data["atol"]), rtol=1e-5, what=f"{name} output{k}")

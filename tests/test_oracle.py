@@ -72,6 +72,26 @@ def test_kat_conv_padding_and_bias():
     assert np.array_equal(run(mlir, args)[0], np.full((1, 1, 2, 2), 4.5, np.float32))
 
 
+def test_kat_batch_norm():
+    # GaweeToLinalg.cpp:1122-1173: ((x - mean) / sqrt(var + eps)) * w + b per channel, eps rounded to f32
+    x = np.array([[[[1.0, 3.0]], [[-2.0, 6.0]]]], np.float32)       # [1, 2, 1, 2]
+    w = np.array([2.0, 0.5], np.float32)
+    b = np.array([1.0, -1.0], np.float32)
+    mean = np.array([1.0, 2.0], np.float32)
+    var = np.array([4.0, 16.0 - 0.25], np.float32)                  # eps 0.25: sqrt(4.25), sqrt(16)
+
+    def g_(g):
+        xs = [g.input(F, a.shape, (lambda a=a: a)) for a in (x,)]
+        ws = [g.weight(a.shape, (lambda a=a: a)) for a in (w, b, mean, var)]
+        return [g.op("batch_norm", xs + ws, {"affine": "true", "eps": "2.500000e-01 : f64"}, F, x.shape)]
+    got = run(*build(g_))[0]
+    d0 = np.float32(np.sqrt(np.float32(4.25)))
+    want = np.array([[[[(np.float32(0.0) / d0) * 2 + 1, (np.float32(2.0) / d0) * 2 + 1]],
+                      [[(-4.0 / 4.0) * 0.5 - 1, (4.0 / 4.0) * 0.5 - 1]]]], np.float32)
+    assert np.array_equal(got, want)
+    assert got[0, 1, 0, 0] == -1.5 and got[0, 1, 0, 1] == -0.5
+
+
 def test_kat_relu_maxpool_semantics():
     def g_(g):
         x = g.input(F, (1, 1, 2, 3), lambda: np.array([[[[-0.0, -2.0, np.nan], [1.0, -1.0, 0.0]]]], np.float32))

@@ -1,16 +1,21 @@
 """The allocation-free matrix product, gawee_matmul_f32_noalloc.
 
 It exists for callers that cannot allocate device memory at the moment they
-need a product — code inside CUDA stream capture (cudaMalloc cannot be
-captured), callers living within a fixed memory budget or their own pool, or
-error-recovery paths where an allocation could fail.  They pass their own A,
-B and C; the library keeps the packed B planes in its static device scratch.
+need a product: a host framework whose caching allocator owns the device
+memory (an allocation behind its back can fail or fragment the pool it
+manages), a caller working within a fixed memory budget, or an
+error-recovery path after an allocation has already failed.  They pass
+their own A, B and C; the library keeps the packed B planes in its static
+device scratch and reports kernel errors through a static status word.
 
 The test drives the entry point through the C ABI on device buffers the test
-owns, twice in a row with different operands (the second call reuses the
-scratch the first one left behind), and compares each result with the
-regular entry points (gawee_create / gawee_set_arg / gawee_forward /
-gawee_get_output) on a graph holding the same gawee.matmul.
+owns, two calls in a row with different operands per shape (the second call
+reuses the scratch the first one left behind), and compares each result with
+the oracle's sequential fp32 product and with the regular entry points
+(gawee_create / gawee_set_arg / gawee_forward / gawee_get_output) on a graph
+holding the same gawee.matmul.  Shapes cover both tile widths (n <= 64 takes
+the 64-wide tile), n not a multiple of 4, a single row, and the largest
+n * k the scratch holds.  This file is collected last on purpose.
 """
 import ctypes
 
@@ -30,21 +35,29 @@ def _matmul_graph(m, k, n):
     return build(g_)[0]
 
 
-def test_noalloc_matmul_matches_planned_graph_twice():
+# (m, k, n): the first-round shape; 1 row with the 64-wide tile; 64-wide tile;
+# n not a multiple of 4 on the 128-wide tile; the scratch limit n * k = 2 Mi.
+SHAPES = [(333, 260, 200), (1, 4, 3), (5, 8, 64), (130, 36, 65), (3, 2048, 1024)]
+
+
+@pytest.mark.parametrize("m,k,n", SHAPES)
+def test_noalloc_matmul_matches_oracle_and_planned_graph_twice(m, k, n):
     import torch
 
+    import oracle
     from gawee_b200 import runtime
 
     lib = runtime.load_library()
-    m, k, n = 333, 260, 200
     mlir = _matmul_graph(m, k, n)
     model = runtime.Model(mlir)
+    atol = 1e-4 * max(1.0, np.sqrt(k) / 8)  # the tolerance of the GEMM parity tests
     try:
         for seed in (1, 2):
             rng = np.random.default_rng(seed)
             a = rng.standard_normal((m, k), dtype=np.float32)
             b = rng.standard_normal((k, n), dtype=np.float32)
-            want = model.run([a, b])[0]
+            want = oracle.run(mlir, [a, b])[0]
+            planned = model.run([a, b])[0]
 
             da = torch.from_numpy(a).cuda()
             db = torch.from_numpy(b).cuda()
@@ -52,9 +65,10 @@ def test_noalloc_matmul_matches_planned_graph_twice():
             stream = torch.cuda.current_stream().cuda_stream
             st = lib.gawee_matmul_f32_noalloc(da.data_ptr(), db.data_ptr(), dc.data_ptr(), m, n, k, stream)
             assert st == 0, f"status {st}"
-            torch.cuda.synchronize()
+            assert lib.gawee_synchronize(None, stream) == 0, "the kernel reported an error"
             got = dc.cpu().numpy()
-            compare(got, want, atol=2e-4, rtol=1e-4, what=f"noalloc call {seed}")
+            compare(got, want, atol=atol, rtol=1e-4, what=f"noalloc call {seed} vs oracle")
+            compare(got, planned, atol=atol, rtol=1e-4, what=f"noalloc call {seed} vs gawee_forward")
     finally:
         model.close()
 
@@ -75,3 +89,6 @@ def test_noalloc_matmul_rejects_oversized_and_unaligned():
     assert b"exceeds" in buf.value
     st = lib.gawee_matmul_f32_noalloc(a.data_ptr(), b.data_ptr(), c.data_ptr(), 4, 8, 6, None)  # k % 4 != 0
     assert st == 1
+    st = lib.gawee_matmul_f32_noalloc(a.data_ptr() + 4, b.data_ptr(), c.data_ptr(), 3, 8, 8, None)  # A misaligned
+    assert st == 1
+    assert lib.gawee_synchronize(None, None) == 0

@@ -112,7 +112,7 @@ def test_embedded_forward_plans_once_and_reports_errors(cuda_lib):
     libc.free.argtypes = [ctypes.c_void_p]
     for call in range(2):
         res = memref_type(3)()
-        st = cuda_lib.gawee_embedded_forward(ctypes.addressof(text), 0, ctypes.addressof(res), ptrs, len(descs))
+        st = cuda_lib.gawee_embedded_forward(text, 0, ctypes.addressof(res), ptrs, len(descs))
         assert st == 0, st
         got = _result_array(res, want.shape, np.float32)
         libc.free(res.allocated)
@@ -123,7 +123,7 @@ def test_embedded_forward_plans_once_and_reports_errors(cuda_lib):
     descs[0] = describe(bad)
     ptrs[0] = ctypes.addressof(descs[0])
     res = memref_type(3)()
-    st = cuda_lib.gawee_embedded_forward(ctypes.addressof(text), 0, ctypes.addressof(res), ptrs, len(descs))
+    st = cuda_lib.gawee_embedded_forward(text, 0, ctypes.addressof(res), ptrs, len(descs))
     assert st == 6  # GAWEE_ERR_DEVICE
     msg = ctypes.create_string_buffer(512)
     cuda_lib.gawee_last_error(None, msg, len(msg))

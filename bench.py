@@ -293,7 +293,7 @@ def latency_entry(name, g, metric, published_ms, published_src, peaks, local, st
             m.synchronize(sp)
             e2e.append(e0.elapsed_time(e1))
         roof, kern, prof = tc_roofline(m, sp, peaks)
-        n_launch = m.num_kernels()
+        n_launch = m.num_launches()
     finally:
         m.close()
     per, reps = _time_oracle(g, os.cpu_count() or 1, 5.0, max_reps=4)
@@ -346,7 +346,7 @@ def decoder_entry(peaks, local, steps):
         m.synchronize(sp)
         ms_e2e = e0.elapsed_time(e1) / steps
         roof, kern, prof = tc_roofline(m, sp, peaks)
-        n_launch = m.num_kernels()
+        n_launch = m.num_launches()
     finally:
         m.close()
     tokens = 64 * 512
@@ -540,7 +540,7 @@ def main():
 
     peaks = load_peaks()
     roofline, kern, prof = tc_roofline(m, sp, peaks)
-    n_kern = m.num_kernels()
+    n_kern = m.num_launches()
     m.synchronize(sp)
 
     line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,

@@ -106,6 +106,8 @@ struct Runtime {
   cudaGraphExec_t gexec = nullptr;
   cudaGraph_t graph = nullptr;
   std::vector<std::array<TMap, 2>> tmaps;  // per op (TC only)
+  std::vector<int> ksplit;                 // per op (TC only): k splits, 1 = none
+  float* splitk_ws = nullptr;              // partial sums of split contractions (ops run in order: shared)
   ncclComm_t comm = nullptr;
   int world = 1, rank = 0;
   // output bytes of every rank (rank-major, one entry per output), exchanged
@@ -127,6 +129,7 @@ struct Runtime {
     if (persist) cudaFree(persist);
     if (arena) cudaFree(arena);
     if (d_status) cudaFree(d_status);
+    if (splitk_ws) cudaFree(splitk_ws);
     if (own_stream) cudaStreamDestroy(own_stream);
   }
 
@@ -174,6 +177,13 @@ void Runtime::allocate() {
 void Runtime::build_tensor_maps() {
   Plan& P = *plan;
   tmaps.assign(P.ops.size(), {});
+  ksplit.assign(P.ops.size(), 1);
+  int sms = 0;
+  GCHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+  // GAWEE_MAX_KSPLIT caps the k splits of small contractions (1 disables them)
+  int cap = 32;
+  if (const char* e = std::getenv("GAWEE_MAX_KSPLIT")) cap = std::max(1, std::atoi(e));
+  size_t ws_floats = 0;
   for (size_t o = 0; o < P.ops.size(); ++o) {
     const Op& op = P.ops[o];
     if (op.dead || op.kind != OpKind::TC) continue;
@@ -182,6 +192,15 @@ void Runtime::build_tensor_maps() {
     const float* lo = static_cast<const float*>(P.bufs[t.lo].ptr);
     if (!kern::make_b_tensor_maps(hi, lo, t.b_batch, t.N, t.ldk, t.block_n, tmaps[o][0].b, tmaps[o][1].b))
       throw std::runtime_error("cuTensorMapEncodeTiled failed for op " + op.name);
+    int nb = 1;
+    for (int64_t d : t.batch_shape) nb *= (int)d;
+    const int k = std::min(cap, kern::choose_ksplit(t.M, t.N, t.K, nb, t.block_n, t.epi, sms));
+    ksplit[o] = k;
+    if (k > 1) ws_floats = std::max(ws_floats, (size_t)k * (size_t)t.M * (size_t)t.N);
+  }
+  if (ws_floats) {
+    if (cudaMalloc(&splitk_ws, ws_floats * sizeof(float)) != cudaSuccess)
+      throw StatusError(GAWEE_ERR_OOM, "cudaMalloc of the split-K workspace failed");
   }
 }
 
@@ -411,6 +430,10 @@ static void launch_tc(Runtime& rt, int o, const Op& op, cudaStream_t s) {
     if (p.fast != kern::FAST_NONE) p.epi = kern::EPI_FAST;
   }
   p.status = rt.status();
+  if (rt.ksplit[o] > 1 && p.epi <= kern::EPI_BIAS_ADD_RELU) {
+    p.ksplit = rt.ksplit[o];
+    p.ws = rt.splitk_ws;
+  }
   if (!kern::launch_conv_gemm_tc(p, rt.tmaps[o][0].b, rt.tmaps[o][1].b, t.block_n, s))
     throw StatusError(GAWEE_ERR_UNSUPPORTED, "tensor-core launch rejected the shape of op " + op.name);
 }
@@ -911,6 +934,13 @@ gawee_status gawee_set_graph_mode(gawee_ctx* ctx, int enabled) {
 
 int gawee_num_kernels(const gawee_ctx* ctx) { return ctx ? (int)ctx->rt.plan->main.size() : -1; }
 
+int gawee_num_launches(const gawee_ctx* ctx) {
+  if (!ctx) return -1;
+  int n = 0;
+  for (int o : ctx->rt.plan->main) n += 1 + (o < (int)ctx->rt.ksplit.size() && ctx->rt.ksplit[o] > 1 ? 1 : 0);
+  return n;
+}
+
 gawee_status gawee_plan_summary(const gawee_ctx* ctx, char* buf, size_t n) {
   if (!ctx || !buf || n == 0) return GAWEE_ERR_INVALID;
   std::string s = ctx->rt.plan->summary();
@@ -921,9 +951,13 @@ gawee_status gawee_plan_summary(const gawee_ctx* ctx, char* buf, size_t n) {
 
 gawee_status gawee_op_info(const gawee_ctx* ctx, int i, char* name, size_t n, int* is_tc, double* flops) {
   if (!ctx || i < 0 || i >= (int)ctx->rt.plan->main.size()) return GAWEE_ERR_INVALID;
-  const gawee::Op& op = ctx->rt.plan->ops[ctx->rt.plan->main[i]];
+  const int o = ctx->rt.plan->main[i];
+  const gawee::Op& op = ctx->rt.plan->ops[o];
   if (name && n) {
-    std::strncpy(name, op.name.c_str(), n - 1);
+    std::string nm = op.name;
+    if (op.kind == gawee::OpKind::TC && o < (int)ctx->rt.ksplit.size() && ctx->rt.ksplit[o] > 1)
+      nm += " [split-k " + std::to_string(ctx->rt.ksplit[o]) + "]";
+    std::strncpy(name, nm.c_str(), n - 1);
     name[n - 1] = 0;
   }
   if (is_tc) *is_tc = op.kind == gawee::OpKind::TC;

@@ -272,6 +272,23 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   const int64_t m_tiles = (p.M + kBM - 1) / kBM;
   const int64_t n_tiles = (p.N + BN - 1) / BN;
   const int64_t num_tiles = m_tiles * n_tiles * p.nb;
+  // Work units: (tile, k split).  With p.ksplit = S > 1 the rounds of a tile
+  // are cut into S contiguous ranges and unit u covers tile u % tiles over
+  // range u / tiles, writing its partial sums to split slice u / tiles of the
+  // output (a workspace the launcher reduces in split order).  Consecutive
+  // units share their k range, so CTAs running together read the same part
+  // of the B operand.
+  const int ksplit = p.ksplit > 1 ? p.ksplit : 1;
+  const int64_t num_units = num_tiles * ksplit;
+  const uint32_t tiles32 = (uint32_t)num_tiles;
+  auto unit_split = [&](int64_t u, int64_t& t, int& split, int& r_lo, int& nr) {
+    const uint32_t uu = (uint32_t)u;
+    const uint32_t sp = uu / tiles32;
+    t = (int64_t)(uu - sp * tiles32);
+    split = (int)sp;
+    r_lo = (int)(((int64_t)sp * num_rounds) / ksplit);
+    nr = (int)(((int64_t)(sp + 1) * num_rounds) / ksplit) - r_lo;
+  };
 
   // Tile t -> (z, n tile, m tile), m fastest so CTAs running together share B.
   // Tile, row and batch coordinates fit in 32 bits (the launcher checks), so
@@ -285,10 +302,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     n0 = (int)((mn - zz * n_tiles32) * BN);
     z = (int)zz;
   };
-  // Each tile walks its rounds starting at (m tile index mod num_rounds):
-  // CTAs that run side by side then fetch different k-blocks of the shared
-  // B operand instead of all hitting the same L2 lines at once.
-  auto r_rotation = [&](int64_t t) -> int { return (int)(((uint32_t)t % m_tiles32) % (uint32_t)num_rounds); };
+  // Each unit walks its rounds starting at (m tile index mod its round
+  // count): CTAs that run side by side then fetch different k-blocks of the
+  // shared B operand instead of all hitting the same L2 lines at once.
+  auto r_rotation = [&](int64_t t, int nr) -> int { return (int)(((uint32_t)t % m_tiles32) % (uint32_t)nr); };
   auto batch_offsets = [&](int z, int64_t& a_off, int64_t& c_off, int& b_plane) {
     a_off = 0;
     c_off = 0;
@@ -338,15 +355,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     const int chunk = lane & 7;
     const int rsub = lane >> 3;
     const int64_t PQ = p.P * p.Q;
-    const int64_t my_tiles = (int64_t)blockIdx.x < num_tiles ? (num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-    const int64_t G = my_tiles * num_kb;  // k-blocks this CTA runs through
     const uint32_t raw_base = smem_u32(smem + L::kRawOff);
     const uint32_t tmem_rows = tmem_base + ((uint32_t)(warp * 32) << 16);
 
-    // load cursor: tile, k-block, and the chunk's (c, r, s) within the filter window
-    int64_t lt = blockIdx.x;
-    int lkb = 0;  // k-blocks of the current tile issued so far
-    int lka = 0;  // the k-block they are at (rotated order)
+    // load cursor: unit, k-block, and the chunk's (c, r, s) within the filter window
+    int64_t lu = blockIdx.x;  // unit being loaded
+    int lkb = 0;              // k-blocks of the current unit issued so far
+    int lka = 0;              // the k-block they are at (rotated order)
+    int l_kb_lo = 0, l_kb_hi = 0;  // the unit's k-block range
     int64_t li = 0;
     int64_t rowoff[8];
     int ih0[8], iw0[8];
@@ -362,8 +378,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       ks = rs - kr * p.S;
     };
     auto start_tile = [&]() {
-      int64_t m0, a_off, c_off;
-      int n0, z, b_plane;
+      int64_t m0, a_off, c_off, lt;
+      int n0, z, b_plane, lsplit, lr_lo, lnr;
+      unit_split(lu, lt, lsplit, lr_lo, lnr);
+      l_kb_lo = lr_lo * kRK;
+      l_kb_hi = min((lr_lo + lnr) * kRK, num_kb);
       tile_coords(lt, m0, n0, z);
       batch_offsets(z, a_off, c_off, b_plane);
 #pragma unroll
@@ -383,11 +402,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           rowoff[i] = 0;
         }
       }
-      lka = r_rotation(lt) * kRK;
+      lka = l_kb_lo + r_rotation(lt, lnr) * kRK;
       decompose(lka * kBK + chunk * 4);
     };
     auto issue = [&]() {
-      if (li < G) {
+      if (lu < num_units) {
         if (lkb == 0) start_tile();
         const uint32_t slot = raw_base + (uint32_t)((li % RD) * L::kATile);
         const bool kin = (int64_t)lka * kBK + chunk * 4 < p.K;
@@ -400,13 +419,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           cp_async16(slot + row * 128 + ((chunk ^ (row & 7)) << 4),
                      ok ? (const void*)(p.x + rowoff[i] + koff) : (const void*)p.x, ok ? 16u : 0u);
         }
-        // next k-block of the same chunk: k advances by 32 (wrapping to 0)
-        if (++lkb == num_kb) {
+        // next k-block of the same chunk: k advances by 32 (wrapping to the
+        // start of the unit's range)
+        if (++lkb == l_kb_hi - l_kb_lo) {
           lkb = 0;
-          lt += gridDim.x;
-        } else if (++lka == num_kb) {
-          lka = 0;
-          decompose(chunk * 4);
+          lu += gridDim.x;
+        } else if (++lka == l_kb_hi) {
+          lka = l_kb_lo;
+          decompose(lka * kBK + chunk * 4);
         } else if (tap_step) {
           ks += tap_step;
           while (ks >= p.S) {
@@ -437,11 +457,15 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     int sa = 0;           // round slot
     uint32_t free_ph = 1;  // parity of the slot's previous round completing (fresh: passes)
     bool alive = true;
-    for (int64_t t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
-      const int rot = r_rotation(t);
-      for (int rr = 0; rr < num_rounds && alive; ++rr) {
+    for (int64_t u = blockIdx.x; u < num_units && alive; u += gridDim.x) {
+      int64_t t;
+      int split, r_lo, nr;
+      unit_split(u, t, split, r_lo, nr);
+      const int rot = r_rotation(t, nr);
+      for (int rr = 0; rr < nr && alive; ++rr) {
         int r = rot + rr;
-        if (r >= num_rounds) r -= num_rounds;
+        if (r >= nr) r -= nr;
+        r += r_lo;
         const int nk = round_kbs(r);
         if (!mbar_wait(smem_u32(&rdone[sa]), free_ph, abort_flag, p.status)) {
           alive = false;
@@ -493,15 +517,17 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       int sb = 0;
       uint32_t free_ph = 1;
       bool alive = true;
-      for (int64_t t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
-        int64_t m0, a_off, c_off;
-        int n0, z, b_plane;
+      for (int64_t u = blockIdx.x; u < num_units && alive; u += gridDim.x) {
+        int64_t m0, a_off, c_off, t;
+        int n0, z, b_plane, split, r_lo, nr;
+        unit_split(u, t, split, r_lo, nr);
         tile_coords(t, m0, n0, z);
         batch_offsets(z, a_off, c_off, b_plane);
-        const int rot = r_rotation(t);
-        for (int rr = 0; rr < num_rounds; ++rr) {
+        const int rot = r_rotation(t, nr);
+        for (int rr = 0; rr < nr; ++rr) {
           int r = rot + rr;
-          if (r >= num_rounds) r -= num_rounds;
+          if (r >= nr) r -= nr;
+          r += r_lo;
           const int nk = round_kbs(r);
           if (!mbar_wait(smem_u32(&rdone[sb]), free_ph, abort_flag, p.status)) {
             alive = false;
@@ -545,11 +571,15 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     int sl = 0;            // round slot
     uint32_t rdy_ph = 0;   // parity of the slot's ready phase for this round
     bool alive = true;
-    for (int64_t t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
-      const int rot = r_rotation(t);
-      for (int rr = 0; rr < num_rounds; ++rr) {
+    for (int64_t u = blockIdx.x; u < num_units && alive; u += gridDim.x) {
+      int64_t t;
+      int split, r_lo, nr;
+      unit_split(u, t, split, r_lo, nr);
+      const int rot = r_rotation(t, nr);
+      for (int rr = 0; rr < nr; ++rr) {
         int r = rot + rr;
-        if (r >= num_rounds) r -= num_rounds;
+        if (r >= nr) r -= nr;
+        r += r_lo;
         const int nk = round_kbs(r);
         if (!mbar_wait(smem_u32(&ready[sl]), rdy_ph, abort_flag, p.status)) {
           alive = false;
@@ -610,15 +640,17 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     // every accumulator starts drained: count toward the first round of each slot
     if (lane == 0)
       for (int k = 0; k < kS; ++k) mbar_arrive(smem_u32(&ready[k]));
-    for (int64_t t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-      int64_t m0, a_off, c_off;
-      int n0, z, b_plane;
+    for (int64_t u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+      int64_t m0, a_off, c_off, t;
+      int n0, z, b_plane, split, r_lo, nr;
+      unit_split(u, t, split, r_lo, nr);
       tile_coords(t, m0, n0, z);
       batch_offsets(z, a_off, c_off, b_plane);
+      c_off += (int64_t)split * p.split_stride;  // partial sums: this split's slice of the workspace
       float acc[HB];
 #pragma unroll
       for (int j = 0; j < HB; ++j) acc[j] = 0.0f;
-      for (int r = 0; r < num_rounds; ++r) {
+      for (int r = 0; r < nr; ++r) {
         const int buf = sl;
         // warp-uniform outcome: the epilogue below uses warp-collective steps
         if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&rdone[sl]), done_ph, abort_flag, p.status))) {
@@ -970,6 +1002,49 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   }
 }
 
+// Split-K reduction: out = epilogue(sum over splits of ws[s]) in split order
+// (deterministic), with the same epilogue operations as the tensor-core
+// kernel: acc + bias[n], + res[m][n], max(., 0).  Four columns per thread.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const __grid_constant__ ConvGemmParams p) {
+  const int64_t n4 = (p.N + 3) / 4;
+  const int64_t total = p.M * n4;
+  const bool vin = (p.N & 3) == 0;
+  const bool vout = vin && p.ldc_n == 1 && (p.ldc & 3) == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 &&
+                    (p.epi != EPI_BIAS_ADD_RELU || (reinterpret_cast<uintptr_t>(p.res) & 15) == 0);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / n4;
+    const int64_t n = (i - m * n4) * 4;
+    float x[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int sp = 0; sp < p.ksplit; ++sp) {
+      const float* w = p.ws + sp * p.split_stride + m * p.N + n;
+      if (vin) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(w));
+        x[0] = __fadd_rn(x[0], v.x); x[1] = __fadd_rn(x[1], v.y);
+        x[2] = __fadd_rn(x[2], v.z); x[3] = __fadd_rn(x[3], v.w);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (n + e < p.N) x[e] = __fadd_rn(x[e], __ldg(w + e));
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (n + e >= p.N) continue;
+      if (p.epi >= EPI_BIAS) x[e] = __fadd_rn(x[e], __ldg(p.bias + n + e));
+      if (p.epi == EPI_BIAS_ADD_RELU) x[e] = __fadd_rn(x[e], __ldg(p.res + m * p.ldc + (n + e) * p.ldc_n));
+      if (p.epi == EPI_BIAS_RELU || p.epi == EPI_BIAS_ADD_RELU) x[e] = maximumf_(x[e], 0.0f);
+    }
+    float* o = p.out + m * p.ldc;
+    if (vout) {
+      *reinterpret_cast<float4*>(o + n) = make_float4(x[0], x[1], x[2], x[3]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (n + e < p.N) o[(n + e) * p.ldc_n] = x[e];
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
@@ -1009,8 +1084,8 @@ bool launch_t(const ConvGemmParams& p, const void* tmh, const void* tml, cudaStr
   int sms = 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (sms <= 0) sms = 148;
-  const int64_t tiles = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN) * p.nb;
-  dim3 grid((unsigned)std::min<int64_t>(tiles, sms), 1, 1);
+  const int64_t units = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN) * p.nb * std::max(1, p.ksplit);
+  dim3 grid((unsigned)std::min<int64_t>(units, sms), 1, 1);
   kern<<<grid, kThreadsTC, smem, s>>>(p, *static_cast<const CUtensorMap*>(tmh), *static_cast<const CUtensorMap*>(tml));
   return true;
 }
@@ -1055,9 +1130,48 @@ bool make_b_tensor_maps(const float* hi, const float* lo, int64_t batch, int64_t
   return true;
 }
 
-bool launch_conv_gemm_tc(const ConvGemmParams& p, const void* tmap_hi, const void* tmap_lo, int block_n,
+int choose_ksplit(int64_t M, int64_t N, int64_t K, int nb, int block_n, int epi, int sms) {
+  if (nb != 1 || epi > EPI_BIAS_ADD_RELU || M <= 0 || N <= 0 || K <= 0 || sms <= 0) return 1;
+  const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + block_n - 1) / block_n);
+  const int rounds = (int)(((K + kBK - 1) / kBK + kRK - 1) / kRK);
+  // Estimated time in rounds: waves of units x (rounds per unit + the fixed
+  // cost of a unit: pipeline fill and epilogue, about 1.5 rounds), plus the
+  // reduce pass (about half a round per extra split of a tile's outputs).
+  auto cost = [&](int S) {
+    const int64_t units = tiles * S;
+    const int64_t waves = (units + sms - 1) / sms;
+    const double per = (double)((rounds + S - 1) / S) + 1.5;
+    return (double)waves * per + (S > 1 ? 0.5 + 0.25 * S : 0.0);
+  };
+  int best = 1;
+  double best_cost = cost(1);
+  for (int S = 2; S <= std::min(rounds, 32); ++S) {
+    const double c = cost(S);
+    if (c < best_cost * 0.97) {  // a split must win clearly to pay for its workspace traffic
+      best = S;
+      best_cost = c;
+    }
+  }
+  return best;
+}
+
+bool launch_conv_gemm_tc(const ConvGemmParams& p_in, const void* tmap_hi, const void* tmap_lo, int block_n,
                          cudaStream_t s) {
+  ConvGemmParams p = p_in;
   if (p.M <= 0 || p.N <= 0 || p.nb <= 0) return true;
+  if (p.ksplit > 1) {
+    const int rounds = (int)(((p.K + kBK - 1) / kBK + kRK - 1) / kRK);
+    if (!p.ws || p.nb != 1 || p.epi > EPI_BIAS_ADD_RELU || p.ksplit > rounds) return false;
+    // the tensor-core pass writes raw partial sums into the workspace slices
+    p.out = p.ws;
+    p.ldc = p.N;
+    p.ldc_n = 1;
+    p.epi = EPI_NONE;
+    p.split_stride = p.M * p.N;
+  } else {
+    p.ksplit = 1;
+    p.split_stride = 0;
+  }
   if (p.K <= 0) return false;  // an empty reduction would leave tensor memory unwritten
   // 16-byte A gathers need channel counts and strides in whole float4s
   if (p.C % 4 != 0 || p.x_sh % 4 != 0 || p.x_sw % 4 != 0 || p.x_sn % 4 != 0 ||
@@ -1069,9 +1183,20 @@ bool launch_conv_gemm_tc(const ConvGemmParams& p, const void* tmap_hi, const voi
   // tile, row and batch coordinates use 32-bit arithmetic in the kernel
   const int64_t tiles = ((p.M + kBM - 1) / kBM) * ((p.N + block_n - 1) / block_n) * p.nb;
   if (p.M >= (int64_t(1) << 31) || tiles >= (int64_t(1) << 31) || p.P * p.Q >= (int64_t(1) << 31)) return false;
-  if (block_n == 64) return launch_epi<64>(p, tmap_hi, tmap_lo, s);
-  if (block_n == 128) return launch_epi<128>(p, tmap_hi, tmap_lo, s);
-  return false;
+  const int64_t units = tiles * p.ksplit;
+  if (units >= (int64_t(1) << 31)) return false;
+  bool ok = false;
+  if (block_n == 64) ok = launch_epi<64>(p, tmap_hi, tmap_lo, s);
+  else if (block_n == 128) ok = launch_epi<128>(p, tmap_hi, tmap_lo, s);
+  if (!ok) return false;
+  if (p.ksplit > 1) {
+    ConvGemmParams r = p_in;
+    r.split_stride = p.split_stride;
+    const int64_t work = p.M * ((p.N + 3) / 4);
+    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, 148 * 16));
+    splitk_reduce_kernel<<<grid, 256, 0, s>>>(r);
+  }
+  return true;
 }
 
 }  // namespace kern

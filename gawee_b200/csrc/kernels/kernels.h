@@ -271,6 +271,13 @@ struct ConvGemmParams {
   int fast;
   float fast_c;
   int* status;
+  // Split-K (conv and unbatched GEMM with EPI_NONE .. EPI_BIAS_ADD_RELU):
+  // ksplit > 1 cuts each tile's k range into ksplit parts whose partial sums
+  // go to `ws` ([ksplit][M][N], dense), then a reduce kernel adds them in
+  // split order and applies the epilogue.  The launcher fills split_stride.
+  int ksplit;
+  float* ws;
+  int64_t split_stride;
 };
 
 enum FastEpi : int {
@@ -284,6 +291,11 @@ enum FastEpi : int {
 // Returns false (and launches nothing) when the shape is not supported.
 bool launch_conv_gemm_tc(const ConvGemmParams& p, const void* tmap_hi, const void* tmap_lo, int block_n,
                          cudaStream_t s);
+
+// Number of k splits for a contraction of this shape on `sms` SMs (1 = no
+// split): splitting pays when the output tiles leave SMs idle.  The
+// workspace it needs is ksplit * M * N floats (0 when ksplit is 1).
+int choose_ksplit(int64_t M, int64_t N, int64_t K, int nb, int block_n, int epi, int sms);
 
 // Build the TMA descriptors for packed B planes [batch][N][ldk] (fp32).
 bool make_b_tensor_maps(const float* hi, const float* lo, int64_t batch, int64_t N, int64_t ldk, int block_n,

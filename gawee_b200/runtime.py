@@ -65,6 +65,7 @@ def load_library(path: str = LIB_PATH):
             "gawee_set_graph_mode": (c.c_int, [P, c.c_int]),
             "gawee_plan_text": (c.c_int, [c.c_char_p, c.c_char_p, c.c_char_p, c.c_size_t]),
             "gawee_num_kernels": (c.c_int, [P]),
+            "gawee_num_launches": (c.c_int, [P]),
             "gawee_plan_summary": (c.c_int, [P, c.c_char_p, c.c_size_t]),
             "gawee_op_info": (c.c_int, [P, c.c_int, c.c_char_p, c.c_size_t, c.POINTER(c.c_int),
                                         c.POINTER(c.c_double)]),
@@ -197,6 +198,10 @@ class Model:
         self.forward()
         self.synchronize()
         return [self.output(i) for i in range(len(self.output_specs))]
+
+    def num_launches(self) -> int:
+        """Kernel launches of one forward (split contractions add a reduce kernel)."""
+        return self._lib.gawee_num_launches(self._h)
 
     def num_kernels(self) -> int:
         return self._lib.gawee_num_kernels(self._h)

@@ -122,9 +122,12 @@ gawee_status gawee_profile_forward(gawee_ctx* ctx, void* stream, float* ms, int 
  * plan summary (or the error message) into buf.  No CUDA call is made. */
 gawee_status gawee_plan_text(const char* mlir_text, const char* entry, char* buf, size_t n);
 
-/* Kernels launched by one forward (planned main-sequence steps) and a
- * human-readable plan summary. */
+/* Planned main-sequence steps of one forward (the index space of
+ * gawee_op_info / gawee_profile_forward) and a human-readable plan summary.
+ * gawee_num_launches counts the kernel launches of one forward: a step whose
+ * contraction is split along k adds a reduce kernel. */
 int gawee_num_kernels(const gawee_ctx* ctx);
+int gawee_num_launches(const gawee_ctx* ctx);
 gawee_status gawee_plan_summary(const gawee_ctx* ctx, char* buf, size_t n);
 
 /* ---------------------------------------------------------------------------

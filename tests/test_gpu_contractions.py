@@ -1,4 +1,6 @@
 """Tensor-core contractions (3xTF32 tcgen05) against the oracle's sequential fp32 sums."""
+import math
+
 import numpy as np
 import pytest
 
@@ -136,3 +138,60 @@ def test_conv_residual_block():
         y = g.op("conv", [y, w2, b2], att, F, (2, 32, 10, 10))
         return [g.relu(g.add(y, x))]
     parity(*build(g_), atol=1e-4, rtol=1e-4)
+
+
+def _run_with_split_cap(mlir, args, cap):
+    import os
+
+    from gawee_b200.runtime import Model
+    old = os.environ.get("GAWEE_MAX_KSPLIT")
+    os.environ["GAWEE_MAX_KSPLIT"] = str(cap)
+    try:
+        m = Model(mlir)
+    finally:
+        if old is None:
+            del os.environ["GAWEE_MAX_KSPLIT"]
+        else:
+            os.environ["GAWEE_MAX_KSPLIT"] = old
+    try:
+        names = [n for n, _, _ in m.kernels()]
+        outs = [m.run(args)[0] for _ in range(2)]  # eager, then the replayed graph
+    finally:
+        m.close()
+    return names, outs
+
+
+@pytest.mark.parametrize("case", ["gemm", "conv_residual", "conv_stride2"])
+def test_split_k_matches_oracle_and_unsplit(case):
+    """Small-M contractions split along k (partial sums in a workspace, a
+    reduce kernel adds them in split order and applies bias / residual /
+    ReLU): same results as the unsplit kernel and the oracle, within the
+    fp32 tolerance of the contraction tests."""
+    import oracle
+
+    def g_(g):
+        if case == "gemm":
+            a = rand_input(g, (49, 4608), 11)
+            b = rand_input(g, (4608, 520), 12)
+            return [g.matmul(a, b)]
+        x = rand_input(g, (1, 256, 14, 14) if case == "conv_stride2" else (1, 512, 7, 7), 13)
+        cin = x.shape[1]
+        cout = 512
+        stride = 2 if case == "conv_stride2" else 1
+        w = g.normal((cout, cin, 3, 3), math.sqrt(2.0 / (cin * 9)))
+        bias = g.normal((cout,), 0.01)
+        y = g.op("conv", [x, w, bias], {"strides": _arr([stride, stride]), "padding": _arr([1, 1]),
+                                        "dilation": _arr([1, 1])}, F, (1, cout, 7, 7))
+        if case == "conv_residual":
+            y = g.relu(g.add(y, x))
+        return [y]
+    mlir, args = build(g_)
+    want = oracle.run(mlir, args)[0]
+    names1, outs1 = _run_with_split_cap(mlir, args, 1)
+    names, outs = _run_with_split_cap(mlir, args, 32)
+    assert not any("split-k" in n for n in names1)
+    assert any("split-k" in n for n in names), names
+    k = 4608 if case == "gemm" else args[0].shape[1] * 9
+    atol = 1e-4 * max(1.0, np.sqrt(k) / 8)
+    for o in outs1 + outs:
+        compare(o, want, atol, 1e-4, case)

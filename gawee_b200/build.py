@@ -24,6 +24,7 @@ BIN = os.path.join(HERE, "bin")
 SOURCES = [
     "kernels/memory_ops.cu",
     "kernels/conv_gemm_tc.cu",
+    "kernels/conv_gemm_tma.cu",
     "kernels/noalloc_gemm.cu",
     "host/ir.cpp",
     "host/plan.cpp",
@@ -32,7 +33,7 @@ SOURCES = [
 TOOLS = {
     "gawee-cuda-runner": "tools/gawee_cuda_runner.cpp",
 }
-HEADERS = ["kernels/kernels.h", "kernels/program.cuh", "host/ir.h", "host/plan.h", "host/launch.h", "host/npy.h"]
+HEADERS = ["kernels/kernels.h", "kernels/program.cuh", "kernels/tc_common.cuh", "host/ir.h", "host/plan.h", "host/launch.h", "host/npy.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",

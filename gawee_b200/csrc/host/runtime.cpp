@@ -105,7 +105,8 @@ struct Runtime {
   int forwards = 0;
   cudaGraphExec_t gexec = nullptr;
   cudaGraph_t graph = nullptr;
-  std::vector<std::array<TMap, 2>> tmaps;  // per op (TC only)
+  std::vector<std::array<TMap, 3>> tmaps;  // per op (TC only): B hi, B lo, A (TMA-fed kernel)
+  std::vector<int> a_tma;                  // per op (TC only): kern::ATma, A_TMA_NONE = warp gather
   std::vector<int> ksplit;                 // per op (TC only): k splits, 1 = none
   float* splitk_ws = nullptr;              // partial sums of split contractions (ops run in order: shared)
   ncclComm_t comm = nullptr;
@@ -178,6 +179,10 @@ void Runtime::build_tensor_maps() {
   Plan& P = *plan;
   tmaps.assign(P.ops.size(), {});
   ksplit.assign(P.ops.size(), 1);
+  a_tma.assign(P.ops.size(), kern::A_TMA_NONE);
+  // GAWEE_TC_TMA=0 keeps every contraction on the warp-gather kernel
+  bool use_tma = true;
+  if (const char* e = std::getenv("GAWEE_TC_TMA")) use_tma = std::atoi(e) != 0;
   int sms = 0;
   GCHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
   // GAWEE_MAX_KSPLIT caps the k splits of small contractions (1 disables them)
@@ -194,6 +199,22 @@ void Runtime::build_tensor_maps() {
       throw std::runtime_error("cuTensorMapEncodeTiled failed for op " + op.name);
     int nb = 1;
     for (int64_t d : t.batch_shape) nb *= (int)d;
+    // A by TMA when the copy engine can address it: a convolution over whole
+    // 32-channel k-blocks (im2col), or an unbatched GEMM with aligned rows
+    if (use_tma && nb == 1) {
+      const float* x = reinterpret_cast<const float*>(ptr(t.x));
+      if (t.conv && t.C % 32 == 0) {
+        if (kern::make_a_tensor_map_im2col(x, t.x.shape[0], t.H, t.W, t.C, t.x.shape[0] > 1 ? t.x.st[0] : 0,
+                                           t.x.st[2], t.x.st[3], t.R, t.S, t.sh, t.sw, t.ph, t.pw, t.dh, t.dw,
+                                           tmaps[o][2].b))
+          a_tma[o] = kern::A_TMA_IM2COL;
+      } else if (!t.conv) {
+        const int r = t.x.rank();
+        if (t.x.st[r - 1] == 1 &&
+            kern::make_a_tensor_map_2d(x, t.M, t.K, t.M > 1 ? t.x.st[r - 2] : 0, tmaps[o][2].b))
+          a_tma[o] = kern::A_TMA_2D;
+      }
+    }
     const int k = std::min(cap, kern::choose_ksplit(t.M, t.N, t.K, nb, t.block_n, t.epi, sms));
     ksplit[o] = k;
     if (k > 1) ws_floats = std::max(ws_floats, (size_t)k * (size_t)t.M * (size_t)t.N);
@@ -434,8 +455,14 @@ static void launch_tc(Runtime& rt, int o, const Op& op, cudaStream_t s) {
     p.ksplit = rt.ksplit[o];
     p.ws = rt.splitk_ws;
   }
-  if (!kern::launch_conv_gemm_tc(p, rt.tmaps[o][0].b, rt.tmaps[o][1].b, t.block_n, s))
-    throw StatusError(GAWEE_ERR_UNSUPPORTED, "tensor-core launch rejected the shape of op " + op.name);
+  bool launched;
+  if (rt.a_tma[o] != kern::A_TMA_NONE) {
+    p.a_tma = rt.a_tma[o];
+    launched = kern::launch_conv_gemm_tma(p, rt.tmaps[o][2].b, rt.tmaps[o][0].b, rt.tmaps[o][1].b, t.block_n, s);
+  } else {
+    launched = kern::launch_conv_gemm_tc(p, rt.tmaps[o][0].b, rt.tmaps[o][1].b, t.block_n, s);
+  }
+  if (!launched) throw StatusError(GAWEE_ERR_UNSUPPORTED, "tensor-core launch rejected the shape of op " + op.name);
 }
 
 void Runtime::run_op(int o, cudaStream_t s) {
@@ -955,6 +982,8 @@ gawee_status gawee_op_info(const gawee_ctx* ctx, int i, char* name, size_t n, in
   const gawee::Op& op = ctx->rt.plan->ops[o];
   if (name && n) {
     std::string nm = op.name;
+    if (op.kind == gawee::OpKind::TC && o < (int)ctx->rt.a_tma.size() && ctx->rt.a_tma[o] != gawee::kern::A_TMA_NONE)
+      nm += ctx->rt.a_tma[o] == gawee::kern::A_TMA_IM2COL ? " [tma im2col]" : " [tma]";
     if (op.kind == gawee::OpKind::TC && o < (int)ctx->rt.ksplit.size() && ctx->rt.ksplit[o] > 1)
       nm += " [split-k " + std::to_string(ctx->rt.ksplit[o]) + "]";
     std::strncpy(name, nm.c_str(), n - 1);

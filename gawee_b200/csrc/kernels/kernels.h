@@ -278,6 +278,16 @@ struct ConvGemmParams {
   int ksplit;
   float* ws;
   int64_t split_stride;
+  // A operand source for launch_conv_gemm_tma (ATma): an im2col tensor map
+  // over the NHWC input (convolutions, C a multiple of 32) or a tiled map over
+  // the GEMM rows.
+  int a_tma;
+};
+
+enum ATma : int {
+  A_TMA_NONE = 0,    // A gathered by warps (launch_conv_gemm_tc)
+  A_TMA_2D = 1,      // tiled 2-D tensor map over rows [M][K] (row stride ld)
+  A_TMA_IM2COL = 2,  // im2col tensor map over the NHWC convolution input
 };
 
 enum FastEpi : int {
@@ -296,6 +306,25 @@ bool launch_conv_gemm_tc(const ConvGemmParams& p, const void* tmap_hi, const voi
 // split): splitting pays when the output tiles leave SMs idle.  The
 // workspace it needs is ksplit * M * N floats (0 when ksplit is 1).
 int choose_ksplit(int64_t M, int64_t N, int64_t K, int nb, int block_n, int epi, int sms);
+
+// The split-K reduction of launch_conv_gemm_tc / launch_conv_gemm_tma: out =
+// epilogue(sum over splits of ws[s]) in split order; p as given to the launch.
+void launch_splitk_reduce(const ConvGemmParams& p, int64_t split_stride, cudaStream_t s);
+
+// The TMA-fed kernel (conv_gemm_tma.cu): A by TMA (ConvGemmParams::a_tma and
+// the map below), B as for launch_conv_gemm_tc.  Unbatched (nb == 1) only.
+bool launch_conv_gemm_tma(const ConvGemmParams& p, const void* tmap_a, const void* tmap_hi, const void* tmap_lo,
+                          int block_n, cudaStream_t s);
+
+// A-operand tensor maps for launch_conv_gemm_tma.  im2col: NHWC input with
+// element strides x_sn, x_sh, x_sw (channel stride 1, C a multiple of 32), the
+// convolution's filter size, stride, padding and dilation.  2d: rows [M][K]
+// with row stride ld (elements).  Return false when TMA cannot express it.
+bool make_a_tensor_map_im2col(const float* x, int64_t images, int64_t H, int64_t W, int64_t C, int64_t x_sn,
+                              int64_t x_sh, int64_t x_sw, int R, int S, int sh, int sw, int ph, int pw, int dh,
+                              int dw, void* tmap_out);
+bool make_a_tensor_map_2d(const float* x, int64_t M, int64_t K, int64_t ld, void* tmap_out);
+int conv_gemm_tma_smem_bytes(int block_n);
 
 // Build the TMA descriptors for packed B planes [batch][N][ldk] (fp32).
 bool make_b_tensor_maps(const float* hi, const float* lo, int64_t batch, int64_t N, int64_t ldk, int block_n,

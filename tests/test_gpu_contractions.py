@@ -195,3 +195,78 @@ def test_split_k_matches_oracle_and_unsplit(case):
     atol = 1e-4 * max(1.0, np.sqrt(k) / 8)
     for o in outs1 + outs:
         compare(o, want, atol, 1e-4, case)
+
+
+def _run_env(mlir, args, env):
+    import os
+
+    from gawee_b200.runtime import Model
+    old = {k: os.environ.get(k) for k in env}
+    os.environ.update({k: str(v) for k, v in env.items()})
+    try:
+        m = Model(mlir)
+    finally:
+        for k, v in old.items():
+            if v is None:
+                del os.environ[k]
+            else:
+                os.environ[k] = v
+    try:
+        names = [n for n, _, _ in m.kernels()]
+        outs = [m.run(args) for _ in range(2)]  # eager, then the replayed graph
+    finally:
+        m.close()
+    return names, outs
+
+
+TMA_CONVS = [
+    # (N, C, H, W, F, k, stride, pad, dil): channel counts that are multiples of 32 take the TMA kernel
+    (3, 32, 9, 11, 40, 3, 1, 1, 1),     # tiles span images; F not a multiple of 64
+    (2, 64, 17, 17, 64, 3, 2, 1, 1),    # stride 2
+    (1, 96, 12, 10, 130, 5, 1, 2, 1),   # 5x5, three 32-channel k-blocks per tap
+    (2, 32, 13, 13, 48, 3, 1, 2, 2),    # dilation 2
+    (2, 64, 14, 14, 128, 1, 2, 0, 1),   # 1x1 stride-2 downsample
+    (1, 32, 23, 21, 64, 7, 2, 3, 1),    # 7x7 stride 2 pad 3: corners -3 / -3
+]
+
+
+@pytest.mark.parametrize("n,c,h,w,f,k,s,p,d", TMA_CONVS)
+def test_conv_tma_im2col_matches_gather_and_oracle(n, c, h, w, f, k, s, p, d):
+    """The TMA-fed kernel (im2col tensor map for A) against the oracle and
+    against the warp-gather kernel on the same graph."""
+    import oracle
+    ho = (h + 2 * p - d * (k - 1) - 1) // s + 1
+    wo = (w + 2 * p - d * (k - 1) - 1) // s + 1
+
+    def g_(g):
+        x = rand_input(g, (n, c, h, w), 41)
+        wt = rand_input(g, (f, c, k, k), 42, scale=float(np.sqrt(2.0 / (c * k * k))))
+        b = rand_input(g, (f,), 43, scale=0.1)
+        y = g.op("conv", [x, wt, b], {"strides": _arr([s, s]), "padding": _arr([p, p]), "dilation": _arr([d, d])},
+                 F, (n, f, ho, wo))
+        return [g.relu(y)]
+    mlir, args = build(g_)
+    want = oracle.run(mlir, args)[0]
+    names, outs = _run_env(mlir, args, {"GAWEE_MAX_KSPLIT": 1})
+    names_g, outs_g = _run_env(mlir, args, {"GAWEE_MAX_KSPLIT": 1, "GAWEE_TC_TMA": 0})
+    assert any("tma im2col" in nm for nm in names), names
+    assert not any("tma" in nm for nm in names_g), names_g
+    for o in outs + outs_g:
+        compare(o[0], want, 1e-4, 1e-4, "conv")
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 36, 70), (200, 300, 130), (129, 64, 64), (517, 1000, 257)])
+def test_gemm_tma_rows_matches_oracle(m, k, n):
+    """Unbatched GEMMs take A through a tiled tensor map (K tails zero-filled by the copy engine)."""
+    import oracle
+
+    def g_(g):
+        a = rand_input(g, (m, k), 51)
+        b = rand_input(g, (k, n), 52)
+        return [g.matmul(a, b)]
+    mlir, args = build(g_)
+    want = oracle.run(mlir, args)[0]
+    names, outs = _run_env(mlir, args, {})
+    assert any("[tma]" in nm for nm in names), names
+    for o in outs:
+        compare(o[0], want, 1e-4 * max(1.0, np.sqrt(k) / 8), 1e-4, "gemm")

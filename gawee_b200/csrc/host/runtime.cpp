@@ -175,6 +175,41 @@ void Runtime::allocate() {
   pack_done.assign(P.ops.size(), 0);
 }
 
+// Batch dims of a GEMM that only continue its rows are merged into M: B is
+// broadcast along them and every other operand's stride along them equals
+// the rows so far times its row stride (A, C and the epilogue's aux
+// operands), innermost batch dim first.  The kernels then see one larger
+// product with fewer (usually no) batch dims, e.g. a [64, 512, 576] x
+// [576, N] projection becomes a single 32768-row GEMM.
+struct GemmRows {
+  int64_t M;
+  int batch_rank;  // outer batch dims left
+};
+static GemmRows merged_rows(const Op& op) {
+  const auto& t = op.tc;
+  GemmRows g{t.M, t.batch_rank};
+  if (t.conv || t.M <= 1) return g;
+  const int ra = t.x.rank(), rc = t.out.rank();
+  while (g.batch_rank > 0) {
+    const int d = g.batch_rank - 1;
+    const int64_t bs = t.batch_shape[d];
+    if (bs != 1) {
+      if (t.b_bst[d] != 0) break;
+      if (t.a_bst[d] != g.M * t.x.st[ra - 2]) break;
+      if (t.out.st[d] != g.M * t.out.st[rc - 2]) break;
+      bool aux_ok = true;
+      for (const View& v : t.aux) {
+        const int rv = v.rank();
+        if (v.st[d] != g.M * v.st[rv - 2]) aux_ok = false;
+      }
+      if (!aux_ok) break;
+    }
+    g.M *= bs;
+    --g.batch_rank;
+  }
+  return g;
+}
+
 void Runtime::build_tensor_maps() {
   Plan& P = *plan;
   tmaps.assign(P.ops.size(), {});
@@ -197,8 +232,9 @@ void Runtime::build_tensor_maps() {
     const float* lo = static_cast<const float*>(P.bufs[t.lo].ptr);
     if (!kern::make_b_tensor_maps(hi, lo, t.b_batch, t.N, t.ldk, t.block_n, tmaps[o][0].b, tmaps[o][1].b))
       throw std::runtime_error("cuTensorMapEncodeTiled failed for op " + op.name);
+    const GemmRows gr = merged_rows(op);
     int nb = 1;
-    for (int64_t d : t.batch_shape) nb *= (int)d;
+    for (int d = 0; d < gr.batch_rank; ++d) nb *= (int)t.batch_shape[d];
     // A by TMA when the copy engine can address it: a convolution over whole
     // 32-channel k-blocks (im2col), or an unbatched GEMM with aligned rows
     if (use_tma && nb == 1) {
@@ -211,13 +247,13 @@ void Runtime::build_tensor_maps() {
       } else if (!t.conv) {
         const int r = t.x.rank();
         if (t.x.st[r - 1] == 1 &&
-            kern::make_a_tensor_map_2d(x, t.M, t.K, t.M > 1 ? t.x.st[r - 2] : 0, tmaps[o][2].b))
+            kern::make_a_tensor_map_2d(x, gr.M, t.K, gr.M > 1 ? t.x.st[r - 2] : 0, tmaps[o][2].b))
           a_tma[o] = kern::A_TMA_2D;
       }
     }
-    const int k = std::min(cap, kern::choose_ksplit(t.M, t.N, t.K, nb, t.block_n, t.epi, sms));
+    const int k = std::min(cap, kern::choose_ksplit(gr.M, t.N, t.K, nb, t.block_n, t.epi, sms));
     ksplit[o] = k;
-    if (k > 1) ws_floats = std::max(ws_floats, (size_t)k * (size_t)t.M * (size_t)t.N);
+    if (k > 1) ws_floats = std::max(ws_floats, (size_t)k * (size_t)gr.M * (size_t)t.N);
   }
   if (ws_floats) {
     if (cudaMalloc(&splitk_ws, ws_floats * sizeof(float)) != cudaSuccess)
@@ -415,9 +451,11 @@ static void launch_tc(Runtime& rt, int o, const Op& op, cudaStream_t s) {
   p.H = t.H; p.W = t.W; p.C = t.C; p.P = t.P; p.Q = t.Q;
   p.R = t.R; p.S = t.S; p.sh = t.sh; p.sw = t.sw; p.ph = t.ph; p.pw = t.pw; p.dh = t.dh; p.dw = t.dw;
   p.M = t.M; p.N = t.N; p.K = t.K;
+  const GemmRows gr = merged_rows(op);
+  if (gr.M != t.M) p.M = p.P = p.H = gr.M;  // batch dims merged into the rows (a GEMM: H = P = M, Q = 1)
   p.nb = 1;
-  p.batch_rank = t.batch_rank;
-  for (int d = 0; d < t.batch_rank; ++d) {
+  p.batch_rank = gr.batch_rank;
+  for (int d = 0; d < gr.batch_rank; ++d) {
     p.batch_shape[d] = t.batch_shape[d];
     p.a_bst[d] = t.a_bst[d];
     p.b_bst[d] = t.b_bst[d];

@@ -270,3 +270,24 @@ def test_gemm_tma_rows_matches_oracle(m, k, n):
     assert any("[tma]" in nm for nm in names), names
     for o in outs:
         compare(o[0], want, 1e-4 * max(1.0, np.sqrt(k) / 8), 1e-4, "gemm")
+
+
+def test_batched_lhs_rows_merge_into_one_gemm():
+    """A batched lhs times a 2-D rhs whose batch dims only continue the rows
+    runs as one unbatched GEMM (the TMA kernel), residual epilogue included."""
+    import oracle
+
+    def g_(g):
+        x = rand_input(g, (4, 50, 36), 61)
+        w = rand_input(g, (36, 72), 62)
+        r = rand_input(g, (4, 50, 72), 63)
+        w2 = rand_input(g, (72, 36), 64)
+        y = g.add(g.matmul(x, w), r)           # residual fused into the epilogue (aux rows merge too)
+        return [y, g.matmul(g.transpose(y, [1, 0, 2]), w2)]  # rows do not continue: stays batched
+    mlir, args = build(g_)
+    want = oracle.run(mlir, args)
+    names, outs = _run_env(mlir, args, {})
+    assert sum("[tma]" in nm for nm in names) == 1, names
+    for o in outs:
+        for k in range(2):
+            compare(o[k], want[k], 2e-4, 1e-4, f"output{k}")

@@ -25,6 +25,7 @@ SOURCES = [
     "kernels/memory_ops.cu",
     "kernels/conv_gemm_tc.cu",
     "kernels/conv_gemm_tma.cu",
+    "kernels/attention_tc.cu",
     "kernels/noalloc_gemm.cu",
     "host/ir.cpp",
     "host/plan.cpp",

@@ -7,6 +7,7 @@
 #include <limits>
 #include <map>
 #include <numeric>
+#include <set>
 #include <sstream>
 #include <stdexcept>
 
@@ -127,8 +128,15 @@ class Planner {
       plan_->arg_buf.push_back(b);
       set_view(g.args[a], dense_view(b, v.type.dtype, v.type.shape));
     }
+    find_attention_clusters();
     for (size_t n = 0; n < g.nodes.size(); ++n) {
+      if (skip_node_.count((int)n)) continue;  // folded into a fused attention op
       try {
+        auto at = attn_at_.find((int)n);
+        if (at != attn_at_.end()) {
+          plan_attention(at->second);
+          continue;
+        }
         plan_node(g.nodes[n]);
       } catch (std::exception& e) {
         throw std::runtime_error("node " + std::to_string(n) + " (" + g.nodes[n].op + "): " + e.what());
@@ -155,6 +163,187 @@ class Planner {
  private:
   std::unique_ptr<Plan> plan_;
   std::vector<bool> has_view_;
+
+  // ---------------------------------------------------------------- attention clusters
+  // matmul(Q, KT) -> div(A, c) -> add(., mask) -> softmax(-1) -> matmul(P, V),
+  // every intermediate used once (GaweeToLinalg.cpp:959-1112, 1377-1441,
+  // 1885-1900).  K and V may come through the GQA head expansion
+  // unsqueeze(x, [2]) -> expand([B, Hkv, rep, S, D]) -> reshape([B, H, S, D]),
+  // which the fused op replaces by reading head h / rep.
+  struct AttnMatch {
+    int q = -1, kt = -1, k_base = -1, v = -1, v_base = -1, mask = -1;
+    double c = 1.0;
+    int out_transpose = -1;  // the node permuting the output to [B, S, H, D], if that is its only use
+    int pv_out = -1;         // the cluster's result value
+  };
+  std::map<int, AttnMatch> attn_at_;  // PV matmul node -> cluster
+  std::set<int> skip_node_;
+  std::vector<int> uses_;
+
+  int def_node(int v) const { return plan_->g.values[v].def_node; }
+  const Node* node_of(int v) const {
+    int d = def_node(v);
+    return d >= 0 ? &plan_->g.nodes[d] : nullptr;
+  }
+  static bool is_op(const Node* n, const char* op) { return n && n->op == op; }
+
+  // x = reshape(expand(unsqueeze(base, [2]), [B, Hkv, rep, S, D]), [B, Hkv * rep, S, D]) -> base
+  int gqa_base(int x, std::vector<int>& nodes) {
+    const Node* r = node_of(x);
+    if (!is_op(r, "gawee.reshape") || uses_[x] != 1) return -1;
+    const Node* e = node_of(r->ins[0]);
+    if (!is_op(e, "gawee.expand") || uses_[r->ins[0]] != 1) return -1;
+    const Node* u = node_of(e->ins[0]);
+    if (!is_op(u, "gawee.unsqueeze") || uses_[e->ins[0]] != 1) return -1;
+    if (!u->has_attr("axes") || u->attr("axes").ints != std::vector<int64_t>{2}) return -1;
+    const auto& es = val(r->ins[0]).type.shape;  // [B, Hkv, rep, S, D]
+    const auto& bs = val(u->ins[0]).type.shape;  // [B, Hkv, S, D]
+    const auto& xs = val(x).type.shape;          // [B, H, S, D]
+    if (es.size() != 5 || bs.size() != 4 || xs.size() != 4) return -1;
+    if (es[0] != bs[0] || es[1] != bs[1] || es[3] != bs[2] || es[4] != bs[3]) return -1;
+    if (xs[0] != bs[0] || xs[1] != es[1] * es[2] || xs[2] != bs[2] || xs[3] != bs[3]) return -1;
+    nodes.push_back(def_node(x));
+    return u->ins[0];
+  }
+
+  void find_attention_clusters() {
+    Graph& g = plan_->g;
+    uses_.assign(g.values.size(), 0);
+    for (const Node& n : g.nodes)
+      for (int v : n.ins) uses_[v]++;
+    for (int r : g.results) uses_[r] += 2;  // a result is never folded away
+    for (size_t e = 0; e < g.nodes.size(); ++e) {
+      const Node& E = g.nodes[e];
+      if (E.op != "gawee.matmul" || E.ins.size() != 2) continue;
+      const Node* P = node_of(E.ins[0]);
+      if (!is_op(P, "gawee.softmax") || uses_[E.ins[0]] != 1) continue;
+      const int rank = val(E.ins[0]).type.rank();
+      int64_t axis = P->has_attr("axis") ? P->attr("axis").i : -1;
+      if (axis < 0) axis += rank;
+      if (rank != 4 || axis != 3) continue;
+      const Node* C = node_of(P->ins[0]);
+      if (!is_op(C, "gawee.add") || uses_[P->ins[0]] != 1) continue;
+      int bi = -1, mask = -1;
+      for (int side = 0; side < 2; ++side) {
+        const Node* Bn = node_of(C->ins[side]);
+        if (is_op(Bn, "gawee.div") && uses_[C->ins[side]] == 1) {
+          bi = side;
+          mask = C->ins[1 - side];
+          break;
+        }
+      }
+      if (bi < 0) continue;
+      const Node* Bn = node_of(C->ins[bi]);
+      double c = 0;
+      int64_t ci = 0;
+      if (!scalar_const(Bn->ins[1], c, ci) || val(Bn->ins[1]).type.dtype != DType::F32 || !(c > 0)) continue;
+      const Node* A = node_of(Bn->ins[0]);
+      if (!is_op(A, "gawee.matmul") || uses_[Bn->ins[0]] != 1) continue;
+      const auto& qs = val(A->ins[0]).type.shape;   // [B, H, S, D]
+      const auto& kts = val(A->ins[1]).type.shape;  // [B, H, D, Skv]
+      const auto& vs = val(E.ins[1]).type.shape;    // [B, H, Skv, D]
+      const Value& ms = val(mask);
+      if (qs.size() != 4 || kts.size() != 4 || vs.size() != 4) continue;
+      if (kts[0] != qs[0] || kts[1] != qs[1] || kts[2] != qs[3] || vs[0] != qs[0] || vs[1] != qs[1] ||
+          vs[2] != kts[3] || vs[3] != qs[3])
+        continue;
+      if (val(A->ins[0]).type.dtype != DType::F32 || val(A->ins[1]).type.dtype != DType::F32 ||
+          val(E.ins[1]).type.dtype != DType::F32 || ms.type.dtype != DType::F32 || ms.type.rank() > 4)
+        continue;
+      const std::vector<int64_t> sshape = {qs[0], qs[1], qs[2], kts[3]};
+      bool bcast_ok = true;  // the mask broadcasts to the score shape
+      for (int d = 0; d < ms.type.rank(); ++d) {
+        const int64_t md = ms.type.shape[ms.type.rank() - 1 - d], sd = sshape[3 - d];
+        if (md != 1 && md != sd) bcast_ok = false;
+      }
+      if (!bcast_ok) continue;
+      if (!kern::attn_supported(qs[3], kts[3], qs[1], qs[1])) continue;
+      AttnMatch m;
+      m.q = A->ins[0];
+      m.kt = A->ins[1];
+      m.v = E.ins[1];
+      m.mask = mask;
+      m.c = c;
+      m.pv_out = E.outs[0];
+      std::vector<int> skip = {def_node(E.ins[0]), def_node(P->ins[0]), def_node(C->ins[bi]), def_node(Bn->ins[0])};
+      // K: the transpose of a GQA expansion, if any
+      const Node* Tk = node_of(m.kt);
+      if (is_op(Tk, "gawee.transpose") && uses_[m.kt] == 1 && Tk->attr("perm").ints == std::vector<int64_t>{0, 1, 3, 2}) {
+        std::vector<int> kn;
+        int kb = gqa_base(Tk->ins[0], kn);
+        if (kb >= 0) {
+          m.k_base = kb;
+          skip.push_back(def_node(m.kt));
+          skip.insert(skip.end(), kn.begin(), kn.end());
+        }
+      }
+      std::vector<int> vn;
+      m.v_base = gqa_base(m.v, vn);
+      if (m.v_base >= 0) skip.insert(skip.end(), vn.begin(), vn.end());
+      // K and V must agree on the head grouping
+      const int64_t hk = m.k_base >= 0 ? val(m.k_base).type.shape[1] : qs[1];
+      const int64_t hv = m.v_base >= 0 ? val(m.v_base).type.shape[1] : qs[1];
+      if (hk != hv || !kern::attn_supported(qs[3], kts[3], qs[1], hk)) continue;
+      // an output used only by transpose(perm [0, 2, 1, 3]) is written in [B, S, H, D] order
+      const int out = E.outs[0];
+      if (uses_[out] == 1) {
+        for (size_t n2 = e + 1; n2 < g.nodes.size(); ++n2) {
+          const Node& X = g.nodes[n2];
+          if (X.op == "gawee.transpose" && X.ins.size() == 1 && X.ins[0] == out &&
+              X.attr("perm").ints == std::vector<int64_t>{0, 2, 1, 3})
+            m.out_transpose = (int)n2;
+        }
+      }
+      for (int sn : skip) skip_node_.insert(sn);
+      attn_at_[(int)e] = m;
+    }
+  }
+
+  void plan_attention(const AttnMatch& m) {
+    View q = value_view(m.q);
+    View k, v;
+    if (m.k_base >= 0) {
+      k = value_view(m.k_base);
+    } else {  // K^T [B, H, D, Skv] -> K [B, H, Skv, D]
+      View kt = value_view(m.kt);
+      k = kt;
+      std::swap(k.shape[2], k.shape[3]);
+      std::swap(k.st[2], k.st[3]);
+    }
+    v = value_view(m.v_base >= 0 ? m.v_base : m.v);
+    const int64_t B = q.shape[0], H = q.shape[1], S = q.shape[2], D = q.shape[3], Skv = k.shape[2];
+    auto dense_inner = [](View& x) {  // d contiguous; strides of size-1 dims are never stepped
+      return x.st[3] == 1 || x.shape[3] == 1;
+    };
+    if (!dense_inner(q)) q = copy_to_new(q, "attn_q_copy");
+    if (!dense_inner(k)) k = copy_to_new(k, "attn_k_copy");
+    if (!dense_inner(v)) v = copy_to_new(v, "attn_v_copy");
+    Op op;
+    op.kind = OpKind::ATTN;
+    op.name = "attention";
+    auto& a = op.attn;
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.B = B; a.H = H; a.Hkv = k.shape[1]; a.S = S; a.Skv = Skv; a.D = D;
+    a.c = m.c;
+    a.has_mask = true;
+    a.mask = broadcast_to(value_view(m.mask), {B, H, S, Skv});
+    a.flops = 4.0 * (double)B * (double)H * (double)S * (double)Skv * (double)D;
+    View out;
+    if (m.out_transpose >= 0) {
+      out = alloc(DType::F32, {B, S, H, D});  // dense [B, S, H, D], seen as [B, H, S, D]
+      std::swap(out.shape[1], out.shape[2]);
+      std::swap(out.st[1], out.st[2]);
+    } else {
+      out = alloc(DType::F32, {B, H, S, D});
+    }
+    a.out = out;
+    op.reads = {q, k, v, a.mask};
+    op.writes = {out};
+    add_op(std::move(op));
+    set_view(m.pv_out, out);
+  }
 
   // ---------------------------------------------------------------- buffers / views
   int new_buf(DType dt, int64_t elems, BufKind kind = BufKind::ARENA) {

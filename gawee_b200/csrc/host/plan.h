@@ -58,7 +58,7 @@ struct Buf {
   size_t bytes() const { return (size_t)elems * dtype_size(dt); }
 };
 
-enum class OpKind { EW, REDUCE, GREDUCE, SOFTMAX, GATHER, GATHER_ELEMS, REMAP, RANGE, POOL, TOPK, PACK, TC };
+enum class OpKind { EW, REDUCE, GREDUCE, SOFTMAX, GATHER, GATHER_ELEMS, REMAP, RANGE, POOL, TOPK, PACK, TC, ATTN };
 
 struct Runtime;  // execution state (device pointers), runtime.cpp
 
@@ -95,6 +95,17 @@ struct Op {
     std::vector<int64_t> batch_shape, a_bst, b_bst;
     double flops = 0;        // algorithmic 2*M*N*K over every batch (unpadded K)
   } tc;
+
+  // ATTN: the attention cluster matmul(Q, K^T) -> div(c) -> add(mask) ->
+  // softmax(-1) -> matmul(., V) as one fused op.  k and v are the key/value
+  // tensors before any GQA head expansion ([B, Hkv, Skv, D], d contiguous).
+  struct Attn {
+    View q, k, v, mask, out;   // q, out: [B, H, S, D]; mask broadcast to [B, H, S, Skv]
+    bool has_mask = false;
+    int64_t B = 0, H = 0, Hkv = 0, S = 0, Skv = 0, D = 0;
+    double c = 1.0;            // the divisor
+    double flops = 0;          // 4 * B * H * S * Skv * D (both products over the full score matrix)
+  } attn;
 
   // Non-structured ops: launcher resolving device pointers at launch time.
   std::function<void(Runtime&, void* stream)> launch;

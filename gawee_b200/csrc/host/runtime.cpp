@@ -108,6 +108,8 @@ struct Runtime {
   std::vector<std::array<TMap, 3>> tmaps;  // per op (TC only): B hi, B lo, A (TMA-fed kernel)
   std::vector<int> a_tma;                  // per op (TC only): kern::ATma, A_TMA_NONE = warp gather
   std::vector<int> ksplit;                 // per op (TC only): k splits, 1 = none
+  std::vector<uint8_t*> attn_skip;         // per op (ATTN only): skip flags of the mask tiles
+  std::vector<std::array<std::array<int8_t, 3>, 3>> attn_cpos;  // per op (ATTN): tensor-map dim order
   float* splitk_ws = nullptr;              // partial sums of split contractions (ops run in order: shared)
   ncclComm_t comm = nullptr;
   int world = 1, rank = 0;
@@ -131,6 +133,8 @@ struct Runtime {
     if (arena) cudaFree(arena);
     if (d_status) cudaFree(d_status);
     if (splitk_ws) cudaFree(splitk_ws);
+    for (uint8_t* f : attn_skip)
+      if (f) cudaFree(f);
     if (own_stream) cudaStreamDestroy(own_stream);
   }
 
@@ -224,9 +228,28 @@ void Runtime::build_tensor_maps() {
   int cap = 32;
   if (const char* e = std::getenv("GAWEE_MAX_KSPLIT")) cap = std::max(1, std::atoi(e));
   size_t ws_floats = 0;
+  attn_skip.assign(P.ops.size(), nullptr);
+  attn_cpos.assign(P.ops.size(), {});
   for (size_t o = 0; o < P.ops.size(); ++o) {
     const Op& op = P.ops[o];
-    if (op.dead || op.kind != OpKind::TC) continue;
+    if (op.dead) continue;
+    if (op.kind == OpKind::ATTN) {
+      const auto& a = op.attn;
+      auto map = [&](const View& v, int64_t heads, int64_t seq, int which) {
+        return kern::make_attn_tensor_map(reinterpret_cast<const float*>(ptr(v)), a.B, heads, seq, a.D, v.st[0],
+                                          v.st[1], v.st[2], tmaps[o][which].b, attn_cpos[o][which].data());
+      };
+      if (!map(a.q, a.H, a.S, 0) || !map(a.k, a.Hkv, a.Skv, 1) || !map(a.v, a.Hkv, a.Skv, 2))
+        throw StatusError(GAWEE_ERR_UNSUPPORTED, "attention operands cannot be addressed by TMA for op " + op.name);
+      if (a.has_mask) {
+        const int64_t mb = a.mask.st[0] ? a.B : 1, mh = a.mask.st[1] ? a.H : 1;
+        const int64_t n = mb * mh * ((a.S + 127) / 128) * ((a.Skv + 127) / 128);
+        if (cudaMalloc(&attn_skip[o], (size_t)n) != cudaSuccess)
+          throw StatusError(GAWEE_ERR_OOM, "cudaMalloc of attention skip flags failed");
+      }
+      continue;
+    }
+    if (op.kind != OpKind::TC) continue;
     const auto& t = op.tc;
     const float* hi = static_cast<const float*>(P.bufs[t.hi].ptr);
     const float* lo = static_cast<const float*>(P.bufs[t.lo].ptr);
@@ -503,10 +526,42 @@ static void launch_tc(Runtime& rt, int o, const Op& op, cudaStream_t s) {
   if (!launched) throw StatusError(GAWEE_ERR_UNSUPPORTED, "tensor-core launch rejected the shape of op " + op.name);
 }
 
+static void launch_attn(Runtime& rt, int o, const Op& op, cudaStream_t s) {
+  const auto& a = op.attn;
+  kern::AttnParams p{};
+  p.B = (int)a.B; p.H = (int)a.H; p.Hkv = (int)a.Hkv; p.S = (int)a.S; p.Skv = (int)a.Skv; p.D = (int)a.D;
+  p.QT = (int)((a.S + 127) / 128);
+  p.KT = (int)((a.Skv + 127) / 128);
+  // (acc / c): a power-of-two c divides exactly as a multiply by 1 / c
+  int e = 0;
+  const double mant = std::frexp(a.c, &e);
+  if (mant == 0.5 && e >= -100 && e <= 100) {
+    p.scale = (float)std::ldexp(1.0, 1 - e);
+    p.scale_mul = 1;
+  } else {
+    p.scale = (float)a.c;
+    p.scale_mul = 0;
+  }
+  if (a.has_mask) {
+    p.mask = reinterpret_cast<const float*>(rt.ptr(a.mask));
+    for (int d = 0; d < 4; ++d) p.m_st[d] = a.mask.st[d];
+    p.mb = a.mask.st[0] ? p.B : 1;
+    p.mh = a.mask.st[1] ? p.H : 1;
+  }
+  p.out = reinterpret_cast<float*>(rt.ptr(a.out));
+  for (int d = 0; d < 4; ++d) p.o_st[d] = a.out.st[d];
+  for (int w = 0; w < 3; ++w)
+    for (int i = 0; i < 3; ++i) p.cpos[w][i] = rt.attn_cpos[o][w][i];
+  p.status = rt.status();
+  if (!kern::launch_attention(p, rt.tmaps[o][0].b, rt.tmaps[o][1].b, rt.tmaps[o][2].b, rt.attn_skip[o], s))
+    throw StatusError(GAWEE_ERR_UNSUPPORTED, "attention launch rejected the shape of op " + op.name);
+}
+
 void Runtime::run_op(int o, cudaStream_t s) {
   const Op& op = plan->ops[o];
   if (op.kind == OpKind::EW) launch_ew(*this, op, s);
   else if (op.kind == OpKind::TC) launch_tc(*this, o, op, s);
+  else if (op.kind == OpKind::ATTN) launch_attn(*this, o, op, s);
   else op.launch(*this, s);
 }
 
@@ -1002,7 +1057,11 @@ int gawee_num_kernels(const gawee_ctx* ctx) { return ctx ? (int)ctx->rt.plan->ma
 int gawee_num_launches(const gawee_ctx* ctx) {
   if (!ctx) return -1;
   int n = 0;
-  for (int o : ctx->rt.plan->main) n += 1 + (o < (int)ctx->rt.ksplit.size() && ctx->rt.ksplit[o] > 1 ? 1 : 0);
+  for (int o : ctx->rt.plan->main) {
+    const auto& op = ctx->rt.plan->ops[o];
+    n += 1 + (o < (int)ctx->rt.ksplit.size() && ctx->rt.ksplit[o] > 1 ? 1 : 0);
+    if (op.kind == gawee::OpKind::ATTN && op.attn.has_mask) ++n;  // the skip-flag pass
+  }
   return n;
 }
 
@@ -1027,8 +1086,8 @@ gawee_status gawee_op_info(const gawee_ctx* ctx, int i, char* name, size_t n, in
     std::strncpy(name, nm.c_str(), n - 1);
     name[n - 1] = 0;
   }
-  if (is_tc) *is_tc = op.kind == gawee::OpKind::TC;
-  if (flops) *flops = op.kind == gawee::OpKind::TC ? op.tc.flops : 0.0;
+  if (is_tc) *is_tc = op.kind == gawee::OpKind::TC || op.kind == gawee::OpKind::ATTN;
+  if (flops) *flops = op.kind == gawee::OpKind::TC ? op.tc.flops : op.kind == gawee::OpKind::ATTN ? op.attn.flops : 0.0;
   return GAWEE_OK;
 }
 

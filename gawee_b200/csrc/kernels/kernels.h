@@ -298,6 +298,37 @@ enum FastEpi : int {
   FAST_MULC_ADD = 4,     // (acc * c) + aux0: acc / d with d a power of two, c = 1 / d (exact)
 };
 
+// ---------------------------------------------------------------------------
+// Fused attention (attention_tc.cu): out = softmax((q . k^T) / c + mask) . v
+// per (batch, head), q [B, H, S, D], k / v [B, Hkv, Skv, D] (query head h
+// reads key/value head h / (H / Hkv)), d contiguous, D <= 64 and a multiple
+// of 16.  The three operands are addressed by 4-D tensor maps
+// (make_attn_tensor_map); the mask by strides (0 = broadcast).
+// ---------------------------------------------------------------------------
+struct AttnParams {
+  int B, H, Hkv, S, Skv, D;
+  int QT, KT;                 // 128-row query tiles, 128-key tiles
+  float scale;
+  int scale_mul;              // scores = acc * scale (scale = 1 / c, c a power of two) or acc / scale (scale = c)
+  const float* mask;          // nullptr: no mask
+  int64_t m_st[4];            // mask strides over (b, h, i, j)
+  int mb, mh;                 // skip-flag extents over b and h (1 where the mask is broadcast)
+  const uint8_t* skip;        // set by launch_attention
+  float* out;
+  int64_t o_st[4];            // output strides over (b, h, i, d)
+  int* status;
+  int8_t cpos[3][3];          // per operand (q, k, v): map dim of (seq, head, batch), from make_attn_tensor_map
+};
+
+bool attn_supported(int64_t D, int64_t Skv, int64_t H, int64_t Hkv);
+// 4-D tensor map (d, seq, head, batch) over a [batch, heads, seq, dim] view with d contiguous.
+// The outer dims are ordered by stride; cpos[0..2] receives the map dim of (seq, head, batch).
+bool make_attn_tensor_map(const float* base, int64_t batch, int64_t heads, int64_t seq, int64_t dim, int64_t st_b,
+                          int64_t st_h, int64_t st_s, void* tmap_out, int8_t* cpos);
+// skip_flags: mb * mh * QT * KT bytes of device scratch (used when p.mask is set).
+bool launch_attention(const AttnParams& p, const void* tq, const void* tk, const void* tv, uint8_t* skip_flags,
+                      cudaStream_t s);
+
 // Returns false (and launches nothing) when the shape is not supported.
 bool launch_conv_gemm_tc(const ConvGemmParams& p, const void* tmap_hi, const void* tmap_lo, int block_n,
                          cudaStream_t s);

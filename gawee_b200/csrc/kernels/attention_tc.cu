@@ -20,13 +20,15 @@
 // forward by attn_skip_kernel).
 //
 // One CTA per (batch, head, 128-query tile), heaviest query tiles first.
-// Warp roles (320 threads):
-//   warps 0-3  softmax rows (lane = query row = tensor-memory lane), the
-//              fp32 output accumulator in registers, the final O / l store
-//   warp 4     TMA (Q once, then K tiles into two buffers and V tiles into
+// Warp roles (448 threads):
+//   warps 0-7  softmax rows, two warps per row quarter (lane = query row =
+//              tensor-memory lane), each over half the keys of a tile and
+//              half the output columns; the fp32 output accumulator in
+//              registers, the final O / l store
+//   warp 8     TMA (Q once, then K tiles into two buffers and V tiles into
 //              one); owns the tensor-memory allocation
-//   warp 5     lane 0 issues the MMAs and the commits that track them
-//   warps 6-9  split: Q lo into tensor memory once, then per key tile K lo,
+//   warp 9     lane 0 issues the MMAs and the commits that track them
+//   warps 10-13 split: Q lo into tensor memory once, then per key tile K lo,
 //              and V^T raw and V^T lo (transposed to K-major) in shared memory
 // Every mbarrier wait is bounded (tc_common.cuh: mbar_wait); on expiry the
 // CTA records ST_BARRIER_TIMEOUT and finishes without its result.
@@ -46,7 +48,7 @@ namespace kern {
 
 namespace {
 
-constexpr int kAttnThreads = 320;
+constexpr int kAttnThreads = 448;
 constexpr int kRowsQ = 128;       // query rows per CTA
 constexpr int kKeys = 128;        // keys per tile
 constexpr int kTile = 16384;      // 128 rows x 32 fp32: one 128-byte-swizzled half of a 64-wide head dim
@@ -66,7 +68,9 @@ enum Bar : int {
   BAR_Q, BAR_QLO, BAR_KF0, BAR_KF1, BAR_KE0, BAR_KE1, BAR_VF, BAR_VE, BAR_KLO_R, BAR_KLO_F, BAR_VT_R, BAR_VT_F,
   BAR_SF0, BAR_SF1, BAR_SE0, BAR_SE1, BAR_P_R, BAR_PLO_F, BAR_PV_F, BAR_PV_E, BAR_DONE, NUM_BARS
 };
-constexpr int kAttnSmem = kOffBar + NUM_BARS * 8 + 16 + kMaxKeyTiles * 4 + 1024;
+constexpr int kOffXch = kOffBar + 512;  // partial row maxima / sums of the two halves: [2][128] floats
+constexpr int kAttnSmem = kOffXch + 2 * kRowsQ * 4 + 1024;
+static_assert(NUM_BARS * 8 + 16 + kMaxKeyTiles * 4 <= 512, "barriers, flags and tile list");
 // tensor memory columns: S buffers (P raw overwrites them), P lo, Q lo, P.V
 constexpr uint32_t kColS0 = 0, kColS1 = 128, kColPlo = 256, kColQlo = 384, kColPV = 448;
 
@@ -183,7 +187,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < NUM_BARS; ++i) {
       uint32_t count = 1;
-      if (i == BAR_QLO || i == BAR_KLO_R || i == BAR_VT_R || i == BAR_VE || i == BAR_P_R || i == BAR_PV_E) count = 4;
+      if (i == BAR_QLO || i == BAR_KLO_R || i == BAR_VT_R || i == BAR_VE) count = 4;
+      if (i == BAR_P_R || i == BAR_PV_E) count = 8;
       mbar_init(bar(i), count);
     }
     *abort_flag = 0;
@@ -195,7 +200,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     *ntiles = n;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 4) {
+  if (warp == 8) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(512u)
                  : "memory");
@@ -207,51 +212,64 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const int T = *ntiles;
 
-  if (warp < 4) {
+  if (warp < 8) {
     // ------------------------------------------------------------------ softmax rows
-    const int r = warp * 32 + lane;
+    // Two warps per lane quarter: warp w owns rows 32 (w % 4) .. + 31 (its
+    // tensor-memory lanes) over key columns 64 hf .. + 63 and output
+    // columns 32 hf .. (hf = w / 4).  The halves of a row exchange their
+    // partial maxima per tile through shared memory (named barrier of the
+    // two warps) and their partial sums once at the end.
+    const int q = warp & 3, hf = warp >> 2;
+    const int r = q * 32 + lane;
     const int qi = q0 + r;
-    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+    float* xch = reinterpret_cast<float*>(smem + kOffXch);  // [2][128]
+    auto pair_sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(1 + q), "r"(64) : "memory"); };
     const float* mrow = p.mask ? p.mask + (int64_t)b * p.m_st[0] + (int64_t)h * p.m_st[1] +
                                      (int64_t)min(qi, p.S - 1) * p.m_st[2]
                                : nullptr;
-    float o[DV];
+    constexpr int kO0 = DV < 32 ? DV : 32;        // output columns of half 0
+    constexpr int kO1 = DV > 32 ? DV - 32 : 0;    // of half 1
+    const int ocol0 = 32 * hf, ocols = hf ? kO1 : kO0;
+    float o[32];
 #pragma unroll
-    for (int d = 0; d < DV; ++d) o[d] = 0.f;
+    for (int d = 0; d < 32; ++d) o[d] = 0.f;
     float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
     bool ok = true;
     const bool mvec = mrow && p.m_st[3] == 1 && (reinterpret_cast<uintptr_t>(mrow) & 15) == 0;
-    auto correct = [&](int u, float alpha) -> bool {  // O = O * alpha_u + (P_u . V_u)
+    auto correct = [&](int u, float alpha) -> bool {  // O = O * alpha_u + (P_u . V_u), this half's columns
       if (!__all_sync(0xffffffffu, mbar_wait(bar(BAR_PV_F), u & 1, abort_flag, p.status))) return false;
       tc_fence_after();
 #pragma unroll
-      for (int c0 = 0; c0 < DV; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(trow + kColPV + c0, v);
+      for (int c0 = 0; c0 < 32; c0 += 16) {
+        if (c0 < ocols) {
+          uint32_t v[16];
+          tmem_ld16(trow + kColPV + ocol0 + c0, v);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) o[c0 + e] = __fadd_rn(__fmul_rn(o[c0 + e], alpha), __uint_as_float(v[e]));
+          for (int e = 0; e < 16; ++e) o[c0 + e] = __fadd_rn(__fmul_rn(o[c0 + e], alpha), __uint_as_float(v[e]));
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(BAR_PV_E));
       return true;
     };
-    for (int t = 0; t < T && ok; ++t) {
+    // The two warps of a row pair meet at a named barrier twice per tile and
+    // once at the end, always: after a failed (bounded) wait a warp skips its
+    // work but never a barrier, so neither can be left waiting at one.
+    for (int t = 0; t < T; ++t) {
       const int sb = t & 1;
-      const uint32_t scol = sb ? kColS1 : kColS0;
-      const int j0 = (tiles[t] & 0xffff) * kKeys;
+      const uint32_t scol = (sb ? kColS1 : kColS0) + 64 * hf;
+      const int j0 = (tiles[t] & 0xffff) * kKeys + 64 * hf;
       const bool use_mask = mrow && !(tiles[t] & 0x10000);
-      if (!__all_sync(0xffffffffu, mbar_wait(bar(sb ? BAR_SF1 : BAR_SF0), (t >> 1) & 1, abort_flag, p.status))) {
-        ok = false;
-        break;
-      }
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(sb ? BAR_SF1 : BAR_SF0), (t >> 1) & 1, abort_flag, p.status));
       tc_fence_after();
       // pass 1: scores (acc / c + mask, the reference's operations and
       // order; -inf past the sequence) written back over the accumulators,
-      // and the tile's row maximum
+      // and this half's row maximum
       float tmax = -INFINITY;
-#pragma unroll 2
-      for (int c0 = 0; c0 < kKeys; c0 += 16) {
+#pragma unroll
+      for (int c0 = 0; c0 < 64 && ok; c0 += 16) {
         uint32_t x[16];
         float mk[16];
         if (use_mask) {
@@ -281,62 +299,67 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         tmem_st16(trow + scol + c0, x);
       }
+      // the row's maximum over both halves
+      xch[hf * kRowsQ + r] = tmax;
+      pair_sync();
+      tmax = maxnan(tmax, xch[(hf ^ 1) * kRowsQ + r]);
+      pair_sync();  // both read before the next tile's writes
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       const float m_new = maxnan(m, tmax);
       const float alpha = m_new == -INFINITY ? 1.f : expf(__fsub_rn(m, m_new));
       // P lo of the previous tile must have been consumed by its P.V
-      if (!__all_sync(0xffffffffu, mbar_wait(bar(BAR_PLO_F), (t & 1) ^ 1, abort_flag, p.status))) {
-        ok = false;
-        break;
-      }
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(BAR_PLO_F), (t & 1) ^ 1, abort_flag, p.status));
+      if (!ok) continue;
       tc_fence_after();
       // pass 2: p = exp(s - m_new); P raw over the scores, P lo beside
       float lsum = 0.f;
-#pragma unroll 2
-      for (int c0 = 0; c0 < kKeys; c0 += 16) {
+#pragma unroll
+      for (int c0 = 0; c0 < 64; c0 += 16) {
         uint32_t x[16], y[16];
         tmem_ld16(trow + scol + c0, x);
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float s = __uint_as_float(x[e]);
-          const float pe = (s == -INFINITY) ? 0.f : expf(__fsub_rn(s, m_new));
+          const float sv = __uint_as_float(x[e]);
+          const float pe = (sv == -INFINITY) ? 0.f : expf(__fsub_rn(sv, m_new));
           lsum = __fadd_rn(lsum, pe);
           x[e] = __float_as_uint(pe);
           y[e] = __float_as_uint(__fsub_rn(pe, tf32_hi(pe)));
         }
         tmem_st16(trow + scol + c0, x);
-        tmem_st16(trow + kColPlo + c0, y);
+        tmem_st16(trow + kColPlo + 64 * hf + c0, y);
       }
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(BAR_P_R));
-      l = __fadd_rn(__fmul_rn(l, alpha), lsum);
+      l = __fadd_rn(__fmul_rn(l, alpha), lsum);  // this half's partial sum
       m = m_new;
-      if (t > 0 && !correct(t - 1, alpha_prev)) {
-        ok = false;
-        break;
-      }
+      if (t > 0) ok = correct(t - 1, alpha_prev);
       alpha_prev = alpha;
     }
     if (ok && T > 0) ok = correct(T - 1, alpha_prev);
     ok = __all_sync(0xffffffffu, ok && !*abort_flag);
+    // the row's sum: both halves add the partials in the same order
+    xch[hf * kRowsQ + r] = l;
+    pair_sync();
+    l = __fadd_rn(xch[r], xch[kRowsQ + r]);
     if (ok && qi < p.S) {
-      float* orow = p.out + (int64_t)b * p.o_st[0] + (int64_t)h * p.o_st[1] + (int64_t)qi * p.o_st[2];
+      float* orow = p.out + (int64_t)b * p.o_st[0] + (int64_t)h * p.o_st[1] + (int64_t)qi * p.o_st[2] +
+                    (int64_t)ocol0 * p.o_st[3];
       // compile-time indices keep o[] in registers
       if (p.o_st[3] == 1 && (reinterpret_cast<uintptr_t>(orow) & 15) == 0 && p.D % 4 == 0) {
 #pragma unroll
-        for (int d = 0; d < DV; d += 4)
-          if (d < p.D)
+        for (int d = 0; d < 32; d += 4)
+          if (d < ocols && ocol0 + d < p.D)
             *reinterpret_cast<float4*>(orow + d) = make_float4(__fdiv_rn(o[d], l), __fdiv_rn(o[d + 1], l),
                                                                __fdiv_rn(o[d + 2], l), __fdiv_rn(o[d + 3], l));
       } else {
 #pragma unroll
-        for (int d = 0; d < DV; ++d)
-          if (d < p.D) orow[(int64_t)d * p.o_st[3]] = __fdiv_rn(o[d], l);
+        for (int d = 0; d < 32; ++d)
+          if (d < ocols && ocol0 + d < p.D) orow[(int64_t)d * p.o_st[3]] = __fdiv_rn(o[d], l);
       }
     }
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     // ------------------------------------------------------------------ TMA
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tq)) : "memory");
@@ -366,7 +389,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t id_s = idesc_tf32(kKeys);  // S: N = 128 keys
@@ -431,7 +454,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // ------------------------------------------------------------------ split
     const int q4 = warp & 3;                 // tensor-memory lane quarter of this warp
     const int row = q4 * 32 + lane;          // Q row for Q lo
-    const int tid = (warp - 6) * 32 + lane;  // 0..127 for the K / V tiles
+    const int tid = (warp - 10) * 32 + lane;  // 0..127 for the K / V tiles
     bool alive = mbar_wait(bar(BAR_Q), 0, abort_flag, p.status);
     if (alive) {
       const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
@@ -519,7 +542,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == 8) {
     volatile int never = 0;
     if (lane == 0) mbar_wait(bar(BAR_DONE), 0, &never, p.status);
     __syncwarp();

@@ -320,7 +320,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const float sv = __uint_as_float(x[e]);
-          const float pe = (sv == -INFINITY) ? 0.f : expf(__fsub_rn(sv, m_new));
+          // __expf: relative error within a few ulp where p is not negligible
+          // (s - m in [-20, 0]); the row's largest term is exactly 1
+          const float pe = (sv == -INFINITY) ? 0.f : __expf(__fsub_rn(sv, m_new));
           lsum = __fadd_rn(lsum, pe);
           x[e] = __float_as_uint(pe);
           y[e] = __float_as_uint(__fsub_rn(pe, tf32_hi(pe)));

@@ -35,6 +35,11 @@ Fn gather_elements(const View& data, const View& idx, const View& out, int axis)
 Fn range(kern::RangeParams rp, const View& out);
 Fn topk(const View& in, const View& vals, const View& idxs, const View& used, int64_t k);
 Fn pack(const PackSpec& ps, int64_t ldk, int hi, int lo);
+// x, cs, sn: views over out's shape (broadcast strides 0); out dense
+Fn rope(const View& x, const View& cs, const View& sn, const View& out);
+// x: [rows][cols] with row stride x_rs (cols contiguous); w, b: per-column views (b.buf < 0: none)
+Fn rownorm(const View& x, int64_t rows, int64_t cols, int64_t x_rs, const View& w, int64_t w_st, const View& b,
+           int64_t b_st, const View& out, float eps, bool centered);
 }  // namespace launch
 
 }  // namespace gawee

@@ -129,12 +129,24 @@ class Planner {
       set_view(g.args[a], dense_view(b, v.type.dtype, v.type.shape));
     }
     find_attention_clusters();
+    find_norm_clusters();
+    find_rope_clusters();
     for (size_t n = 0; n < g.nodes.size(); ++n) {
-      if (skip_node_.count((int)n)) continue;  // folded into a fused attention op
+      if (skip_node_.count((int)n)) continue;  // folded into a fused op
       try {
         auto at = attn_at_.find((int)n);
         if (at != attn_at_.end()) {
           plan_attention(at->second);
+          continue;
+        }
+        auto nt = norm_at_.find((int)n);
+        if (nt != norm_at_.end()) {
+          plan_rownorm(nt->second);
+          continue;
+        }
+        auto rt = rope_at_.find((int)n);
+        if (rt != rope_at_.end()) {
+          plan_rope(rt->second);
           continue;
         }
         plan_node(g.nodes[n]);
@@ -297,6 +309,267 @@ class Planner {
       for (int sn : skip) skip_node_.insert(sn);
       attn_at_[(int)e] = m;
     }
+  }
+
+  // ---------------------------------------------------------------- normalisation chains
+  // RMSNorm:   pow(x, 2) -> reduce_mean(-1, keepdims) -> add(eps) -> sqrt -> div(x, .) -> mul(., w) [-> add(., b)]
+  // LayerNorm: the same over xc = sub(x0, reduce_mean(x0, -1)), as the emitter decomposes them
+  // (ReduceMeanOpLowering GaweeToLinalg.cpp:1443-1514, Pow ONNXMLIREmitter.cpp:846-871,
+  // Sqrt / Div 1902-1927 / 1421-1441, Mul / Add 532-557, 1377-1419).
+  struct NormMatch {
+    int x = -1, x0 = -1, w = -1, b = -1, out = -1;
+    double eps = 0;
+    bool centered = false;
+  };
+  std::map<int, NormMatch> norm_at_;  // final node of the chain -> match
+
+  bool is_square_of(const Node* P, int x) {
+    if (!P) return false;
+    if (P->op == "gawee.mul") return P->ins.size() == 2 && P->ins[0] == x && P->ins[1] == x;
+    if (P->op != "linalg.generic" || P->ins.empty() || P->ins[0] != x || P->outs.size() != 1) return false;
+    if (!P->maps.empty() && !P->maps[0].is_identity()) return false;
+    const EProgram& b = P->body;
+    if (P->n_linalg_ins == 2) {  // powf(in, c) with c a scalar constant 2
+      double f;
+      int64_t i;
+      if (!scalar_const(P->ins[1], f, i) || f != 2.0) return false;
+      return b.code.size() == 1 && b.code[0].op == EOp::POWF && b.code[0].a == 0 && b.code[0].b == 1 &&
+             b.result == b.code[0].dst;
+    }
+    if (P->n_linalg_ins != 1) return false;
+    if (b.code.size() == 1 && b.code[0].op == EOp::MULF && b.code[0].a == 0 && b.code[0].b == 0)
+      return b.result == b.code[0].dst;
+    return b.code.size() == 2 && b.code[0].op == EOp::CONST && b.code[0].fimm == 2.0 && b.code[1].op == EOp::POWF &&
+           b.code[1].a == 0 && b.code[1].b == b.code[0].dst && b.result == b.code[1].dst;
+  }
+
+  bool is_last_dim_mean(const Node* M) {
+    if (!is_op(M, "gawee.reduce_mean") || M->ins.size() != 1) return false;
+    const int rank = val(M->ins[0]).type.rank();
+    const auto& ax = M->attr("axes").ints;
+    const bool keep = !M->has_attr("keepDims") || M->attr("keepDims").b || M->attr("keepDims").i != 0;
+    return keep && ax.size() == 1 && (ax[0] == -1 || ax[0] == rank - 1);
+  }
+
+  // w (or b) broadcasts over every dim of `shape` but the last
+  bool per_column(int v, const std::vector<int64_t>& shape) {
+    const auto& ws = val(v).type.shape;
+    if (val(v).type.dtype != DType::F32 || ws.size() > shape.size()) return false;
+    for (size_t d = 0; d + 1 < ws.size(); ++d)
+      if (ws[d] != 1) return false;
+    return ws.empty() || ws.back() == 1 || ws.back() == shape.back();
+  }
+
+  void find_norm_clusters() {
+    Graph& g = plan_->g;
+    for (size_t f = 0; f < g.nodes.size(); ++f) {
+      const Node& F = g.nodes[f];
+      if (F.op != "gawee.mul" || F.ins.size() != 2 || skip_node_.count((int)f)) continue;
+      for (int side = 0; side < 2; ++side) {
+        const int dv = F.ins[side], w = F.ins[1 - side];
+        const Node* D = node_of(dv);
+        if (!is_op(D, "gawee.div") || uses_[dv] != 1) continue;
+        const int x = D->ins[0];
+        const Node* Q = node_of(D->ins[1]);
+        if (!is_op(Q, "gawee.sqrt") || uses_[D->ins[1]] != 1) continue;
+        const Node* A = node_of(Q->ins[0]);
+        if (!is_op(A, "gawee.add") || uses_[Q->ins[0]] != 1) continue;
+        int mi = -1;
+        double eps = 0;
+        int64_t ei = 0;
+        for (int k = 0; k < 2; ++k)
+          if (is_last_dim_mean(node_of(A->ins[k])) && scalar_const(A->ins[1 - k], eps, ei)) mi = k;
+        if (mi < 0 || uses_[A->ins[mi]] != 1) continue;
+        const Node* M = node_of(A->ins[mi]);
+        const Node* P = node_of(M->ins[0]);
+        if (!is_square_of(P, x) || uses_[M->ins[0]] != 1) continue;
+        const auto& xs = val(x).type.shape;
+        if (val(x).type.dtype != DType::F32 || xs.empty() || val(F.outs[0]).type.shape != xs ||
+            !per_column(w, xs))
+          continue;
+        NormMatch m;
+        m.x = x;
+        m.w = w;
+        m.eps = eps;
+        std::vector<int> skip = {def_node(dv), def_node(D->ins[1]), def_node(Q->ins[0]), def_node(A->ins[mi]),
+                                 def_node(M->ins[0])};
+        // LayerNorm: x = sub(x0, mean(x0)), used only by the square and the divide
+        const Node* X = node_of(x);
+        if (is_op(X, "gawee.sub") && uses_[x] == 2 && X->ins.size() == 2) {
+          const Node* MU = node_of(X->ins[1]);
+          if (is_last_dim_mean(MU) && MU->ins[0] == X->ins[0] && uses_[X->ins[1]] == 1 &&
+              val(X->ins[0]).type.shape == xs) {
+            m.centered = true;
+            m.x0 = X->ins[0];
+            skip.push_back(def_node(x));
+            skip.push_back(def_node(X->ins[1]));
+          }
+        }
+        // a trailing per-column add (LayerNorm's beta)
+        int last = (int)f;
+        m.out = F.outs[0];
+        if (uses_[F.outs[0]] == 1) {
+          for (size_t n2 = f + 1; n2 < g.nodes.size(); ++n2) {
+            const Node& B = g.nodes[n2];
+            if (B.op != "gawee.add" || B.ins.size() != 2) continue;
+            const int k = B.ins[0] == F.outs[0] ? 0 : B.ins[1] == F.outs[0] ? 1 : -1;
+            if (k < 0) continue;
+            if (per_column(B.ins[1 - k], xs) && val(B.outs[0]).type.shape == xs) {
+              m.b = B.ins[1 - k];
+              m.out = B.outs[0];
+              skip.push_back(last);
+              last = (int)n2;
+            }
+            break;
+          }
+        }
+        for (int sn : skip) skip_node_.insert(sn);
+        norm_at_[last] = m;
+        break;
+      }
+    }
+  }
+
+  void plan_rownorm(const NormMatch& m) {
+    View x = value_view(m.centered ? m.x0 : m.x);
+    const int r = x.rank();
+    const int64_t cols = x.shape[r - 1], rows = x.numel() / std::max<int64_t>(cols, 1);
+    // rows with one stride and contiguous columns, else a dense copy
+    bool ok = x.st[r - 1] == 1 || cols == 1;
+    int64_t x_rs = cols;
+    if (ok && !x.dense_rowmajor()) {
+      int64_t expect = -1;
+      for (int d = r - 2; d >= 0 && ok; --d) {
+        if (x.shape[d] == 1) continue;
+        if (expect < 0) {
+          x_rs = x.st[d];
+          expect = x.st[d] * x.shape[d];
+        } else if (x.st[d] != expect) {
+          ok = false;
+        } else {
+          expect *= x.shape[d];
+        }
+      }
+    }
+    if (!ok) {
+      x = copy_to_new(x, "rownorm_in");
+      x_rs = cols;
+    }
+    View w = broadcast_to(value_view(m.w), x.shape);
+    View b;
+    if (m.b >= 0) b = broadcast_to(value_view(m.b), x.shape);
+    View out = alloc(DType::F32, x.shape);
+    Op op;
+    op.kind = OpKind::REDUCE;
+    op.name = m.centered ? "layer_norm" : "rms_norm";
+    op.reads = {x, w};
+    if (m.b >= 0) op.reads.push_back(b);
+    op.writes = {out};
+    op.launch = launch::rownorm(x, rows, cols, x_rs, w, w.st[r - 1], b, m.b >= 0 ? b.st[r - 1] : 0, out,
+                                (float)m.eps, m.centered);
+    add_op(std::move(op));
+    set_view(m.out, out);
+  }
+
+  // ---------------------------------------------------------------- rotary embedding
+  // add(mul(x, cos), mul(cat([neg(slice(x, d/2..d)), slice(x, 0..d/2)], -1), sin)), the rotate-half
+  // form the emitter produces from Slice / Neg / Concat / Mul / Add (ONNXMLIREmitter.cpp:873-903,
+  // 2074-2124; SliceOpLowering GaweeToLinalg.cpp:2594-2715, CatOpLowering 1260-1325).
+  struct RopeMatch {
+    int x = -1, cs = -1, sn = -1, out = -1;
+  };
+  std::map<int, RopeMatch> rope_at_;
+
+  // the slice [start, start + len) of `data` along its last axis, step 1
+  bool last_axis_slice(const Node* n, int data, int64_t start, int64_t len) {
+    if (!is_op(n, "gawee.slice") || n->ins.size() < 5 || n->ins[0] != data) return false;
+    const Value& v = val(data);
+    const int r = v.type.rank();
+    const Value& o = val(n->outs[0]);
+    if (!val(n->ins[1]).is_const || !val(n->ins[3]).is_const || !val(n->ins[4]).is_const) return false;
+    auto starts = const_ints(n->ins[1]), axes = const_ints(n->ins[3]), steps = const_ints(n->ins[4]);
+    if (axes.size() != 1 || starts.size() != 1 || steps.size() != 1 || steps[0] != 1) return false;
+    if (!(axes[0] == -1 || axes[0] == r - 1)) return false;
+    int64_t st = starts[0] < 0 ? starts[0] + v.type.shape[r - 1] : starts[0];
+    return st == start && o.type.shape.size() == (size_t)r && o.type.shape[r - 1] == len;
+  }
+
+  bool is_negation(const Node* n) {
+    if (!n) return false;
+    if (n->op == "gawee.neg") return n->ins.size() == 1;
+    if (n->op != "linalg.generic" || n->n_linalg_ins != 1 || n->outs.size() != 1) return false;
+    if (!n->maps.empty() && !n->maps[0].is_identity()) return false;
+    const EProgram& b = n->body;
+    return b.code.size() == 1 && b.code[0].op == EOp::NEGF && b.code[0].a == 0 && b.result == b.code[0].dst;
+  }
+
+  void find_rope_clusters() {
+    Graph& g = plan_->g;
+    for (size_t i = 0; i < g.nodes.size(); ++i) {
+      const Node& R = g.nodes[i];
+      if (R.op != "gawee.add" || R.ins.size() != 2 || skip_node_.count((int)i)) continue;
+      const auto& os = val(R.outs[0]).type.shape;
+      if (os.empty() || os.size() > 4 || os.back() % 2 || val(R.outs[0]).type.dtype != DType::F32) continue;
+      const int64_t d = os.back(), half = d / 2;
+      for (int k = 0; k < 2; ++k) {
+        const Node* M1 = node_of(R.ins[k]);
+        const Node* M2 = node_of(R.ins[1 - k]);
+        if (!is_op(M1, "gawee.mul") || !is_op(M2, "gawee.mul") || uses_[R.ins[k]] != 1 || uses_[R.ins[1 - k]] != 1)
+          continue;
+        // M2 = rotate_half(x) * sin
+        int rhi = -1;
+        for (int j = 0; j < 2; ++j)
+          if (is_op(node_of(M2->ins[j]), "gawee.cat")) rhi = j;
+        if (rhi < 0 || uses_[M2->ins[rhi]] != 1) continue;
+        const Node* C = node_of(M2->ins[rhi]);
+        int64_t ax = C->attr("axis").i;
+        if (ax < 0) ax += (int64_t)os.size();
+        if (C->ins.size() != 2 || ax != (int64_t)os.size() - 1) continue;
+        const Node* N = node_of(C->ins[0]);
+        if (!is_negation(N) || uses_[C->ins[0]] != 1 || uses_[C->ins[1]] != 1 || uses_[N->ins[0]] != 1) continue;
+        const Node* S2 = node_of(N->ins[0]);
+        const Node* S1 = node_of(C->ins[1]);
+        if (!S2 || !S1) continue;
+        const int x = S2->ins[0];
+        if (!last_axis_slice(S2, x, half, half) || !last_axis_slice(S1, x, 0, half)) continue;
+        // M1 = x * cos
+        int xi = -1;
+        for (int j = 0; j < 2; ++j)
+          if (M1->ins[j] == x) xi = j;
+        if (xi < 0 || val(x).type.shape != os) continue;
+        const int cs = M1->ins[1 - xi], sn = M2->ins[1 - rhi];
+        auto bcast_ok = [&](int v) {
+          const auto& vs = val(v).type.shape;
+          if (val(v).type.dtype != DType::F32 || vs.size() > os.size()) return false;
+          for (size_t q = 0; q < vs.size(); ++q)
+            if (vs[vs.size() - 1 - q] != 1 && vs[vs.size() - 1 - q] != os[os.size() - 1 - q]) return false;
+          return true;
+        };
+        if (!bcast_ok(cs) || !bcast_ok(sn)) continue;
+        RopeMatch m{x, cs, sn, R.outs[0]};
+        for (int sn2 : {def_node(R.ins[k]), def_node(R.ins[1 - k]), def_node(M2->ins[rhi]), def_node(C->ins[0]),
+                        def_node(N->ins[0]), def_node(C->ins[1])})
+          skip_node_.insert(sn2);
+        rope_at_[(int)i] = m;
+        break;
+      }
+    }
+  }
+
+  void plan_rope(const RopeMatch& m) {
+    const auto& os = val(m.out).type.shape;
+    View x = value_view(m.x);
+    View cs = broadcast_to(value_view(m.cs), os);
+    View sn = broadcast_to(value_view(m.sn), os);
+    View out = alloc(DType::F32, os);
+    Op op;
+    op.kind = OpKind::REMAP;
+    op.name = "rope";
+    op.reads = {x, cs, sn};
+    op.writes = {out};
+    op.launch = launch::rope(x, cs, sn, out);
+    add_op(std::move(op));
+    set_view(m.out, out);
   }
 
   void plan_attention(const AttnMatch& m) {

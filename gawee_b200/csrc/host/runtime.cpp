@@ -695,6 +695,46 @@ Fn reduce(const View& in, const View& out, const std::vector<bool>& red, bool me
   };
 }
 
+Fn rope(const View& x, const View& cs, const View& sn, const View& out) {
+  kern::RopeParams rp{};
+  rp.rank = out.rank();
+  if (rp.rank < 1 || rp.rank > 4) throw std::runtime_error("rope: rank must be 1..4");
+  rp.numel = out.numel();
+  rp.half = out.shape[rp.rank - 1] / 2;
+  for (int d = 0; d < rp.rank; ++d) {
+    rp.shape[d] = out.shape[d];
+    rp.x_st[d] = x.st[d];
+    rp.c_st[d] = cs.st[d];
+    rp.s_st[d] = sn.st[d];
+  }
+  return [rp, x, cs, sn, out](Runtime& rt, void* s) mutable {
+    rp.x = reinterpret_cast<const float*>(rt.ptr(x));
+    rp.cs = reinterpret_cast<const float*>(rt.ptr(cs));
+    rp.sn = reinterpret_cast<const float*>(rt.ptr(sn));
+    rp.out = reinterpret_cast<float*>(rt.ptr(out));
+    kern::launch_rope(rp, static_cast<cudaStream_t>(s));
+  };
+}
+
+Fn rownorm(const View& x, int64_t rows, int64_t cols, int64_t x_rs, const View& w, int64_t w_st, const View& b,
+           int64_t b_st, const View& out, float eps, bool centered) {
+  kern::RowNormParams rp{};
+  rp.rows = rows;
+  rp.cols = cols;
+  rp.x_rs = x_rs;
+  rp.w_st = w_st;
+  rp.b_st = b_st;
+  rp.eps = eps;
+  rp.centered = centered ? 1 : 0;
+  return [rp, x, w, b, out](Runtime& rt, void* s) mutable {
+    rp.x = reinterpret_cast<const float*>(rt.ptr(x));
+    rp.w = reinterpret_cast<const float*>(rt.ptr(w));
+    rp.b = b.buf >= 0 ? reinterpret_cast<const float*>(rt.ptr(b)) : nullptr;
+    rp.out = reinterpret_cast<float*>(rt.ptr(out));
+    kern::launch_rownorm(rp, static_cast<cudaStream_t>(s));
+  };
+}
+
 Fn generic_reduce(const View& in, const View& out, const std::vector<bool>& red, const EProgram& body) {
   kern::GenericReduceParams gp{};
   split_dims(in, red, nullptr, &gp, out);

@@ -177,6 +177,38 @@ struct RangeParams {
 };
 void launch_range(const RangeParams& p, cudaStream_t s);
 
+// Row normalisation, the reference's RMSNorm / LayerNorm chains over the
+// last dim in one pass per row: (centered: xc = x - mean(x), else xc = x)
+//   out = (xc / sqrt(mean(xc * xc) + eps)) * w  [+ b]
+// mean = sum / cols (ReduceMeanOpLowering: sum, then divide).  Row i starts at
+// x + i * x_rs (elements, cols contiguous); w / b indexed by column with
+// stride w_st / b_st (0 = broadcast scalar); out dense [rows][cols].
+struct RowNormParams {
+  const float* x;
+  float* out;
+  const float* w;
+  const float* b;  // nullptr: no bias
+  int64_t rows, cols, x_rs, w_st, b_st;
+  float eps;
+  int centered;
+};
+void launch_rownorm(const RowNormParams& p, cudaStream_t s);
+
+// Rotary position embedding as the reference's graph computes it:
+//   out = x * cos + rotate_half(x) * sin,  rotate_half(x)[i] = -x[i + d/2] (i < d/2), x[i - d/2] (else)
+// over the last dim d (= 2 * half).  x, cos, sin are strided views over the
+// output shape (stride 0 = broadcast); out is dense.
+struct RopeParams {
+  const float* x;
+  const float* cs;
+  const float* sn;
+  float* out;
+  int rank;  // <= 4
+  int64_t numel, half;
+  int64_t shape[4], x_st[4], c_st[4], s_st[4];
+};
+void launch_rope(const RopeParams& p, cudaStream_t s);
+
 // Max / sum pooling over (n, c, oh, ow) with arbitrary strides on both sides.
 struct PoolParams {
   const float* in;

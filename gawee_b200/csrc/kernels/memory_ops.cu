@@ -927,6 +927,171 @@ void launch_topk(const TopKParams& p, cudaStream_t s) {
 }
 
 // ---------------------------------------------------------------------------
+// Row normalisation: one warp per row.  The row is read twice (the second
+// read hits L1), written once; the sums are per-lane then a shuffle tree.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads) rownorm_kernel(const __grid_constant__ RowNormParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
+  const float count = (float)p.cols;  // the mean divides by it, as the reference does
+  const bool vec = (p.cols & 3) == 0 && (p.x_rs & 3) == 0 && (reinterpret_cast<uintptr_t>(p.x) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 && p.w_st == 1 &&
+                   (reinterpret_cast<uintptr_t>(p.w) & 15) == 0 &&
+                   (!p.b || (p.b_st == 1 && (reinterpret_cast<uintptr_t>(p.b) & 15) == 0));
+  auto warp_sum = [](float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+  };
+  for (int64_t row = blockIdx.x * (int64_t)(blockDim.x / 32) + threadIdx.x / 32; row < p.rows; row += warps) {
+    const float* x = p.x + row * p.x_rs;
+    float* y = p.out + row * p.cols;
+    float mu = 0.f;
+    if (p.centered) {
+      float s = 0.f;
+      if (vec) {
+        for (int64_t c = lane * 4; c < p.cols; c += 128) {
+          const float4 v = *reinterpret_cast<const float4*>(x + c);
+          s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v.x), v.y), v.z), v.w);
+        }
+      } else {
+        for (int64_t c = lane; c < p.cols; c += 32) s = __fadd_rn(s, x[c]);
+      }
+      mu = __fdiv_rn(warp_sum(s), count);
+    }
+    float s2 = 0.f;
+    if (vec) {
+      for (int64_t c = lane * 4; c < p.cols; c += 128) {
+        const float4 v = *reinterpret_cast<const float4*>(x + c);
+        const float a = __fsub_rn(v.x, mu), b = __fsub_rn(v.y, mu), d = __fsub_rn(v.z, mu), e = __fsub_rn(v.w, mu);
+        s2 = __fadd_rn(s2, __fmul_rn(a, a));
+        s2 = __fadd_rn(s2, __fmul_rn(b, b));
+        s2 = __fadd_rn(s2, __fmul_rn(d, d));
+        s2 = __fadd_rn(s2, __fmul_rn(e, e));
+      }
+    } else {
+      for (int64_t c = lane; c < p.cols; c += 32) {
+        const float a = __fsub_rn(x[c], mu);
+        s2 = __fadd_rn(s2, __fmul_rn(a, a));
+      }
+    }
+    const float r = __fsqrt_rn(__fadd_rn(__fdiv_rn(warp_sum(s2), count), p.eps));
+    if (vec) {
+      for (int64_t c = lane * 4; c < p.cols; c += 128) {
+        const float4 v = *reinterpret_cast<const float4*>(x + c);
+        const float4 w = __ldg(reinterpret_cast<const float4*>(p.w + c));
+        float4 o = make_float4(__fmul_rn(__fdiv_rn(__fsub_rn(v.x, mu), r), w.x),
+                               __fmul_rn(__fdiv_rn(__fsub_rn(v.y, mu), r), w.y),
+                               __fmul_rn(__fdiv_rn(__fsub_rn(v.z, mu), r), w.z),
+                               __fmul_rn(__fdiv_rn(__fsub_rn(v.w, mu), r), w.w));
+        if (p.b) {
+          const float4 bb = __ldg(reinterpret_cast<const float4*>(p.b + c));
+          o = make_float4(__fadd_rn(o.x, bb.x), __fadd_rn(o.y, bb.y), __fadd_rn(o.z, bb.z), __fadd_rn(o.w, bb.w));
+        }
+        *reinterpret_cast<float4*>(y + c) = o;
+      }
+    } else {
+      for (int64_t c = lane; c < p.cols; c += 32) {
+        float o = __fmul_rn(__fdiv_rn(__fsub_rn(x[c], mu), r), __ldg(p.w + c * p.w_st));
+        if (p.b) o = __fadd_rn(o, __ldg(p.b + c * p.b_st));
+        y[c] = o;
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) rope_kernel(const __grid_constant__ RopeParams p) {
+  const int r = p.rank;
+  const int64_t d = p.shape[r - 1];
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < p.numel; i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rem = i / d;
+    const int64_t col = i - rem * d;
+    int64_t xo = 0, co = 0, so = 0;
+    for (int k = r - 2; k >= 0; --k) {
+      const int64_t c = rem % p.shape[k];
+      rem /= p.shape[k];
+      xo += c * p.x_st[k];
+      co += c * p.c_st[k];
+      so += c * p.s_st[k];
+    }
+    const int64_t xl = p.x_st[r - 1];
+    const float xv = p.x[xo + col * xl];
+    const float rot = col < p.half ? -p.x[xo + (col + p.half) * xl] : p.x[xo + (col - p.half) * xl];
+    p.out[i] = __fadd_rn(__fmul_rn(xv, __ldg(p.cs + co + col * p.c_st[r - 1])),
+                         __fmul_rn(rot, __ldg(p.sn + so + col * p.s_st[r - 1])));
+  }
+}
+
+// Four consecutive outputs of one row per thread (d and d / 2 multiples of
+// 4, so the four sit on one side of the half), 32-bit coordinates, float4
+// loads of x, cos and sin where their last stride is 1 and rows are aligned.
+__global__ void __launch_bounds__(kThreads) rope4_kernel(const __grid_constant__ RopeParams p, unsigned vec_mask) {
+  const int r = p.rank;
+  const uint32_t d = (uint32_t)p.shape[r - 1], q4 = d / 4, half = (uint32_t)p.half;
+  const uint32_t total = (uint32_t)(p.numel / 4);
+  for (uint32_t u = blockIdx.x * blockDim.x + threadIdx.x; u < total; u += gridDim.x * blockDim.x) {
+    uint32_t rem = u / q4;
+    const uint32_t col = (u - rem * q4) * 4;
+    int64_t xo = 0, co = 0, so = 0;
+    for (int k = r - 2; k >= 0; --k) {
+      const uint32_t sh = (uint32_t)p.shape[k];
+      const uint32_t qq = rem / sh;
+      const int64_t c = rem - qq * sh;
+      rem = qq;
+      xo += c * p.x_st[k];
+      co += c * p.c_st[k];
+      so += c * p.s_st[k];
+    }
+    const uint32_t rcol = col < half ? col + half : col - half;
+    float xv[4], rv[4], cv[4], sv[4];
+    auto load4 = [&](const float* base, int64_t st, bool v, float (&o)[4]) {
+      if (v) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(base));
+        o[0] = t.x; o[1] = t.y; o[2] = t.z; o[3] = t.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[e] = __ldg(base + e * st);
+      }
+    };
+    const int64_t xl = p.x_st[r - 1], cl = p.c_st[r - 1], sl = p.s_st[r - 1];
+    load4(p.x + xo + col * xl, xl, vec_mask & 1, xv);
+    load4(p.x + xo + rcol * xl, xl, vec_mask & 1, rv);
+    load4(p.cs + co + col * cl, cl, vec_mask & 2, cv);
+    load4(p.sn + so + col * sl, sl, vec_mask & 4, sv);
+    const bool neg = col < half;
+    float o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      o[e] = __fadd_rn(__fmul_rn(xv[e], cv[e]), __fmul_rn(neg ? -rv[e] : rv[e], sv[e]));
+    *reinterpret_cast<float4*>(p.out + (int64_t)u * 4) = make_float4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+void launch_rope(const RopeParams& p, cudaStream_t s) {
+  if (p.numel <= 0) return;
+  const int r = p.rank;
+  const int64_t d = p.shape[r - 1];
+  auto rows_aligned = [&](const float* b, const int64_t* st) {
+    if (st[r - 1] != 1 || (reinterpret_cast<uintptr_t>(b) & 15)) return false;
+    for (int k = 0; k < r - 1; ++k)
+      if (st[k] % 4) return false;
+    return true;
+  };
+  if (d % 8 == 0 && p.numel / 4 < (int64_t(1) << 31) && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0) {
+    const unsigned mask = (rows_aligned(p.x, p.x_st) ? 1u : 0u) | (rows_aligned(p.cs, p.c_st) ? 2u : 0u) |
+                          (rows_aligned(p.sn, p.s_st) ? 4u : 0u);
+    rope4_kernel<<<resident_grid<rope4_kernel>(p.numel / 4), kThreads, 0, s>>>(p, mask);
+    return;
+  }
+  rope_kernel<<<resident_grid<rope_kernel>(p.numel), kThreads, 0, s>>>(p);
+}
+
+void launch_rownorm(const RowNormParams& p, cudaStream_t s) {
+  if (p.rows <= 0) return;
+  rownorm_kernel<<<resident_grid<rownorm_kernel>(p.rows * 32), kThreads, 0, s>>>(p);
+}
+
+// ---------------------------------------------------------------------------
 // B-operand packing into TF32 hi/lo planes [batch][N][ldk].
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads) pack_b_kernel(const __grid_constant__ PackBParams p) {

@@ -332,3 +332,44 @@ def test_golden_fixtures_on_cuda():
             m.close()
         for k, o in enumerate(outs):
             compare(o, data[f"out{k}"], atol=float(data["atol"]), rtol=1e-5, what=f"{name} output{k}")
+
+
+def _names(mlir):
+    from gawee_b200.runtime import plan_text
+    return plan_text(mlir)
+
+
+def test_fused_rms_and_layer_norm():
+    """RMSNorm and LayerNorm chains as the emitter decomposes them (Pow /
+    ReduceMean / Add / Sqrt / Div / Mul [/ Add], centering by Sub of a mean)
+    run as one row kernel each, on a dense and on a strided (transposed)
+    input, within fp32 rounding of the oracle's sequential sums."""
+    from gawee_b200.synth import _layer_norm, _rms_norm
+
+    def g_(g):
+        x = rand_input(g, (2, 5, 96), 91, scale=3.0)
+        xt = g.transpose(rand_input(g, (5, 2, 96), 92), [1, 0, 2])  # rows with two strides
+        y = rand_input(g, (3, 7, 100), 93)                           # cols not a multiple of 4
+        return [_rms_norm(g, x, 1e-5), _rms_norm(g, xt, 1e-6), _layer_norm(g, y, 1e-12), _layer_norm(g, x, 1e-5)]
+    mlir, args = build(g_)
+    s = _names(mlir)
+    assert s.count("rms_norm") == 2 and s.count("layer_norm") == 2, s
+    parity(mlir, args, atol=2e-6, rtol=2e-6)
+
+
+def test_fused_rope():
+    """x * cos + rotate_half(x) * sin (Slice / Neg / Concat / Mul / Add) as
+    one kernel, over a transposed [B, H, S, D] view with broadcast tables:
+    the same IEEE operations as the graph, bit-exact."""
+    def g_(g):
+        x = g.transpose(rand_input(g, (2, 7, 3, 16), 95), [0, 2, 1, 3])     # [2, 3, 7, 16]
+        cos = g.unsqueeze(rand_input(g, (7, 16), 96), [0, 1])
+        sin = g.unsqueeze(rand_input(g, (7, 16), 97), [0, 1])
+        d = 16
+        x1 = g.slice(x, [0], [d // 2], [3])
+        x2 = g.slice(x, [d // 2], [d], [3])
+        rot = g.cat([g.neg(x2), x1], 3)
+        return [g.add(g.mul(x, cos), g.mul(rot, sin))]
+    mlir, args = build(g_)
+    assert "rope" in _names(mlir)
+    parity(mlir, args, atol=0.0, rtol=0.0)

@@ -74,3 +74,50 @@ def test_gqa_decoder_reduced():
     # the 135M GQA architecture (hidden 576, 9 q / 3 kv heads of 64, SwiGLU 1536)
     # with 2 layers, batch 2 and sequence 64 so the oracle finishes in seconds
     _check(synth.llama(2, 64, dim=576, layers=2, heads=9, kv_heads=3, ffn=1536, vocab=4096, name="decoder135m_l2"))
+
+
+def test_decoder135m_full_size_sampled_sequences_match_oracle():
+    """Configuration 4 at its full size: the 135M GQA decoder (30 layers,
+    hidden 576, 9 / 3 heads) prefilling batch 64 x 512 tokens.  Sequences
+    are independent, so the logits of the first and the last sequence of the
+    full-batch GPU forward must match the oracle's forward of those single
+    sequences, at the reference's transformer tolerance (5e-4 absolute,
+    1e-4 relative).  Only those rows are copied back (the full logits are
+    6.4 GB)."""
+    import os
+
+    import torch
+
+    import oracle
+    from gawee_b200.runtime import Model
+
+    big = synth.smollm135m(64, 512)
+    args = big.make_args()
+    rows = (0, 63)
+    m = Model(big.mlir)
+    try:
+        m.set_args(args)
+        got = []
+        for _ in range(2):  # eager, then the replayed CUDA graph
+            m.forward()
+            m.synchronize()
+            base = m.output_ptr(0)
+            row_elems = 512 * 49152
+            per = []
+            from cuda.bindings import runtime as cudart
+            for r in rows:
+                t = torch.empty(row_elems, dtype=torch.float32, device="cuda")
+                err, = cudart.cudaMemcpy(t.data_ptr(), base + r * row_elems * 4, row_elems * 4,
+                                         cudart.cudaMemcpyKind.cudaMemcpyDeviceToDevice)
+                assert err == cudart.cudaError_t.cudaSuccess
+                per.append(t.cpu().numpy().reshape(1, 512, 49152))
+            got.append(per)
+    finally:
+        m.close()
+    one = synth.smollm135m(1, 512)  # same weights: they do not depend on the batch size
+    o = oracle.Oracle(one.mlir)
+    for i, r in enumerate(rows):
+        a1 = [np.ascontiguousarray(args[0][r:r + 1])] + list(args[1:])
+        want = o.run(a1, threads=os.cpu_count() or 1)[0]
+        for k in range(2):
+            compare(got[k][i], want, 5e-4, 1e-4, f"decoder135m b64 sequence {r} run {k}")

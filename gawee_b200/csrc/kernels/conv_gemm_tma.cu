@@ -12,17 +12,19 @@
 //     padding, stride and dilation applied by the copy engine (zero fill
 //     outside the image).  A plain GEMM uses a tiled 2-D map over its rows.
 //     Both land in the 128-byte-swizzled K-major layout the MMA reads.
-//   * The MMAs that take the raw A value (the tensor core reads fp32 as TF32
-//     by dropping the 13 low mantissa bits, so raw is the high part) read it
-//     from shared memory.  The four A warps only form the remainders
-//     x - tf32(x) of each staged tile and store them to tensor memory, where
-//     the lo*hi MMA reads them.
+//   * The four A warps read each staged A tile once and store its raw values
+//     (the tensor core reads fp32 as TF32 by dropping the 13 low mantissa
+//     bits, so raw is the high part) and remainders x - tf32(x) to tensor
+//     memory; all three MMAs take A from there and only B from shared
+//     memory.  (Measured: an MMA reading A from shared memory costs about
+//     twice one reading it from tensor memory here, where TMA writes and
+//     the A warps' reads share the shared-memory bandwidth.)
 //   * Shared-memory stages (one k-block of A and of both B planes each) and
 //     round accumulators (tensor memory) are separate pipelines: a stage is
 //     refilled as soon as its MMAs complete, up to NS k-blocks ahead.
 //
 // Warp roles (448 threads), persistent over work units (tile, k split):
-//   warps 0-3  remainders: wait for a stage, read its A rows, store the
+//   warps 0-3  A: wait for a stage, read its A rows, store raw values and
 //              remainders into the stage's tensor-memory columns
 //   warp 4     TMA for A and the B planes; owns the tensor-memory allocation
 //   warp 5     lane 0 issues the MMAs and the commits that track them
@@ -46,13 +48,14 @@ namespace kern {
 
 namespace {
 
-// Stages per tile width: 4 x 48 KB (BN 128) or 6 x 32 KB (BN 64) of shared
-// memory, plus 20 KB of epilogue staging.
+// Stages per tile width: 4 x 48 KB (BN 128) or 4 x 32 KB (BN 64) of shared
+// memory plus 20 KB of epilogue staging; tensor memory holds 4 A stages of
+// 64 columns (raw, remainder) beside the two round accumulators.
 template <int BN>
 struct TmaConfig;
 template <>
 struct TmaConfig<64> {
-  static constexpr int NS = 6;
+  static constexpr int NS = 4;
 };
 template <>
 struct TmaConfig<128> {
@@ -73,8 +76,8 @@ struct TmaSmem {
   // BN 64 folds hi*hi and hi*lo into one N = 128 MMA (B stage: hi rows then lo rows)
   static constexpr bool kFold = BN == 64;
   static constexpr int kAccCols = kFold ? 2 * BN : BN;
-  static constexpr int kRemCol = kNAcc * kAccCols;      // first remainder column
-  static constexpr int kUsedCols = kRemCol + NS * kBK;  // 32 remainder columns per stage
+  static constexpr int kACol = kNAcc * kAccCols;          // first A column
+  static constexpr int kUsedCols = kACol + NS * 2 * kBK;  // per stage 32 raw and 32 remainder columns
   static constexpr int kTmemCols = kUsedCols <= 256 ? 256 : 512;
   static_assert(kStage % 1024 == 0, "stages must keep the 1024-byte swizzle alignment");
   static_assert(kUsedCols <= 512, "tensor memory columns");
@@ -96,17 +99,6 @@ __device__ __forceinline__ void tma_load_im2col_4d(uint32_t dst, const CUtensorM
       "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
       "[%2], {%7, %8};" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c), "r"(w), "r"(h), "r"(n), "h"(ow), "h"(oh)
-      : "memory");
-}
-
-// D (tensor memory) += A (shared memory) . B (shared memory)
-__device__ __forceinline__ void umma_tf32_ss(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                             uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -204,16 +196,24 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           }
           // the stage's raw A row, 128-byte-swizzled: chunk c of row r sits at c ^ (r & 7)
           const uint32_t src = smem_u32(smem + st * L::kStage) + row * 128;
-          uint32_t y[32];
+          uint32_t x[32];
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const float4 v = lds128(src + ((c ^ (row & 7)) << 4));
-            y[4 * c] = __float_as_uint(__fsub_rn(v.x, tf32_hi(v.x)));
-            y[4 * c + 1] = __float_as_uint(__fsub_rn(v.y, tf32_hi(v.y)));
-            y[4 * c + 2] = __float_as_uint(__fsub_rn(v.z, tf32_hi(v.z)));
-            y[4 * c + 3] = __float_as_uint(__fsub_rn(v.w, tf32_hi(v.w)));
+            x[4 * c] = __float_as_uint(v.x);
+            x[4 * c + 1] = __float_as_uint(v.y);
+            x[4 * c + 2] = __float_as_uint(v.z);
+            x[4 * c + 3] = __float_as_uint(v.w);
           }
-          tmem_st32(tmem_rows + (uint32_t)(L::kRemCol + st * kBK), y);
+          const uint32_t acol = tmem_rows + (uint32_t)(L::kACol + st * 2 * kBK);
+          tmem_st32(acol, x);
+          uint32_t y[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float v = __uint_as_float(x[e]);
+            y[e] = __float_as_uint(__fsub_rn(v, tf32_hi(v)));
+          }
+          tmem_st32(acol + kBK, y);
           asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
           tc_fence_before();
           __syncwarp();
@@ -307,23 +307,23 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           }
           tc_fence_after();
           if (lane == 0) {
-            const uint64_t da = desc0 + (uint64_t)st * kStageDesc;
-            const uint64_t dbh = da + kATileDesc;
+            const uint64_t dbh = desc0 + (uint64_t)st * kStageDesc + kATileDesc;
             const uint64_t dbl = dbh + kBTileDesc;
-            const uint32_t a_rem = tmem_base + (uint32_t)(L::kRemCol + st * kBK);
+            const uint32_t a_raw = tmem_base + (uint32_t)(L::kACol + st * 2 * kBK);
+            const uint32_t a_rem = a_raw + kBK;
             // a K-major SW128 descriptor advances 32 bytes (2 units) per
-            // 8-wide k-step; a remainder column holds one k
+            // 8-wide k-step; an A column holds one k
 #pragma unroll
             for (int kk = 0; kk < kBK / 8; ++kk) {
               const uint64_t o = (uint64_t)(2 * kk);
               const uint32_t ka = (uint32_t)(8 * kk);
               const uint32_t first = (j | kk) != 0;
               if (L::kFold) {
-                umma_tf32_ss(tmem_d, da + o, dbh + o, idesc2, first);  // [hi*hi | hi*lo]
-                umma_tf32_ts(tmem_d, a_rem + ka, dbh + o, idesc, 1);   // lo*hi
+                umma_tf32_ts(tmem_d, a_raw + ka, dbh + o, idesc2, first);  // [hi*hi | hi*lo]
+                umma_tf32_ts(tmem_d, a_rem + ka, dbh + o, idesc, 1);       // lo*hi
               } else {
-                umma_tf32_ss(tmem_d, da + o, dbh + o, idesc, first);
-                umma_tf32_ss(tmem_d, da + o, dbl + o, idesc, 1);
+                umma_tf32_ts(tmem_d, a_raw + ka, dbh + o, idesc, first);
+                umma_tf32_ts(tmem_d, a_raw + ka, dbl + o, idesc, 1);
                 umma_tf32_ts(tmem_d, a_rem + ka, dbh + o, idesc, 1);
               }
             }

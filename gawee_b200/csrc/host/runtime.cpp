@@ -107,6 +107,7 @@ struct Runtime {
   cudaGraph_t graph = nullptr;
   std::vector<std::array<TMap, 3>> tmaps;  // per op (TC only): B hi, B lo, A (TMA-fed kernel)
   std::vector<int> a_tma;                  // per op (TC only): kern::ATma, A_TMA_NONE = warp gather
+  int tma_rk = kern::kRK;                  // TMA kernel: k-blocks per promotion round
   std::vector<int> ksplit;                 // per op (TC only): k splits, 1 = none
   std::vector<uint8_t*> attn_skip;         // per op (ATTN only): skip flags of the mask tiles
   std::vector<std::array<std::array<int8_t, 3>, 3>> attn_cpos;  // per op (ATTN): tensor-map dim order
@@ -227,6 +228,10 @@ void Runtime::build_tensor_maps() {
   // GAWEE_MAX_KSPLIT caps the k splits of small contractions (1 disables them)
   int cap = 32;
   if (const char* e = std::getenv("GAWEE_MAX_KSPLIT")) cap = std::max(1, std::atoi(e));
+  // GAWEE_TMA_ROUND_KB: k-blocks per promotion round of the TMA kernel (1..16).
+  // Longer rounds accumulate more truncating tensor-memory additions: at 4 the
+  // ResNet-18 logits left the reference tolerance (1.47x of it, 0.80x at 2).
+  if (const char* e = std::getenv("GAWEE_TMA_ROUND_KB")) tma_rk = std::min(16, std::max(1, std::atoi(e)));
   size_t ws_floats = 0;
   attn_skip.assign(P.ops.size(), nullptr);
   attn_cpos.assign(P.ops.size(), {});
@@ -262,11 +267,16 @@ void Runtime::build_tensor_maps() {
     // 32-channel k-blocks (im2col), or an unbatched GEMM with aligned rows
     if (use_tma && nb == 1) {
       const float* x = reinterpret_cast<const float*>(ptr(t.x));
-      if (t.conv && t.C % 32 == 0) {
+      // tap blocks (C = 4, 8, 16) only on request: on the ResNet stem (C = 4,
+      // 16-byte pixels) the im2col copies ran slower than the warp gather
+      bool taps = false;
+      if (const char* e = std::getenv("GAWEE_TC_TMA_TAPS")) taps = std::atoi(e) != 0;
+      if (t.conv && (t.C % 32 == 0 || (taps && (t.C == 4 || t.C == 8 || t.C == 16)))) {
+        int mode = kern::A_TMA_NONE;
         if (kern::make_a_tensor_map_im2col(x, t.x.shape[0], t.H, t.W, t.C, t.x.shape[0] > 1 ? t.x.st[0] : 0,
                                            t.x.st[2], t.x.st[3], t.R, t.S, t.sh, t.sw, t.ph, t.pw, t.dh, t.dw,
-                                           tmaps[o][2].b))
-          a_tma[o] = kern::A_TMA_IM2COL;
+                                           tmaps[o][2].b, &mode))
+          a_tma[o] = mode;
       } else if (!t.conv) {
         const int r = t.x.rank();
         if (t.x.st[r - 1] == 1 &&
@@ -274,7 +284,8 @@ void Runtime::build_tensor_maps() {
           a_tma[o] = kern::A_TMA_2D;
       }
     }
-    const int k = std::min(cap, kern::choose_ksplit(gr.M, t.N, t.K, nb, t.block_n, t.epi, sms));
+    const int k = std::min(cap, kern::choose_ksplit(gr.M, t.N, t.K, nb, t.block_n, t.epi, sms,
+                                                    a_tma[o] != kern::A_TMA_NONE ? tma_rk : kern::kRK));
     ksplit[o] = k;
     if (k > 1) ws_floats = std::max(ws_floats, (size_t)k * (size_t)gr.M * (size_t)t.N);
   }
@@ -519,6 +530,7 @@ static void launch_tc(Runtime& rt, int o, const Op& op, cudaStream_t s) {
   bool launched;
   if (rt.a_tma[o] != kern::A_TMA_NONE) {
     p.a_tma = rt.a_tma[o];
+    p.rk = rt.tma_rk;
     launched = kern::launch_conv_gemm_tma(p, rt.tmaps[o][2].b, rt.tmaps[o][0].b, rt.tmaps[o][1].b, t.block_n, s);
   } else {
     launched = kern::launch_conv_gemm_tc(p, rt.tmaps[o][0].b, rt.tmaps[o][1].b, t.block_n, s);
@@ -1120,7 +1132,9 @@ gawee_status gawee_op_info(const gawee_ctx* ctx, int i, char* name, size_t n, in
   if (name && n) {
     std::string nm = op.name;
     if (op.kind == gawee::OpKind::TC && o < (int)ctx->rt.a_tma.size() && ctx->rt.a_tma[o] != gawee::kern::A_TMA_NONE)
-      nm += ctx->rt.a_tma[o] == gawee::kern::A_TMA_IM2COL ? " [tma im2col]" : " [tma]";
+      nm += ctx->rt.a_tma[o] == gawee::kern::A_TMA_IM2COL        ? " [tma im2col]"
+            : ctx->rt.a_tma[o] == gawee::kern::A_TMA_IM2COL_TAPS ? " [tma im2col taps]"
+                                                                  : " [tma]";
     if (op.kind == gawee::OpKind::TC && o < (int)ctx->rt.ksplit.size() && ctx->rt.ksplit[o] > 1)
       nm += " [split-k " + std::to_string(ctx->rt.ksplit[o]) + "]";
     std::strncpy(name, nm.c_str(), n - 1);

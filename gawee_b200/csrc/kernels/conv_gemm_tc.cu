@@ -681,10 +681,10 @@ bool make_b_tensor_maps(const float* hi, const float* lo, int64_t batch, int64_t
   return true;
 }
 
-int choose_ksplit(int64_t M, int64_t N, int64_t K, int nb, int block_n, int epi, int sms) {
-  if (nb != 1 || epi > EPI_BIAS_ADD_RELU || M <= 0 || N <= 0 || K <= 0 || sms <= 0) return 1;
+int choose_ksplit(int64_t M, int64_t N, int64_t K, int nb, int block_n, int epi, int sms, int rk) {
+  if (nb != 1 || epi > EPI_BIAS_ADD_RELU || M <= 0 || N <= 0 || K <= 0 || sms <= 0 || rk <= 0) return 1;
   const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + block_n - 1) / block_n);
-  const int rounds = (int)(((K + kBK - 1) / kBK + kRK - 1) / kRK);
+  const int rounds = (int)(((K + kBK - 1) / kBK + rk - 1) / rk);
   // Estimated time in rounds: waves of units x (rounds per unit + the fixed
   // cost of a unit: pipeline fill and epilogue, about 1.5 rounds), plus the
   // reduce pass (about half a round per extra split of a tile's outputs).

@@ -113,7 +113,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* full = bars;               // stage loaded (TMA transaction bytes)
-  uint64_t* remr = bars + NS;          // stage's remainders in tensor memory (4 A warps)
+  uint64_t* remr = bars + NS;          // stage's A in tensor memory, and for a round's first stage
+                                       // the round's accumulator drained (4 A warps)
   uint64_t* empty = bars + 2 * NS;     // stage's MMAs completed (one commit)
   uint64_t* accf = bars + 3 * NS;      // round accumulator complete (one commit)
   uint64_t* acce = accf + L::kNAcc;    // round accumulator drained (8 accumulator warps)
@@ -124,8 +125,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   const int num_kb = (int)((p.K + kBK - 1) / kBK);
-  const int num_rounds = (num_kb + kRK - 1) / kRK;
-  auto round_kbs = [&](int r) { return min(kRK, num_kb - r * kRK); };
+  const int rk = p.rk;  // k-blocks per promotion round (the launcher fills it)
+  const int num_rounds = (num_kb + rk - 1) / rk;
+  auto round_kbs = [&](int r) { return min(rk, num_kb - r * rk); };
   const int64_t m_tiles = (p.M + kBM - 1) / kBM;
   const int64_t n_tiles = (p.N + BN - 1) / BN;
   const int64_t num_tiles = m_tiles * n_tiles;  // unbatched: the launcher requires nb == 1
@@ -180,13 +182,20 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     // Lane = row of the A tile = tensor-memory lane (warp w owns 32w..32w+31).
     const int row = warp * 32 + lane;
     const uint32_t tmem_rows = tmem_base + ((uint32_t)(warp * 32) << 16);
-    uint32_t g = 0;  // k-blocks consumed
+    const bool taps = p.a_tma == A_TMA_IM2COL_TAPS;
+    // tap blocks: C / 4 16-byte chunks per row (C = 4, 8, 16 -> shift 0, 1, 2)
+    const uint32_t tap_shift = taps ? (p.C == 4 ? 0u : p.C == 8 ? 1u : 2u) : 0u;
+    const uint32_t tap_mask = (1u << tap_shift) - 1u;
+    const uint32_t row_bytes = taps ? (uint32_t)p.C * 4u : 0u;
+    const uint32_t tap_bytes = row_bytes * kBM;
+    uint32_t g = 0;   // k-blocks consumed
+    uint32_t ar = 0;  // rounds consumed
     bool alive = true;
     for (int64_t u = blockIdx.x; u < num_units && alive; u += gridDim.x) {
       int64_t m0;
       int n0, split, r_lo, nr;
       unit_split(u, m0, n0, split, r_lo, nr);
-      for (int rr = 0; rr < nr && alive; ++rr) {
+      for (int rr = 0; rr < nr && alive; ++rr, ++ar) {
         const int nk = round_kbs(r_lo + (r_rotation(m0, nr) + rr) % nr);
         for (int j = 0; j < nk; ++j, ++g) {
           const uint32_t st = g % NS;
@@ -194,12 +203,17 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             alive = false;
             break;
           }
-          // the stage's raw A row, 128-byte-swizzled: chunk c of row r sits at c ^ (r & 7)
-          const uint32_t src = smem_u32(smem + st * L::kStage) + row * 128;
+          // the stage's raw A row: 128-byte-swizzled (chunk c of row r sits at
+          // c ^ (r & 7)), or for tap blocks chunk c at tap c / (C / 4) of
+          // 128 rows x C * 4 bytes, byte (c % (C / 4)) * 16 of the row
+          const uint32_t stage = smem_u32(smem + st * L::kStage);
           uint32_t x[32];
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
-            const float4 v = lds128(src + ((c ^ (row & 7)) << 4));
+            const uint32_t addr = taps ? stage + (uint32_t)(c >> tap_shift) * tap_bytes + row * row_bytes +
+                                             ((uint32_t)(c & tap_mask) << 4)
+                                       : stage + row * 128 + ((c ^ (row & 7)) << 4);
+            const float4 v = lds128(addr);
             x[4 * c] = __float_as_uint(v.x);
             x[4 * c + 1] = __float_as_uint(v.y);
             x[4 * c + 2] = __float_as_uint(v.z);
@@ -215,6 +229,15 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           }
           tmem_st32(acol + kBK, y);
           asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+          // A round's first stage also certifies that the accumulator buffer
+          // the round overwrites has been drained, so the MMA issuer never
+          // waits on the accumulator warps itself (every wait it makes is
+          // idle tensor time: the tensor core queues only a few MMAs).
+          if (j == 0 &&
+              !__all_sync(0xffffffffu, mbar_wait(smem_u32(&acce[ar & 1]), ((ar >> 1) & 1) ^ 1, abort_flag, p.status))) {
+            alive = false;
+            break;
+          }
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(smem_u32(&remr[st]));
@@ -253,12 +276,22 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             const uint32_t bar = smem_u32(&full[st]);
             mbar_arrive_tx(bar, (uint32_t)L::kStage);
             const uint32_t sa = smem_u32(smem + st * L::kStage);
-            const int k0 = (r * kRK + j) * kBK;
+            const int k0 = (r * rk + j) * kBK;
             if (p.a_tma == A_TMA_IM2COL) {
               const int tap = k0 / C, c0 = k0 - tap * C;  // C is a multiple of 32: one tap per k-block
               const int fr = tap / S, fs = tap - fr * S;
               tma_load_im2col_4d(sa, &tm_a, bar, c0, w0, h0, (int)img, (uint16_t)(fs * p.dw),
                                  (uint16_t)(fr * p.dh));
+            } else if (p.a_tma == A_TMA_IM2COL_TAPS) {
+              // 32 / C taps, each a dense [128][C] block; taps past the filter
+              // repeat its last one (their B rows are the zero fill past K)
+              const int tpk = kBK / C, last = p.R * S - 1;
+              for (int t = 0; t < tpk; ++t) {
+                const int tap = min(k0 / C + t, last);
+                const int fr = tap / S, fs = tap - fr * S;
+                tma_load_im2col_4d(sa + (uint32_t)(t * kBM * C * 4), &tm_a, bar, 0, w0, h0, (int)img,
+                                   (uint16_t)(fs * p.dw), (uint16_t)(fr * p.dh));
+              }
             } else {
               tma_load_2d(sa, &tm_a, bar, k0, (int)m0);
             }
@@ -292,12 +325,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       const int rot = r_rotation(m0, nr);
       for (int rr = 0; rr < nr && alive; ++rr, ++ar) {
         const int nk = round_kbs(r_lo + (rot + rr) % nr);
+        // the round's first remr barrier includes the drain of buffer buf
         const uint32_t buf = ar & 1;
-        if (!mbar_wait(smem_u32(&acce[buf]), ((ar >> 1) & 1) ^ 1, abort_flag, p.status)) {
-          alive = false;
-          break;
-        }
-        tc_fence_after();
         const uint32_t tmem_d = tmem_base + buf * L::kAccCols;
         for (int j = 0; j < nk; ++j, ++g) {
           const uint32_t st = g % NS;
@@ -478,10 +507,11 @@ int conv_gemm_tma_smem_bytes(int block_n) {
 
 bool make_a_tensor_map_im2col(const float* x, int64_t images, int64_t H, int64_t W, int64_t C, int64_t x_sn,
                               int64_t x_sh, int64_t x_sw, int R, int S, int sh, int sw, int ph, int pw, int dh,
-                              int dw, void* tmap_out) {
+                              int dw, void* tmap_out, int* mode) {
   auto enc = get_encode_im2col();
   if (!enc) return false;
-  if (C % kBK != 0 || (reinterpret_cast<uintptr_t>(x) & 15)) return false;
+  const bool taps = C == 4 || C == 8 || C == 16;
+  if ((C % kBK != 0 && !taps) || (reinterpret_cast<uintptr_t>(x) & 15)) return false;
   if (images == 1 && x_sn == 0) x_sn = x_sh * H;  // a size-1 dimension: any valid stride
   if (x_sw % 4 || x_sh % 4 || x_sn % 4 || x_sw <= 0 || x_sh <= 0 || x_sn <= 0) return false;
   // bounding box of the window bases: [-pad, dim - 1 + pad - dilation * (filter - 1)],
@@ -494,10 +524,14 @@ bool make_a_tensor_map_im2col(const float* x, int64_t images, int64_t H, int64_t
   cuuint64_t dims[4] = {(cuuint64_t)C, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)images};
   cuuint64_t strides[3] = {(cuuint64_t)(x_sw * 4), (cuuint64_t)(x_sh * 4), (cuuint64_t)(x_sn * 4)};
   cuuint32_t estr[4] = {1, (cuuint32_t)sw, (cuuint32_t)sh, 1};
+  // a tap block of C channels is C * 4 bytes per pixel (16, 32 or 64): dense rows, no swizzle
   CUresult r = enc(static_cast<CUtensorMap*>(tmap_out), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(x),
-                   dims, strides, lower, upper, (cuuint32_t)kBK, (cuuint32_t)kBM, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
+                   dims, strides, lower, upper, (cuuint32_t)(taps ? C : kBK), (cuuint32_t)kBM, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, taps ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  if (mode) *mode = taps ? A_TMA_IM2COL_TAPS : A_TMA_IM2COL;
+  return true;
 }
 
 bool make_a_tensor_map_2d(const float* x, int64_t M, int64_t K, int64_t ld, void* tmap_out) {
@@ -519,10 +553,14 @@ bool launch_conv_gemm_tma(const ConvGemmParams& p_in, const void* tmap_a, const 
                           int block_n, cudaStream_t s) {
   ConvGemmParams p = p_in;
   if (p.M <= 0 || p.N <= 0) return true;
-  if (p.K <= 0 || p.nb != 1 || (p.a_tma != A_TMA_2D && p.a_tma != A_TMA_IM2COL)) return false;
+  if (p.rk <= 0) p.rk = kRK;
+  if (p.rk > 16) return false;
+  if (p.K <= 0 || p.nb != 1 || (p.a_tma != A_TMA_2D && p.a_tma != A_TMA_IM2COL && p.a_tma != A_TMA_IM2COL_TAPS))
+    return false;
   if (p.a_tma == A_TMA_IM2COL && p.C % kBK != 0) return false;
+  if (p.a_tma == A_TMA_IM2COL_TAPS && p.C != 4 && p.C != 8 && p.C != 16) return false;
   if (p.ksplit > 1) {
-    const int rounds = (int)(((p.K + kBK - 1) / kBK + kRK - 1) / kRK);
+    const int rounds = (int)(((p.K + kBK - 1) / kBK + p.rk - 1) / p.rk);
     if (!p.ws || p.epi > EPI_BIAS_ADD_RELU || p.ksplit > rounds) return false;
     p.out = p.ws;  // raw partial sums into the workspace slices
     p.ldc = p.N;

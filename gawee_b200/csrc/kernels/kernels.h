@@ -10,6 +10,11 @@ namespace kern {
 
 constexpr int kMaxRank = 8;
 constexpr int kMaxIn = 8;
+// Promotion granularity of the tensor-core kernels: each round of kRK
+// 32-wide k-blocks is accumulated alone in a tensor-memory buffer, and the
+// accumulator warps add the round sums into fp32 registers with IEEE
+// round-to-nearest (the TMA kernel may take a longer round: ConvGemmParams::rk).
+constexpr int kRK = 2;
 constexpr int kMaxInstr = 40;
 constexpr int kMaxRegs = 32;
 
@@ -314,12 +319,17 @@ struct ConvGemmParams {
   // over the NHWC input (convolutions, C a multiple of 32) or a tiled map over
   // the GEMM rows.
   int a_tma;
+  // launch_conv_gemm_tma only: k-blocks per promotion round (0 = kRK).
+  int rk;
 };
 
 enum ATma : int {
   A_TMA_NONE = 0,    // A gathered by warps (launch_conv_gemm_tc)
   A_TMA_2D = 1,      // tiled 2-D tensor map over rows [M][K] (row stride ld)
   A_TMA_IM2COL = 2,  // im2col tensor map over the NHWC convolution input
+  // im2col with few channels (C = 4, 8 or 16): a k-block spans 32 / C filter
+  // taps, each loaded as its own dense [128 pixels][C] block (no swizzle)
+  A_TMA_IM2COL_TAPS = 3,
 };
 
 enum FastEpi : int {
@@ -368,7 +378,7 @@ bool launch_conv_gemm_tc(const ConvGemmParams& p, const void* tmap_hi, const voi
 // Number of k splits for a contraction of this shape on `sms` SMs (1 = no
 // split): splitting pays when the output tiles leave SMs idle.  The
 // workspace it needs is ksplit * M * N floats (0 when ksplit is 1).
-int choose_ksplit(int64_t M, int64_t N, int64_t K, int nb, int block_n, int epi, int sms);
+int choose_ksplit(int64_t M, int64_t N, int64_t K, int nb, int block_n, int epi, int sms, int rk = kRK);
 
 // The split-K reduction of launch_conv_gemm_tc / launch_conv_gemm_tma: out =
 // epilogue(sum over splits of ws[s]) in split order; p as given to the launch.
@@ -380,12 +390,15 @@ bool launch_conv_gemm_tma(const ConvGemmParams& p, const void* tmap_a, const voi
                           int block_n, cudaStream_t s);
 
 // A-operand tensor maps for launch_conv_gemm_tma.  im2col: NHWC input with
-// element strides x_sn, x_sh, x_sw (channel stride 1, C a multiple of 32), the
-// convolution's filter size, stride, padding and dilation.  2d: rows [M][K]
-// with row stride ld (elements).  Return false when TMA cannot express it.
+// element strides x_sn, x_sh, x_sw (channel stride 1), the convolution's
+// filter size, stride, padding and dilation; C a multiple of 32 gives the
+// A_TMA_IM2COL map (32-channel boxes, 128-byte swizzle), C = 4, 8 or 16 the
+// A_TMA_IM2COL_TAPS map (C-channel boxes, no swizzle); *mode receives which.
+// 2d: rows [M][K] with row stride ld (elements).  Return false when TMA
+// cannot express it.
 bool make_a_tensor_map_im2col(const float* x, int64_t images, int64_t H, int64_t W, int64_t C, int64_t x_sn,
                               int64_t x_sh, int64_t x_sw, int R, int S, int sh, int sw, int ph, int pw, int dh,
-                              int dw, void* tmap_out);
+                              int dw, void* tmap_out, int* mode);
 bool make_a_tensor_map_2d(const float* x, int64_t M, int64_t K, int64_t ld, void* tmap_out);
 int conv_gemm_tma_smem_bytes(int block_n);
 

@@ -22,10 +22,6 @@ constexpr int kBM = 128;
 constexpr int kBK = 32;               // fp32 elements per k-block (one 128-byte swizzle row)
 constexpr int kThreadsTC = 448;  // 4 A warps, 1 TMA, 1 MMA, 8 accumulator warps
 constexpr unsigned long long kWaitNs = 4000000000ull;  // 4 s per barrier wait
-// Promotion granularity: each round of kRK k-blocks (64 k) is accumulated
-// alone in a tensor-memory buffer, and the accumulator warps add the round
-// sums into fp32 registers with IEEE round-to-nearest.
-constexpr int kRK = 2;
 // Epilogue staging: each accumulator warp transposes 16-column chunks of its
 // 32 rows through shared memory (row pitch 20 floats: conflict-free float4
 // writes by row, float4 reads by column group).

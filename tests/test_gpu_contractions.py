@@ -220,13 +220,20 @@ def _run_env(mlir, args, env):
 
 
 TMA_CONVS = [
-    # (N, C, H, W, F, k, stride, pad, dil): channel counts that are multiples of 32 take the TMA kernel
+    # (N, C, H, W, F, k, stride, pad, dil): channel counts that are multiples of 32, or 4, 8 and 16,
+    # take the TMA kernel
     (3, 32, 9, 11, 40, 3, 1, 1, 1),     # tiles span images; F not a multiple of 64
     (2, 64, 17, 17, 64, 3, 2, 1, 1),    # stride 2
     (1, 96, 12, 10, 130, 5, 1, 2, 1),   # 5x5, three 32-channel k-blocks per tap
     (2, 32, 13, 13, 48, 3, 1, 2, 2),    # dilation 2
     (2, 64, 14, 14, 128, 1, 2, 0, 1),   # 1x1 stride-2 downsample
     (1, 32, 23, 21, 64, 7, 2, 3, 1),    # 7x7 stride 2 pad 3: corners -3 / -3
+    # 4, 8 or 16 channels (3 is padded to 4): tap blocks, several taps per k-block
+    (2, 3, 30, 27, 64, 7, 2, 3, 1),     # the ResNet stem's shape: 49 taps, 7 k-blocks, last repeats tap 48
+    (1, 4, 19, 19, 40, 3, 1, 1, 1),     # 9 taps of 4 channels: 2 k-blocks (8 + 1 taps)
+    (2, 8, 15, 16, 64, 3, 1, 1, 1),     # 4 taps per k-block
+    (1, 16, 13, 11, 72, 5, 2, 2, 1),    # 2 taps per k-block, stride 2
+    (1, 8, 12, 12, 64, 3, 1, 2, 2),     # dilation 2 with tap blocks
 ]
 
 
@@ -247,9 +254,9 @@ def test_conv_tma_im2col_matches_gather_and_oracle(n, c, h, w, f, k, s, p, d):
         return [g.relu(y)]
     mlir, args = build(g_)
     want = oracle.run(mlir, args)[0]
-    names, outs = _run_env(mlir, args, {"GAWEE_MAX_KSPLIT": 1})
+    names, outs = _run_env(mlir, args, {"GAWEE_MAX_KSPLIT": 1, "GAWEE_TC_TMA_TAPS": 1})
     names_g, outs_g = _run_env(mlir, args, {"GAWEE_MAX_KSPLIT": 1, "GAWEE_TC_TMA": 0})
-    assert any("tma im2col" in nm for nm in names), names
+    assert any(("tma im2col taps" if c % 32 else "tma im2col") in nm for nm in names), names
     assert not any("tma" in nm for nm in names_g), names_g
     for o in outs + outs_g:
         compare(o[0], want, 1e-4, 1e-4, "conv")

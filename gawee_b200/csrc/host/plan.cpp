@@ -177,7 +177,7 @@ class Planner {
   std::vector<bool> has_view_;
 
   // ---------------------------------------------------------------- attention clusters
-  // matmul(Q, KT) -> div(A, c) -> add(., mask) -> softmax(-1) -> matmul(P, V),
+  // matmul(Q, KT) -> div(A, c) [-> add(., mask)] -> softmax(-1) -> matmul(P, V),
   // every intermediate used once (GaweeToLinalg.cpp:959-1112, 1377-1441,
   // 1885-1900).  K and V may come through the GQA head expansion
   // unsqueeze(x, [2]) -> expand([B, Hkv, rep, S, D]) -> reshape([B, H, S, D]),
@@ -233,19 +233,24 @@ class Planner {
       int64_t axis = P->has_attr("axis") ? P->attr("axis").i : -1;
       if (axis < 0) axis += rank;
       if (rank != 4 || axis != 3) continue;
+      // softmax input: add(div(.), mask), or the div itself (no mask)
       const Node* C = node_of(P->ins[0]);
-      if (!is_op(C, "gawee.add") || uses_[P->ins[0]] != 1) continue;
-      int bi = -1, mask = -1;
-      for (int side = 0; side < 2; ++side) {
-        const Node* Bn = node_of(C->ins[side]);
-        if (is_op(Bn, "gawee.div") && uses_[C->ins[side]] == 1) {
-          bi = side;
-          mask = C->ins[1 - side];
-          break;
+      if (uses_[P->ins[0]] != 1) continue;
+      const Node* Bn = nullptr;
+      int mask = -1;
+      if (is_op(C, "gawee.div")) {
+        Bn = C;
+      } else if (is_op(C, "gawee.add")) {
+        for (int side = 0; side < 2; ++side) {
+          const Node* D = node_of(C->ins[side]);
+          if (is_op(D, "gawee.div") && uses_[C->ins[side]] == 1) {
+            Bn = D;
+            mask = C->ins[1 - side];
+            break;
+          }
         }
       }
-      if (bi < 0) continue;
-      const Node* Bn = node_of(C->ins[bi]);
+      if (!Bn) continue;
       double c = 0;
       int64_t ci = 0;
       if (!scalar_const(Bn->ins[1], c, ci) || val(Bn->ins[1]).type.dtype != DType::F32 || !(c > 0)) continue;
@@ -254,21 +259,24 @@ class Planner {
       const auto& qs = val(A->ins[0]).type.shape;   // [B, H, S, D]
       const auto& kts = val(A->ins[1]).type.shape;  // [B, H, D, Skv]
       const auto& vs = val(E.ins[1]).type.shape;    // [B, H, Skv, D]
-      const Value& ms = val(mask);
       if (qs.size() != 4 || kts.size() != 4 || vs.size() != 4) continue;
       if (kts[0] != qs[0] || kts[1] != qs[1] || kts[2] != qs[3] || vs[0] != qs[0] || vs[1] != qs[1] ||
           vs[2] != kts[3] || vs[3] != qs[3])
         continue;
       if (val(A->ins[0]).type.dtype != DType::F32 || val(A->ins[1]).type.dtype != DType::F32 ||
-          val(E.ins[1]).type.dtype != DType::F32 || ms.type.dtype != DType::F32 || ms.type.rank() > 4)
+          val(E.ins[1]).type.dtype != DType::F32)
         continue;
-      const std::vector<int64_t> sshape = {qs[0], qs[1], qs[2], kts[3]};
-      bool bcast_ok = true;  // the mask broadcasts to the score shape
-      for (int d = 0; d < ms.type.rank(); ++d) {
-        const int64_t md = ms.type.shape[ms.type.rank() - 1 - d], sd = sshape[3 - d];
-        if (md != 1 && md != sd) bcast_ok = false;
+      if (mask >= 0) {
+        const Value& ms = val(mask);
+        if (ms.type.dtype != DType::F32 || ms.type.rank() > 4) continue;
+        const std::vector<int64_t> sshape = {qs[0], qs[1], qs[2], kts[3]};
+        bool bcast_ok = true;  // the mask broadcasts to the score shape
+        for (int d = 0; d < ms.type.rank(); ++d) {
+          const int64_t md = ms.type.shape[ms.type.rank() - 1 - d], sd = sshape[3 - d];
+          if (md != 1 && md != sd) bcast_ok = false;
+        }
+        if (!bcast_ok) continue;
       }
-      if (!bcast_ok) continue;
       if (!kern::attn_supported(qs[3], kts[3], qs[1], qs[1])) continue;
       AttnMatch m;
       m.q = A->ins[0];
@@ -277,7 +285,8 @@ class Planner {
       m.mask = mask;
       m.c = c;
       m.pv_out = E.outs[0];
-      std::vector<int> skip = {def_node(E.ins[0]), def_node(P->ins[0]), def_node(C->ins[bi]), def_node(Bn->ins[0])};
+      std::vector<int> skip = {def_node(E.ins[0]), def_node(P->ins[0]), def_node(Bn->ins[0])};
+      if (Bn != C) skip.push_back(def_node(C->ins[C->ins[0] == mask ? 1 : 0]));  // the div under the add
       // K: the transpose of a GQA expansion, if any
       const Node* Tk = node_of(m.kt);
       if (is_op(Tk, "gawee.transpose") && uses_[m.kt] == 1 && Tk->attr("perm").ints == std::vector<int64_t>{0, 1, 3, 2}) {
@@ -600,8 +609,8 @@ class Planner {
     a.v = v;
     a.B = B; a.H = H; a.Hkv = k.shape[1]; a.S = S; a.Skv = Skv; a.D = D;
     a.c = m.c;
-    a.has_mask = true;
-    a.mask = broadcast_to(value_view(m.mask), {B, H, S, Skv});
+    a.has_mask = m.mask >= 0;
+    if (a.has_mask) a.mask = broadcast_to(value_view(m.mask), {B, H, S, Skv});
     a.flops = 4.0 * (double)B * (double)H * (double)S * (double)Skv * (double)D;
     View out;
     if (m.out_transpose >= 0) {
@@ -612,7 +621,8 @@ class Planner {
       out = alloc(DType::F32, {B, H, S, D});
     }
     a.out = out;
-    op.reads = {q, k, v, a.mask};
+    op.reads = {q, k, v};
+    if (a.has_mask) op.reads.push_back(a.mask);
     op.writes = {out};
     add_op(std::move(op));
     set_view(m.pv_out, out);

@@ -108,6 +108,7 @@ struct Runtime {
   std::vector<std::array<TMap, 3>> tmaps;  // per op (TC only): B hi, B lo, A (TMA-fed kernel)
   std::vector<int> a_tma;                  // per op (TC only): kern::ATma, A_TMA_NONE = warp gather
   int tma_rk = kern::kRK;                  // TMA kernel: k-blocks per promotion round
+  int passes = 3;                          // tensor-core passes per product (precision mode: 3 fp32, 1 tf32)
   std::vector<int> ksplit;                 // per op (TC only): k splits, 1 = none
   std::vector<uint8_t*> attn_skip;         // per op (ATTN only): skip flags of the mask tiles
   std::vector<std::array<std::array<int8_t, 3>, 3>> attn_cpos;  // per op (ATTN): tensor-map dim order
@@ -232,6 +233,12 @@ void Runtime::build_tensor_maps() {
   // Longer rounds accumulate more truncating tensor-memory additions: at 4 the
   // ResNet-18 logits left the reference tolerance (1.47x of it, 0.80x at 2).
   if (const char* e = std::getenv("GAWEE_TMA_ROUND_KB")) tma_rk = std::min(16, std::max(1, std::atoi(e)));
+  if (const char* e = std::getenv("GAWEE_PRECISION")) {
+    const std::string m(e);
+    if (m == "tf32") passes = 1;
+    else if (m == "fp32" || m.empty()) passes = 3;
+    else throw StatusError(GAWEE_ERR_INVALID, "GAWEE_PRECISION must be fp32 or tf32, not " + m);
+  }
   size_t ws_floats = 0;
   attn_skip.assign(P.ops.size(), nullptr);
   attn_cpos.assign(P.ops.size(), {});
@@ -523,6 +530,7 @@ static void launch_tc(Runtime& rt, int o, const Op& op, cudaStream_t s) {
     if (p.fast != kern::FAST_NONE) p.epi = kern::EPI_FAST;
   }
   p.status = rt.status();
+  p.passes = rt.passes;
   if (rt.ksplit[o] > 1 && p.epi <= kern::EPI_BIAS_ADD_RELU) {
     p.ksplit = rt.ksplit[o];
     p.ws = rt.splitk_ws;
@@ -565,6 +573,7 @@ static void launch_attn(Runtime& rt, int o, const Op& op, cudaStream_t s) {
   for (int w = 0; w < 3; ++w)
     for (int i = 0; i < 3; ++i) p.cpos[w][i] = rt.attn_cpos[o][w][i];
   p.status = rt.status();
+  p.passes = rt.passes;
   if (!kern::launch_attention(p, rt.tmaps[o][0].b, rt.tmaps[o][1].b, rt.tmaps[o][2].b, rt.attn_skip[o], s))
     throw StatusError(GAWEE_ERR_UNSUPPORTED, "attention launch rejected the shape of op " + op.name);
 }
@@ -1102,6 +1111,25 @@ gawee_status gawee_set_graph_mode(gawee_ctx* ctx, int enabled) {
   if (!ctx) return GAWEE_ERR_INVALID;
   ctx->rt.graph_mode = enabled != 0;
   return GAWEE_OK;
+}
+
+gawee_status gawee_set_precision(gawee_ctx* ctx, int mode) {
+  if (!ctx || (mode != GAWEE_PRECISION_FP32 && mode != GAWEE_PRECISION_TF32)) return GAWEE_ERR_INVALID;
+  const int passes = mode == GAWEE_PRECISION_TF32 ? 1 : 3;
+  if (passes == ctx->rt.passes) return GAWEE_OK;
+  cudaSetDevice(ctx->rt.device);
+  // the captured graph holds the old kernel parameters: capture again
+  if (ctx->rt.gexec) cudaGraphExecDestroy(ctx->rt.gexec);
+  if (ctx->rt.graph) cudaGraphDestroy(ctx->rt.graph);
+  ctx->rt.gexec = nullptr;
+  ctx->rt.graph = nullptr;
+  ctx->rt.passes = passes;
+  return GAWEE_OK;
+}
+
+int gawee_precision(const gawee_ctx* ctx) {
+  if (!ctx) return -1;
+  return ctx->rt.passes == 1 ? GAWEE_PRECISION_TF32 : GAWEE_PRECISION_FP32;
 }
 
 int gawee_num_kernels(const gawee_ctx* ctx) { return ctx ? (int)ctx->rt.plan->main.size() : -1; }

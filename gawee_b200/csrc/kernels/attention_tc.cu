@@ -394,6 +394,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else if (warp == 9) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
+      const bool three = p.passes != 1;
       const uint32_t id_s = idesc_tf32(kKeys);  // S: N = 128 keys
       const uint32_t id_o = idesc_tf32(DV);     // O: N = head dim
       const uint32_t aq = smem_u32(smem + kOffQ);
@@ -413,8 +414,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const uint64_t o = (uint64_t)(2 * (kk & 3));
           const uint64_t dv = umma_desc_sw128(vt + blk) + o, dvl = umma_desc_sw128(vtl + blk) + o;
           umma_tf32_ts(dpv, praw + 8 * kk, dv, id_o, kk != 0);
-          umma_tf32_ts(dpv, praw + 8 * kk, dvl, id_o, 1);
-          umma_tf32_ts(dpv, plo + 8 * kk, dv, id_o, 1);
+          if (three) {
+            umma_tf32_ts(dpv, praw + 8 * kk, dvl, id_o, 1);
+            umma_tf32_ts(dpv, plo + 8 * kk, dv, id_o, 1);
+          }
         }
         umma_commit(bar(BAR_PV_F));
         umma_commit(bar(sb ? BAR_SE1 : BAR_SE0));
@@ -439,8 +442,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t o = (uint64_t)(2 * kk);
             umma_ss(ds, dq + o, dk + o, id_s, (hd | kk) != 0);
-            umma_ss(ds, dq + o, dkl + o, id_s, 1);
-            umma_tf32_ts(ds, qlo + 8 * kk, dk + o, id_s, 1);
+            if (three) {  // the single-pass mode keeps the lo operands' data flow and skips their products
+              umma_ss(ds, dq + o, dkl + o, id_s, 1);
+              umma_tf32_ts(ds, qlo + 8 * kk, dk + o, id_s, 1);
+            }
           }
         }
         umma_commit(bar(kb ? BAR_SF1 : BAR_SF0));
@@ -635,7 +640,9 @@ bool attn_supported(int64_t D, int64_t Skv, int64_t H, int64_t Hkv) {
 bool launch_attention(const AttnParams& p, const void* tq, const void* tk, const void* tv, uint8_t* skip_flags,
                       cudaStream_t s) {
   if (!attn_supported(p.D, p.Skv, p.H, p.Hkv) || p.B <= 0 || p.S <= 0) return false;
+  if (p.passes != 0 && p.passes != 1 && p.passes != 3) return false;
   AttnParams q = p;
+  if (q.passes == 0) q.passes = 3;
   q.skip = nullptr;
   if (p.mask && skip_flags) {
     const int blocks = p.mb * p.mh * p.QT * p.KT;

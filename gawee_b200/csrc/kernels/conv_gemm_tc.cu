@@ -119,6 +119,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
+  const bool three = p.passes != 1;  // fp32 from three TF32 products (else one)
   const int num_kb = (int)((p.K + kBK - 1) / kBK);
   const int num_rounds = (num_kb + kRK - 1) / kRK;
   auto round_kbs = [&](int r) { return min(kRK, num_kb - r * kRK); };
@@ -340,15 +341,20 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           }
           const uint32_t acol = tmem_rows + (uint32_t)(L::kACol + sa * L::kAStageCols + j * 2 * kBK);
           tmem_st32(acol, x);
-          uint32_t y[32];
+          if (three) {
+            uint32_t y[32];
 #pragma unroll
-          for (int q = 0; q < 32; ++q) {
-            const float v = __uint_as_float(x[q]);
-            y[q] = __float_as_uint(__fsub_rn(v, tf32_hi(v)));
+            for (int q = 0; q < 32; ++q) {
+              const float v = __uint_as_float(x[q]);
+              y[q] = __float_as_uint(__fsub_rn(v, tf32_hi(v)));
+            }
+            __syncwarp();  // every lane has read its row: the slot may be refilled
+            issue();
+            tmem_st32(acol + kBK, y);
+          } else {
+            __syncwarp();
+            issue();
           }
-          __syncwarp();  // every lane has read its row: the slot may be refilled
-          issue();
-          tmem_st32(acol + kBK, y);
         }
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         tc_fence_before();
@@ -387,13 +393,13 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             break;
           }
           const uint32_t bar = smem_u32(&ready[sb]);
-          mbar_arrive_tx(bar, (uint32_t)(nk * 2 * L::kBTile));
+          mbar_arrive_tx(bar, (uint32_t)(nk * (three ? 2 : 1) * L::kBTile));
           for (int j = 0; j < nk; ++j) {
             uint8_t* b_hi = smem + sb * L::kBStage + j * 2 * L::kBTile;
             uint8_t* b_lo = b_hi + L::kBTile;
             const int kb = r * kRK + j;
             tma_load_3d(smem_u32(b_hi), &tm_hi, bar, kb * kBK, n0, b_plane);
-            tma_load_3d(smem_u32(b_lo), &tm_lo, bar, kb * kBK, n0, b_plane);
+            if (three) tma_load_3d(smem_u32(b_lo), &tm_lo, bar, kb * kBK, n0, b_plane);
           }
           ++g;
           if (++sb == kS) {
@@ -452,7 +458,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             for (int kk = 0; kk < kBK / 8; ++kk) {
               const uint64_t o = (uint64_t)(2 * kk);
               const uint32_t ka = (uint32_t)(8 * kk);
-              if (L::kFold) {
+              if (!three) {
+                umma_tf32_ts(tmem_d, a_raw + ka, dbh + o, idesc, (j | kk) != 0);  // single pass: hi*hi
+              } else if (L::kFold) {
                 // The B stage holds the hi plane's BN rows directly followed by
                 // the lo plane's, so one N = 2*BN MMA gives [hi*hi | hi*lo];
                 // lo*hi (N = BN) accumulates into the first half.  An M = 128
@@ -515,7 +523,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         for (int c0 = 0; c0 < HB; c0 += 32) {
           uint32_t r[32];
           tmem_ld32(lane_base + (uint32_t)(buf * L::kAccCols + cbase + c0), r);
-          if (L::kFold) {  // the round's sum is split over the two halves
+          if (L::kFold && three) {  // the round's sum is split over the two halves
             uint32_t r2[32];
             tmem_ld32(lane_base + (uint32_t)(buf * L::kAccCols + BN + cbase + c0), r2);
 #pragma unroll
@@ -710,6 +718,8 @@ bool launch_conv_gemm_tc(const ConvGemmParams& p_in, const void* tmap_hi, const 
                          cudaStream_t s) {
   ConvGemmParams p = p_in;
   if (p.M <= 0 || p.N <= 0 || p.nb <= 0) return true;
+  if (p.passes == 0) p.passes = 3;
+  if (p.passes != 1 && p.passes != 3) return false;
   if (p.ksplit > 1) {
     const int rounds = (int)(((p.K + kBK - 1) / kBK + kRK - 1) / kRK);
     if (!p.ws || p.nb != 1 || p.epi > EPI_BIAS_ADD_RELU || p.ksplit > rounds) return false;

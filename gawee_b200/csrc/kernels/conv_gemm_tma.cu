@@ -124,6 +124,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
+  const bool three = p.passes != 1;  // fp32 from three TF32 products (else one)
   const int num_kb = (int)((p.K + kBK - 1) / kBK);
   const int rk = p.rk;  // k-blocks per promotion round (the launcher fills it)
   const int num_rounds = (num_kb + rk - 1) / rk;
@@ -221,13 +222,15 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           }
           const uint32_t acol = tmem_rows + (uint32_t)(L::kACol + st * 2 * kBK);
           tmem_st32(acol, x);
-          uint32_t y[32];
+          if (three) {
+            uint32_t y[32];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float v = __uint_as_float(x[e]);
-            y[e] = __float_as_uint(__fsub_rn(v, tf32_hi(v)));
+            for (int e = 0; e < 32; ++e) {
+              const float v = __uint_as_float(x[e]);
+              y[e] = __float_as_uint(__fsub_rn(v, tf32_hi(v)));
+            }
+            tmem_st32(acol + kBK, y);
           }
-          tmem_st32(acol + kBK, y);
           asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
           // A round's first stage also certifies that the accumulator buffer
           // the round overwrites has been drained, so the MMA issuer never
@@ -274,7 +277,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
               break;
             }
             const uint32_t bar = smem_u32(&full[st]);
-            mbar_arrive_tx(bar, (uint32_t)L::kStage);
+            mbar_arrive_tx(bar, three ? (uint32_t)L::kStage : (uint32_t)(L::kATile + L::kBTile));
             const uint32_t sa = smem_u32(smem + st * L::kStage);
             const int k0 = (r * rk + j) * kBK;
             if (p.a_tma == A_TMA_IM2COL) {
@@ -296,7 +299,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
               tma_load_2d(sa, &tm_a, bar, k0, (int)m0);
             }
             tma_load_3d(sa + L::kATile, &tm_hi, bar, k0, n0, 0);
-            tma_load_3d(sa + L::kATile + L::kBTile, &tm_lo, bar, k0, n0, 0);
+            if (three) tma_load_3d(sa + L::kATile + L::kBTile, &tm_lo, bar, k0, n0, 0);
           }
         }
       }
@@ -347,7 +350,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
               const uint64_t o = (uint64_t)(2 * kk);
               const uint32_t ka = (uint32_t)(8 * kk);
               const uint32_t first = (j | kk) != 0;
-              if (L::kFold) {
+              if (!three) {
+                umma_tf32_ts(tmem_d, a_raw + ka, dbh + o, idesc, first);  // single pass: hi*hi
+              } else if (L::kFold) {
                 umma_tf32_ts(tmem_d, a_raw + ka, dbh + o, idesc2, first);  // [hi*hi | hi*lo]
                 umma_tf32_ts(tmem_d, a_rem + ka, dbh + o, idesc, 1);       // lo*hi
               } else {
@@ -394,7 +399,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         for (int c0 = 0; c0 < HB; c0 += 32) {
           uint32_t v[32];
           tmem_ld32(lane_base + (uint32_t)(buf * L::kAccCols + cbase + c0), v);
-          if (L::kFold) {  // the round's sum is split over the two halves
+          if (L::kFold && three) {  // the round's sum is split over the two halves
             uint32_t v2[32];
             tmem_ld32(lane_base + (uint32_t)(buf * L::kAccCols + BN + cbase + c0), v2);
 #pragma unroll
@@ -555,6 +560,8 @@ bool launch_conv_gemm_tma(const ConvGemmParams& p_in, const void* tmap_a, const 
   if (p.M <= 0 || p.N <= 0) return true;
   if (p.rk <= 0) p.rk = kRK;
   if (p.rk > 16) return false;
+  if (p.passes == 0) p.passes = 3;
+  if (p.passes != 1 && p.passes != 3) return false;
   if (p.K <= 0 || p.nb != 1 || (p.a_tma != A_TMA_2D && p.a_tma != A_TMA_IM2COL && p.a_tma != A_TMA_IM2COL_TAPS))
     return false;
   if (p.a_tma == A_TMA_IM2COL && p.C % kBK != 0) return false;

@@ -321,6 +321,10 @@ struct ConvGemmParams {
   int a_tma;
   // launch_conv_gemm_tma only: k-blocks per promotion round (0 = kRK).
   int rk;
+  // Tensor-core passes per product: 3 (fp32 from three TF32 products,
+  // hi*hi + hi*lo + lo*hi; the default, also for 0) or 1 (one TF32 product
+  // of the truncated operands: the single-pass TF32 precision mode).
+  int passes;
 };
 
 enum ATma : int {
@@ -360,6 +364,7 @@ struct AttnParams {
   int64_t o_st[4];            // output strides over (b, h, i, d)
   int* status;
   int8_t cpos[3][3];          // per operand (q, k, v): map dim of (seq, head, batch), from make_attn_tensor_map
+  int passes;                 // 3 (default, also 0): fp32 from three TF32 products; 1: single TF32 pass
 };
 
 bool attn_supported(int64_t D, int64_t Skv, int64_t H, int64_t Hkv);

@@ -63,6 +63,8 @@ def load_library(path: str = LIB_PATH):
             "gawee_output_device_ptr": (c.c_int, [P, c.c_int, c.POINTER(P)]),
             "gawee_synchronize": (c.c_int, [P, P]),
             "gawee_set_graph_mode": (c.c_int, [P, c.c_int]),
+            "gawee_set_precision": (c.c_int, [P, c.c_int]),
+            "gawee_precision": (c.c_int, [P]),
             "gawee_plan_text": (c.c_int, [c.c_char_p, c.c_char_p, c.c_char_p, c.c_size_t]),
             "gawee_num_kernels": (c.c_int, [P]),
             "gawee_num_launches": (c.c_int, [P]),
@@ -107,7 +109,10 @@ def _stream_ptr(stream) -> Optional[int]:
 class Model:
     """A gawee `forward` function compiled for one B200."""
 
-    def __init__(self, mlir: str, device: int = 0, entry: str = "forward", graph_mode: bool = True):
+    PRECISIONS = {"fp32": 0, "tf32": 1}
+
+    def __init__(self, mlir: str, device: int = 0, entry: str = "forward", graph_mode: bool = True,
+                 precision: Optional[str] = None):
         self._lib = load_library()
         h = ctypes.c_void_p()
         st = self._lib.gawee_create(mlir.encode(), entry.encode(), device, ctypes.byref(h))
@@ -118,6 +123,8 @@ class Model:
         self._h = h
         self.device = device
         self._lib.gawee_set_graph_mode(h, 1 if graph_mode else 0)
+        if precision is not None:
+            self.set_precision(precision)
         self.arg_specs = [self._info(self._lib.gawee_arg_info, i) for i in range(self._lib.gawee_num_args(h))]
         self.output_specs = [self._info(self._lib.gawee_output_info, i)
                              for i in range(self._lib.gawee_num_outputs(h))]
@@ -126,6 +133,18 @@ class Model:
     def from_file(cls, path: str, **kw) -> "Model":
         with open(path) as f:
             return cls(f.read(), **kw)
+
+    def set_precision(self, precision: str):
+        """Tensor-core arithmetic: "fp32" (three TF32 passes, the default and the
+        parity mode) or "tf32" (one pass; see gawee_set_precision in
+        include/gawee_cuda.h for its error bound)."""
+        if precision not in self.PRECISIONS:
+            raise ValueError(f"precision must be one of {sorted(self.PRECISIONS)}, not {precision!r}")
+        self._check(self._lib.gawee_set_precision(self._h, self.PRECISIONS[precision]))
+
+    @property
+    def precision(self) -> str:
+        return {v: k for k, v in self.PRECISIONS.items()}[self._lib.gawee_precision(self._h)]
 
     def close(self):
         h = getattr(self, "_h", None)

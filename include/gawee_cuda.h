@@ -108,6 +108,23 @@ gawee_status gawee_synchronize(gawee_ctx* ctx, void* stream);
  * (enabled = 1, the default) or launch kernels one by one (0). */
 gawee_status gawee_set_graph_mode(gawee_ctx* ctx, int enabled);
 
+/* Arithmetic of the tensor-core contractions (convolutions, GEMMs, fused
+ * attention).  The reference computes in fp32 on the CPU; there is no
+ * reference counterpart to this call.
+ *   GAWEE_PRECISION_FP32 (default): each product from three TF32 products of
+ *     the operands' high parts and remainders (hi*hi + hi*lo + lo*hi), fp32
+ *     accumulation with round-to-nearest promotion every 64 k: parity with
+ *     the fp32 reference at its own tolerances.
+ *   GAWEE_PRECISION_TF32: one TF32 product of the truncated operands (10
+ *     explicit mantissa bits each), same accumulation: |error| <= 2^-9 *
+ *     sum |a_k * b_k| per output plus the accumulation term; not a parity mode.
+ * GAWEE_PRECISION=tf32 in the environment selects TF32 at gawee_create.
+ * Changing the mode drops the captured CUDA graph (it is captured again on
+ * the next forward); call it between forwards, with no forward in flight. */
+enum { GAWEE_PRECISION_FP32 = 0, GAWEE_PRECISION_TF32 = 1 };
+gawee_status gawee_set_precision(gawee_ctx* ctx, int mode);
+int gawee_precision(const gawee_ctx* ctx); /* the current mode, -1 for NULL */
+
 /* Kernel i of the per-forward sequence: name (fused ops joined by '+'),
  * whether it is a tensor-core contraction, and its algorithmic FLOPs
  * (2*M*N*K with the unpadded K; 0 for other kernels). */

@@ -5,7 +5,7 @@ matmul(., V) (GaweeToLinalg.cpp:959-1112, 1377-1441, 1885-1900), with the GQA
 head expansion unsqueeze -> expand -> reshape of K and V, into one tcgen05
 kernel with an online softmax.  Cases: sequence tails (S not a multiple of
 128), head dims 32 / 48 / 64, GQA, causal -inf masks (whole key tiles
-skipped), a padding mask broadcast over rows, a power-of-two and a
+skipped), a padding mask broadcast over rows, no mask at all, a power-of-two and a
 non-power-of-two divisor, and an output consumed in [B, S, H, D] order.
 """
 import math
@@ -29,7 +29,9 @@ def _graph(B, H, Hkv, S, D, mask_kind, c, transpose_out):
             rep = H // Hkv
             k = g.reshape(g.expand(g.unsqueeze(k, [2]), (B, Hkv, rep, S, D)), (B, H, S, D))
             v = g.reshape(g.expand(g.unsqueeze(v, [2]), (B, Hkv, rep, S, D)), (B, H, S, D))
-        if mask_kind == "causal":
+        if mask_kind == "none":
+            mask = None
+        elif mask_kind == "causal":
             r = g.range_(0, S, 1)
             allowed = g.less_equal(g.unsqueeze(r, [0]), g.unsqueeze(r, [1]))
             mask = g.where(allowed, g.const(0.0, F), g.const(float("-inf"), F))
@@ -38,7 +40,9 @@ def _graph(B, H, Hkv, S, D, mask_kind, c, transpose_out):
             m[-1, 0, 0, S - S // 3:] = -np.inf
             m[0, 0, 0, 1] = -10000.0
             mask = g.const(m, F, (B, 1, 1, S))
-        s = g.add(g.div(g.matmul(q, g.transpose(k, [0, 1, 3, 2])), g.const(c, F)), mask)
+        s = g.div(g.matmul(q, g.transpose(k, [0, 1, 3, 2])), g.const(c, F))
+        if mask is not None:
+            s = g.add(s, mask)
         o = g.matmul(g.softmax(s, -1), v)
         if transpose_out:
             o = g.reshape(g.transpose(o, [0, 2, 1, 3]), (B, S, H * D))
@@ -53,6 +57,7 @@ CASES = [
     (2, 2, 2, 130, 48, "causal", math.sqrt(48), False),  # head dim 48, non-power-of-two divisor
     (2, 2, 1, 96, 32, "padding", math.sqrt(32), True),   # padding mask, GQA 2:1
     (1, 2, 2, 256, 64, "padding", 8.0, False),
+    (2, 4, 2, 160, 64, "none", 8.0, False),             # no mask: softmax straight over the scaled scores
 ]
 
 

@@ -110,6 +110,18 @@ def test_plan_all_configs(name):
         assert int(kv["prologue"]) >= 6  # RoPE tables and causal mask computed once
 
 
+def test_plan_fuses_attention_without_a_mask():
+    # matmul(Q, K^T) -> div(c) -> softmax -> matmul(., V): the add(mask) step is optional
+    from tests.helpers import build, rand_input
+
+    def g_(g):
+        q, k, v = (rand_input(g, (2, 4, 160, 64), i) for i in (1, 2, 3))
+        s = g.div(g.matmul(q, g.transpose(k, [0, 1, 3, 2])), g.const(8.0, "f32"))
+        return [g.matmul(g.softmax(s, -1), v)]
+    s = _plan(build(g_)[0])
+    assert s.count("attention") == 1 and "softmax" not in s and "matmul" not in s
+
+
 def test_plan_memory_reuse():
     g = synth.resnet18(256)
     s = _plan(g.mlir)

@@ -215,7 +215,27 @@ def run_reference(a):
     return 0
 
 
-def tc_roofline(m, sp, peaks):
+# DRAM bytes (read + write) of the tensor-core kernels per batch row, from one
+# ncu capture (dram__bytes_read.sum + dram__bytes_write.sum over one forward):
+# workload -> (bytes per row, batch captured, summary).  Scaled to the bench's
+# batch, where traffic grows with the rows (batches at least as large as the
+# captured one; smaller batches keep more of their activations in L2).
+TC_DRAM_BYTES = {
+    "resnet18": (968.2e6 / 64, 64, "profiles/resnet18_b64_dram.md"),
+}
+
+
+def tc_traffic(workload, rows):
+    if workload not in TC_DRAM_BYTES:
+        return None, None
+    per_row, cap_rows, src = TC_DRAM_BYTES[workload]
+    if rows < cap_rows:
+        return None, None
+    return per_row * rows, (f"{src}: ncu DRAM bytes of the tensor-core kernels of one batch-{cap_rows} forward, "
+                            f"x {rows}/{cap_rows}")
+
+
+def tc_roofline(m, sp, peaks, workload=None, rows=0):
     """Tensor-core kernels of one eagerly profiled forward: algorithmic FLOPs
     over their CUDA-event device time, against the measured peaks."""
     kern = m.kernels()
@@ -225,22 +245,35 @@ def tc_roofline(m, sp, peaks):
     fwd_ms = sum(prof)
     achieved = tc_flops / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else 0.0
     peak = peaks["bf16"]
+    tf32, tf32_src = tf32_mma_rate(m.device)
+    traffic, traffic_src = tc_traffic(workload, rows)
     r = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-         "frac": achieved / peak if peak else None, "traffic": None,
+         "frac": achieved / peak if peak else None, "traffic": traffic, "traffic_source": traffic_src,
          "peak_source": f"{peaks['source']} bf16 dense (cuBLAS burst); fp32 here is 3 TF32 passes",
-         "fp32_3xtf32_ceiling": TF32_MMA_TFLOPS / 3.0,
-         "frac_of_fp32_3xtf32_ceiling": achieved / (TF32_MMA_TFLOPS / 3.0),
-         "kernel": "conv_gemm_tc_kernel (tcgen05 kind::tf32, 3 passes)",
+         "tf32_mma_tflops": tf32, "tf32_mma_source": tf32_src,
+         "fp32_3xtf32_ceiling": tf32 / 3.0,
+         "frac_of_fp32_3xtf32_ceiling": achieved / (tf32 / 3.0),
+         "kernel": "conv_gemm_tma_kernel + conv_gemm_tc_kernel (tcgen05 kind::tf32, 3 passes)",
          "tc_share_of_forward": tc_ms / fwd_ms if fwd_ms else None,
          "tc_ms_per_forward": tc_ms, "tc_flops_per_forward": tc_flops, "forward_ms_eager": fwd_ms}
     return r, kern, prof
 
 
-# Raw tcgen05.mma kind::tf32 rate on this B200 (M = 128, N = 128, both
-# operands in shared memory, back to back: 64 cycles per MMA at 1965 MHz over
-# 148 SMs), measured with a standalone microbenchmark.  The fp32 path issues
-# three TF32 MMAs per product, so its tensor ceiling is a third of this.
-TF32_MMA_TFLOPS = 1114.0
+# Raw tcgen05.mma kind::tf32 rate: measured at run time by gawee_probe_tf32_mma
+# (back-to-back M = 128, N = 128, K = 8 MMAs on every SM).  The fallback is the
+# same shape's cost measured on this pool's B200s, 64 cycles per MMA: 4096
+# FLOP per cycle per SM, 148 SMs at 1965 MHz.  The fp32 path issues three
+# TF32 MMAs per product, so its tensor ceiling is a third of the rate.
+TF32_MMA_TFLOPS_FALLBACK = 4096 * 148 * 1.965e9 / 1e12
+
+
+def tf32_mma_rate(device):
+    import ctypes
+    from gawee_b200.runtime import load_library
+    out = ctypes.c_double(0.0)
+    if load_library().gawee_probe_tf32_mma(device, ctypes.byref(out)) == 0 and out.value > 0:
+        return out.value, "measured now (gawee_probe_tf32_mma)"
+    return TF32_MMA_TFLOPS_FALLBACK, "64 cycles per 128x128x8 MMA at 1965 MHz (earlier measurement)"
 
 
 def l2_flush_buffer(dev):
@@ -540,7 +573,7 @@ def main():
     e2e_value = global_batch * items * a.steps / (ms_e2e / 1e3)
 
     peaks = load_peaks()
-    roofline, kern, prof = tc_roofline(m, sp, peaks)
+    roofline, kern, prof = tc_roofline(m, sp, peaks, a.workload, s1 - s0)
     n_kern = m.num_launches()
     m.synchronize(sp)
 

@@ -27,6 +27,7 @@ SOURCES = [
     "kernels/conv_gemm_tma.cu",
     "kernels/attention_tc.cu",
     "kernels/noalloc_gemm.cu",
+    "kernels/tc_probe.cu",
     "host/ir.cpp",
     "host/plan.cpp",
     "host/runtime.cpp",

@@ -341,20 +341,15 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           }
           const uint32_t acol = tmem_rows + (uint32_t)(L::kACol + sa * L::kAStageCols + j * 2 * kBK);
           tmem_st32(acol, x);
-          if (three) {
-            uint32_t y[32];
+          uint32_t y[32];  // remainders (formed in both modes; stored for three passes)
 #pragma unroll
-            for (int q = 0; q < 32; ++q) {
-              const float v = __uint_as_float(x[q]);
-              y[q] = __float_as_uint(__fsub_rn(v, tf32_hi(v)));
-            }
-            __syncwarp();  // every lane has read its row: the slot may be refilled
-            issue();
-            tmem_st32(acol + kBK, y);
-          } else {
-            __syncwarp();
-            issue();
+          for (int q = 0; q < 32; ++q) {
+            const float v = __uint_as_float(x[q]);
+            y[q] = __float_as_uint(__fsub_rn(v, tf32_hi(v)));
           }
+          __syncwarp();  // every lane has read its row: the slot may be refilled
+          issue();
+          if (three) tmem_st32(acol + kBK, y);
         }
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         tc_fence_before();

@@ -64,6 +64,7 @@ def load_library(path: str = LIB_PATH):
             "gawee_synchronize": (c.c_int, [P, P]),
             "gawee_set_graph_mode": (c.c_int, [P, c.c_int]),
             "gawee_set_precision": (c.c_int, [P, c.c_int]),
+            "gawee_probe_tf32_mma": (c.c_int, [c.c_int, c.POINTER(c.c_double)]),
             "gawee_precision": (c.c_int, [P]),
             "gawee_plan_text": (c.c_int, [c.c_char_p, c.c_char_p, c.c_char_p, c.c_size_t]),
             "gawee_num_kernels": (c.c_int, [P]),

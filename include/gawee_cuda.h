@@ -204,6 +204,13 @@ gawee_status gawee_embedded_forward(const char* mlir_text, int device, void* res
 gawee_status gawee_matmul_f32_noalloc(const float* a, const float* b, float* c, int64_t m, int64_t n, int64_t k,
                                       void* stream);
 
+/* Diagnostic: the tensor cores' TF32 rate on `device`, measured now (one CTA
+ * per SM issuing back-to-back M = 128, N = 128, K = 8 tcgen05 TF32 MMAs with
+ * both operands in shared memory, timed with CUDA events; about 5 ms).  The
+ * fp32 mode issues three such products per multiply-add, so a third of
+ * *tflops is its tensor ceiling.  No reference counterpart. */
+gawee_status gawee_probe_tf32_mma(int device, double* tflops);
+
 /* ---------------------------------------------------------------------------
  * Data parallelism: batch sharding with replicated weights (one process or
  * thread per GPU).  The only collective is the gather of each rank's output

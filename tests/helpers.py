@@ -55,6 +55,21 @@ def compare(got: np.ndarray, want: np.ndarray, atol: float, rtol: float, what: s
     return 0.0
 
 
+def parity_line(what: str, got: np.ndarray, want: np.ndarray, atol: float, rtol: float) -> str:
+    """One line of the parity table (printed by the model tests under -s):
+    max |got - want|, max |want|, and the worst |got - want| / (atol + rtol |want|),
+    the fraction of the reference tolerance used (below 1 passes)."""
+    g64, w64 = got.astype(np.float64), want.astype(np.float64)
+    ok = np.isfinite(w64)
+    diff = np.abs(g64[ok] - w64[ok])
+    ratio = float(np.max(diff / (atol + rtol * np.abs(w64[ok])))) if diff.size else 0.0
+    line = (f"PARITY {what}: max_abs_diff={float(diff.max()) if diff.size else 0.0:.3e} "
+            f"max_abs_ref={float(np.max(np.abs(w64[ok]))) if diff.size else 0.0:.3e} "
+            f"tolerance_used={ratio:.3f} (atol {atol:g}, rtol {rtol:g})")
+    print(line)
+    return line
+
+
 def parity(mlir: str, args: List[np.ndarray], atol: float = 1e-5, rtol: float = 1e-5, runs: int = 1,
            graph_mode: bool = True):
     """Run the graph on the CUDA backend and on the oracle; assert they agree."""

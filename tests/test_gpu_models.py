@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 
 from gawee_b200 import synth
-from tests.helpers import compare
+from tests.helpers import compare, parity_line
 
 pytestmark = pytest.mark.gpu
 
@@ -23,6 +23,8 @@ def _check(graph, runs=2):
             got = m.run(args)
             for k, (a, b) in enumerate(zip(got, want)):
                 compare(a, b, graph.atol, 1e-4, f"{graph.name} output{k}")
+        for k, (a, b) in enumerate(zip(got, want)):
+            parity_line(f"{graph.name} output{k}", a, b, graph.atol, 1e-4)
     finally:
         m.close()
 
@@ -60,6 +62,7 @@ def test_resnet18_full_batch_rows_match_oracle():
         want = o.run(a1, threads=os.cpu_count() or 1)[0]
         for k, g in enumerate(got):
             compare(g[r:r + 1], want, big.atol, 1e-4, f"resnet18 b256 row {r} run {k}")
+        parity_line(f"resnet18 b256 row {r}", got[-1][r:r + 1], want, big.atol, 1e-4)
 
 
 def test_bert_tiny_s128():
@@ -121,3 +124,4 @@ def test_decoder135m_full_size_sampled_sequences_match_oracle():
         want = o.run(a1, threads=os.cpu_count() or 1)[0]
         for k in range(2):
             compare(got[k][i], want, 5e-4, 1e-4, f"decoder135m b64 sequence {r} run {k}")
+        parity_line(f"decoder135m b64x512 sequence {r}", got[-1][i], want, 5e-4, 1e-4)

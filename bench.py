@@ -29,8 +29,10 @@ One JSON line on rank 0:
               one thread as the reference's generated code runs)
   extra       N=1 only: the metric's other configurations -- the decoder-135M
               prefill (configuration 4, tokens/s) and the batch-1 latencies of
-              ResNet-18, BERT-tiny and Llama-15M (configurations 0-2) -- each
-              with its own e2e, roofline and CPU baseline
+              ResNet-18, BERT-tiny and Llama-15M (configurations 0-2; Llama-15M
+              both as the reference binding's KV-cache decode step and as a
+              256-token prefill) -- each with its own e2e, roofline and CPU
+              baseline
 `--impl reference` times that CPU implementation alone (the reference's own
 MLIR/LLVM toolchain is not available, so its AOT binary cannot be built).
 """
@@ -398,12 +400,16 @@ def run_extra(peaks, local):
     out = {"decoder135m_prefill": decoder_entry(peaks, local, steps=5)}
     cfgs = [("resnet18_b1_latency", synth.resnet18(1), "ResNet-18 fp32 batch-1 latency (1x3x224x224)", 6814.2),
             ("bert_tiny_s128_latency", synth.bert_tiny(), "BERT-tiny fp32 encoder latency (batch 1, seq 128)", 354.0),
+            ("llama15m_decode_step_latency", synth.llama15m_decode(1, 1),
+             "Llama-15M fp32 KV-cache decode step latency (batch 1, 1 new token over a past of 1: the reference "
+             "tinyllama binding's shapes)", 107.6),
             ("llama15m_s256_prefill_latency", synth.llama15m(),
              "Llama-15M fp32 prefill latency (batch 1, seq 256)", None)]
     for name, g, metric, pub in cfgs:
         src = ("middle/delta.md:22-24 (Gawee CPU AOT p50 on an Apple M1-class CPU, 1 thread, process launch "
                "and npy I/O included)" if pub else
-               "none: the reference publishes a tinyllama_15m decode step (107.6 ms), not a 256-token prefill")
+               "none: the reference publishes the tinyllama_15m decode step (see llama15m_decode_step_latency), "
+               "not a 256-token prefill")
         out[name] = latency_entry(name, g, metric, pub, src, peaks, local, steps=30)
     return out
 

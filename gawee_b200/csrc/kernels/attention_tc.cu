@@ -408,15 +408,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tc_fence_after();
         const uint32_t praw = tmem + (sb ? kColS1 : kColS0), plo = tmem + kColPlo, dpv = tmem + kColPV;
         const uint32_t vt = smem_u32(smem + kOffVt), vtl = smem_u32(smem + kOffVtlo);
+        if (three) {
 #pragma unroll 4
-        for (int kk = 0; kk < kKeys / 8; ++kk) {  // 8 keys per step; a V^T k-block holds 32
-          const uint32_t blk = (uint32_t)(kk >> 2) * kVtBlock;
-          const uint64_t o = (uint64_t)(2 * (kk & 3));
-          const uint64_t dv = umma_desc_sw128(vt + blk) + o, dvl = umma_desc_sw128(vtl + blk) + o;
-          umma_tf32_ts(dpv, praw + 8 * kk, dv, id_o, kk != 0);
-          if (three) {
+          for (int kk = 0; kk < kKeys / 8; ++kk) {  // 8 keys per step; a V^T k-block holds 32
+            const uint32_t blk = (uint32_t)(kk >> 2) * kVtBlock;
+            const uint64_t o = (uint64_t)(2 * (kk & 3));
+            const uint64_t dv = umma_desc_sw128(vt + blk) + o, dvl = umma_desc_sw128(vtl + blk) + o;
+            umma_tf32_ts(dpv, praw + 8 * kk, dv, id_o, kk != 0);
             umma_tf32_ts(dpv, praw + 8 * kk, dvl, id_o, 1);
             umma_tf32_ts(dpv, plo + 8 * kk, dv, id_o, 1);
+          }
+        } else {  // single pass: the lo operands' data flow stays, their products are skipped
+#pragma unroll 4
+          for (int kk = 0; kk < kKeys / 8; ++kk) {
+            const uint64_t dv = umma_desc_sw128(vt + (uint32_t)(kk >> 2) * kVtBlock) + (uint64_t)(2 * (kk & 3));
+            umma_tf32_ts(dpv, praw + 8 * kk, dv, id_o, kk != 0);
           }
         }
         umma_commit(bar(BAR_PV_F));
@@ -438,14 +444,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const uint64_t dk = umma_desc_sw128(smem_u32(smem + kOffK + (2 * kb + hd) * kTile));
           const uint64_t dkl = umma_desc_sw128(smem_u32(smem + kOffKlo + hd * kTile));
           const uint32_t qlo = tmem + kColQlo + 32 * hd;
+          if (three) {
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t o = (uint64_t)(2 * kk);
-            umma_ss(ds, dq + o, dk + o, id_s, (hd | kk) != 0);
-            if (three) {  // the single-pass mode keeps the lo operands' data flow and skips their products
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t o = (uint64_t)(2 * kk);
+              umma_ss(ds, dq + o, dk + o, id_s, (hd | kk) != 0);
               umma_ss(ds, dq + o, dkl + o, id_s, 1);
               umma_tf32_ts(ds, qlo + 8 * kk, dk + o, id_s, 1);
             }
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) umma_ss(ds, dq + 2 * kk, dk + 2 * kk, id_s, (hd | kk) != 0);
           }
         }
         umma_commit(bar(kb ? BAR_SF1 : BAR_SF0));

@@ -449,13 +449,17 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             const uint64_t dbl = dbh + kBTileDesc;
             const uint32_t a_raw = tmem_base + (uint32_t)(L::kACol + sl * L::kAStageCols + j * 2 * kBK);
             const uint32_t a_rem = a_raw + kBK;
+            if (!three) {  // single pass: hi*hi (tested once per k-block, outside the issue loop)
+#pragma unroll
+              for (int kk = 0; kk < kBK / 8; ++kk)
+                umma_tf32_ts(tmem_d, a_raw + 8 * kk, dbh + 2 * kk, idesc, (j | kk) != 0);
+              continue;
+            }
 #pragma unroll
             for (int kk = 0; kk < kBK / 8; ++kk) {
               const uint64_t o = (uint64_t)(2 * kk);
               const uint32_t ka = (uint32_t)(8 * kk);
-              if (!three) {
-                umma_tf32_ts(tmem_d, a_raw + ka, dbh + o, idesc, (j | kk) != 0);  // single pass: hi*hi
-              } else if (L::kFold) {
+              if (L::kFold) {
                 // The B stage holds the hi plane's BN rows directly followed by
                 // the lo plane's, so one N = 2*BN MMA gives [hi*hi | hi*lo];
                 // lo*hi (N = BN) accumulates into the first half.  An M = 128

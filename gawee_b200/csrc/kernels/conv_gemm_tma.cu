@@ -104,7 +104,7 @@ __device__ __forceinline__ void tma_load_im2col_4d(uint32_t dst, const CUtensorM
 
 }  // namespace
 
-template <int BN, int NS, int EPI>
+template <int BN, int NS, int EPI, int PASSES>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     conv_gemm_tma_kernel(const __grid_constant__ ConvGemmParams p, const __grid_constant__ CUtensorMap tm_a,
                          const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo) {
@@ -124,7 +124,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
-  const bool three = p.passes != 1;  // fp32 from three TF32 products (else one)
+  // fp32 from three TF32 products, or one (the single-pass TF32 mode): a
+  // template parameter, so the three-pass kernel carries no test of it
+  constexpr bool three = PASSES == 3;
   const int num_kb = (int)((p.K + kBK - 1) / kBK);
   const int rk = p.rk;  // k-blocks per promotion round (the launcher fills it)
   const int num_rounds = (num_kb + rk - 1) / rk;
@@ -345,21 +347,27 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             const uint32_t a_rem = a_raw + kBK;
             // a K-major SW128 descriptor advances 32 bytes (2 units) per
             // 8-wide k-step; an A column holds one k
+            // the pass count is tested once per k-block, outside the issue
+            // loop: the issuing thread is the kernel's critical path
+            if (three) {
 #pragma unroll
-            for (int kk = 0; kk < kBK / 8; ++kk) {
-              const uint64_t o = (uint64_t)(2 * kk);
-              const uint32_t ka = (uint32_t)(8 * kk);
-              const uint32_t first = (j | kk) != 0;
-              if (!three) {
-                umma_tf32_ts(tmem_d, a_raw + ka, dbh + o, idesc, first);  // single pass: hi*hi
-              } else if (L::kFold) {
-                umma_tf32_ts(tmem_d, a_raw + ka, dbh + o, idesc2, first);  // [hi*hi | hi*lo]
-                umma_tf32_ts(tmem_d, a_rem + ka, dbh + o, idesc, 1);       // lo*hi
-              } else {
-                umma_tf32_ts(tmem_d, a_raw + ka, dbh + o, idesc, first);
-                umma_tf32_ts(tmem_d, a_raw + ka, dbl + o, idesc, 1);
-                umma_tf32_ts(tmem_d, a_rem + ka, dbh + o, idesc, 1);
+              for (int kk = 0; kk < kBK / 8; ++kk) {
+                const uint64_t o = (uint64_t)(2 * kk);
+                const uint32_t ka = (uint32_t)(8 * kk);
+                const uint32_t first = (j | kk) != 0;
+                if (L::kFold) {
+                  umma_tf32_ts(tmem_d, a_raw + ka, dbh + o, idesc2, first);  // [hi*hi | hi*lo]
+                  umma_tf32_ts(tmem_d, a_rem + ka, dbh + o, idesc, 1);       // lo*hi
+                } else {
+                  umma_tf32_ts(tmem_d, a_raw + ka, dbh + o, idesc, first);
+                  umma_tf32_ts(tmem_d, a_raw + ka, dbl + o, idesc, 1);
+                  umma_tf32_ts(tmem_d, a_rem + ka, dbh + o, idesc, 1);
+                }
               }
+            } else {
+#pragma unroll
+              for (int kk = 0; kk < kBK / 8; ++kk)  // single pass: hi*hi
+                umma_tf32_ts(tmem_d, a_raw + 8 * kk, dbh + 2 * kk, idesc, (j | kk) != 0);
             }
             umma_commit(smem_u32(&empty[st]));  // the stage may be refilled once these MMAs complete
           }
@@ -464,10 +472,10 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_tiled() {
   return fn;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, int PASSES>
 bool launch_t(const ConvGemmParams& p, const void* tma, const void* tmh, const void* tml, cudaStream_t s) {
   constexpr int NS = TmaConfig<BN>::NS;
-  auto kern = conv_gemm_tma_kernel<BN, NS, EPI>;
+  auto kern = conv_gemm_tma_kernel<BN, NS, EPI, PASSES>;
   constexpr int smem = TmaSmem<BN, NS>::kBytes;
   static_assert(smem <= 232448, "shared memory per CTA");
   static std::mutex mu;
@@ -491,17 +499,22 @@ bool launch_t(const ConvGemmParams& p, const void* tma, const void* tmh, const v
   return true;
 }
 
-template <int BN>
-bool launch_epi(const ConvGemmParams& p, const void* tma, const void* tmh, const void* tml, cudaStream_t s) {
+template <int BN, int PASSES>
+bool launch_epi_p(const ConvGemmParams& p, const void* tma, const void* tmh, const void* tml, cudaStream_t s) {
   switch (p.epi) {
-    case EPI_NONE: return launch_t<BN, EPI_NONE>(p, tma, tmh, tml, s);
-    case EPI_BIAS: return launch_t<BN, EPI_BIAS>(p, tma, tmh, tml, s);
-    case EPI_BIAS_RELU: return launch_t<BN, EPI_BIAS_RELU>(p, tma, tmh, tml, s);
-    case EPI_BIAS_ADD_RELU: return launch_t<BN, EPI_BIAS_ADD_RELU>(p, tma, tmh, tml, s);
-    case EPI_PROGRAM: return launch_t<BN, EPI_PROGRAM>(p, tma, tmh, tml, s);
-    case EPI_FAST: return launch_t<BN, EPI_FAST>(p, tma, tmh, tml, s);
+    case EPI_NONE: return launch_t<BN, EPI_NONE, PASSES>(p, tma, tmh, tml, s);
+    case EPI_BIAS: return launch_t<BN, EPI_BIAS, PASSES>(p, tma, tmh, tml, s);
+    case EPI_BIAS_RELU: return launch_t<BN, EPI_BIAS_RELU, PASSES>(p, tma, tmh, tml, s);
+    case EPI_BIAS_ADD_RELU: return launch_t<BN, EPI_BIAS_ADD_RELU, PASSES>(p, tma, tmh, tml, s);
+    case EPI_PROGRAM: return launch_t<BN, EPI_PROGRAM, PASSES>(p, tma, tmh, tml, s);
+    case EPI_FAST: return launch_t<BN, EPI_FAST, PASSES>(p, tma, tmh, tml, s);
     default: return false;
   }
+}
+
+template <int BN>
+bool launch_epi(const ConvGemmParams& p, const void* tma, const void* tmh, const void* tml, cudaStream_t s) {
+  return p.passes == 1 ? launch_epi_p<BN, 1>(p, tma, tmh, tml, s) : launch_epi_p<BN, 3>(p, tma, tmh, tml, s);
 }
 
 }  // namespace

@@ -575,6 +575,86 @@ def llama(batch: int = 1, seq: int = 256, dim: int = 288, layers: int = 6, heads
                       batch, seq, flops[0])
 
 
+def llama_decode(batch: int = 1, past: int = 1, dim: int = 288, layers: int = 6, heads: int = 6,
+                 kv_heads: Optional[int] = None, ffn: int = 768, vocab: int = 32000, eps: float = 1e-5,
+                 theta: float = 10000.0, seed: int = 42, name: str = "llama15m_decode",
+                 present: bool = True) -> SynthGraph:
+    """One KV-cache decode step, with the inputs of the reference's tinyllama
+    binding (eval_priority_models.py:38-54): input_ids [B, 1],
+    attention_mask [B, past + 1] (1 = attend), position_ids [B, 1], then per
+    layer past key and value [B, kv_heads, past, head_dim].  Each layer
+    appends the new key and value to the past ones (Concat on the sequence
+    axis), rotates the new query and key by position_ids (RoPE), and attends
+    over all past + 1 positions; masked positions get -inf.  Outputs: logits
+    [B, 1, vocab], then (present=True) each layer's present key and value
+    [B, kv_heads, past + 1, head_dim], the next step's past."""
+    kv_heads = kv_heads or heads
+    rep = heads // kv_heads
+    hd = dim // heads
+    total = past + 1
+    g = GraphBuilder(f"synthetic:{name}_b{batch}_p{past}", seed)
+    flops = [0]
+    rng = np.random.default_rng(seed + 1)
+    ids_v = rng.integers(0, vocab, (batch, 1), dtype=np.int64)
+    mask_v = np.ones((batch, total), np.int64)
+    if past >= 2:
+        mask_v[:, 0] = 0  # a padded first position: exercises the mask
+    pos_v = np.full((batch, 1), past, np.int64)
+    ids = g.input("i64", (batch, 1), lambda: ids_v)
+    am = g.input("i64", (batch, total), lambda: mask_v)
+    pid = g.input("i64", (batch, 1), lambda: pos_v)
+    pasts = []
+    for li in range(layers):
+        kv = [np.random.default_rng(seed + 100 + 2 * li + j).standard_normal((batch, kv_heads, past, hd),
+                                                                          dtype=np.float32) for j in (0, 1)]
+        pasts.append((g.input("f32", (batch, kv_heads, past, hd), lambda a=kv[0]: a),
+                      g.input("f32", (batch, kv_heads, past, hd), lambda a=kv[1]: a)))
+    emb = g.normal((vocab, dim), 0.02)
+    h = g.gather(emb, ids)                                                  # [B,1,dim]
+    inv = g.const((1.0 / (theta ** (np.arange(0, hd, 2, dtype=np.float64) / hd))).astype(np.float32).reshape(1, hd // 2), "f32")
+    pos = g.unsqueeze(g.cast(pid, 1, "f32"), [2])                           # [B,1,1]
+    freqs = g.mul(pos, inv)                                                 # [B,1,hd/2]
+    embp = g.cat([freqs, freqs], 2)                                         # [B,1,hd]
+    cos = g.unsqueeze(g.cos(embp), [1])                                     # [B,1,1,hd]
+    sin = g.unsqueeze(g.sin(embp), [1])
+    masked = g.less_equal(am, g.const(0, "i64"))                            # [B,total]
+    mask = g.unsqueeze(g.where(masked, g.const(float("-inf"), "f32"), g.const(0.0, "f32")), [1, 2])  # [B,1,1,total]
+    scale = g.const(math.sqrt(hd), "f32")
+    presents = []
+    for li in range(layers):
+        x = _rms_norm(g, h, eps)
+        q = g.transpose(g.reshape(_dense(g, x, dim, heads * hd, flops, False), (batch, 1, heads, hd)), [0, 2, 1, 3])
+        k = g.transpose(g.reshape(_dense(g, x, dim, kv_heads * hd, flops, False), (batch, 1, kv_heads, hd)), [0, 2, 1, 3])
+        v = g.transpose(g.reshape(_dense(g, x, dim, kv_heads * hd, flops, False), (batch, 1, kv_heads, hd)), [0, 2, 1, 3])
+        q = g.add(g.mul(q, cos), g.mul(_rotate_half(g, q), sin))
+        k = g.add(g.mul(k, cos), g.mul(_rotate_half(g, k), sin))
+        kc = g.cat([pasts[li][0], k], 2)                                    # [B,kv_heads,total,hd]
+        vc = g.cat([pasts[li][1], v], 2)
+        presents += [kc, vc]
+        if rep > 1:
+            kc = g.reshape(g.expand(g.unsqueeze(kc, [2]), (batch, kv_heads, rep, total, hd)), (batch, heads, total, hd))
+            vc = g.reshape(g.expand(g.unsqueeze(vc, [2]), (batch, kv_heads, rep, total, hd)), (batch, heads, total, hd))
+        s = g.add(g.div(g.matmul(q, g.transpose(kc, [0, 1, 3, 2])), scale), mask)
+        flops[0] += 2 * batch * heads * total * hd * 2
+        o = g.reshape(g.transpose(g.matmul(g.softmax(s, -1), vc), [0, 2, 1, 3]), (batch, 1, heads * hd))
+        h = g.add(h, _dense(g, o, heads * hd, dim, flops, False))
+        x = _rms_norm(g, h, eps)
+        gate = _dense(g, x, dim, ffn, flops, False)
+        up = _dense(g, x, dim, ffn, flops, False)
+        h = g.add(h, _dense(g, g.mul(g.mul(gate, g.sigmoid(gate)), up), ffn, dim, flops, False))
+    h = _rms_norm(g, h, eps)
+    flops[0] += 2 * batch * dim * vocab
+    logits = g.matmul(h, g.transpose(emb, [1, 0]))
+    outs = [logits] + (presents if present else [])
+    return SynthGraph(f"{name}_b{batch}_p{past}", g.finish(outs), g.args, [o.shape for o in outs], 5e-4,
+                      batch, 1, flops[0])
+
+
+def llama15m_decode(batch: int = 1, past: int = 1, **kw) -> SynthGraph:
+    """Tinyllama-15M's decode step; past = 1 is the reference binding's static shape."""
+    return llama_decode(batch, past, dim=288, layers=6, heads=6, ffn=768, vocab=32000, name="llama15m_decode", **kw)
+
+
 def llama15m(batch: int = 1, seq: int = 256, **kw) -> SynthGraph:
     return llama(batch, seq, dim=288, layers=6, heads=6, ffn=768, vocab=32000, name="llama15m", **kw)
 

@@ -79,6 +79,23 @@ def test_gqa_decoder_reduced():
     _check(synth.llama(2, 64, dim=576, layers=2, heads=9, kv_heads=3, ffn=1536, vocab=4096, name="decoder135m_l2"))
 
 
+@pytest.mark.parametrize("past", [1, 255])
+def test_llama15m_decode_step(past):
+    """A KV-cache decode step with the reference tinyllama binding's inputs
+    (input_ids [1, 1], attention_mask, position_ids, past key/value per layer;
+    eval_priority_models.py:38-54): logits and every layer's present key and
+    value against the oracle.  past = 1 is the binding's static shape; at 255
+    the first position is masked out."""
+    _check(synth.llama15m_decode(1, past))
+
+
+def test_gqa_decoder_decode_step():
+    """Decode with grouped KV heads (9 query heads over 3 key/value heads) and
+    batch 2: the concatenated cache is read through the head mapping."""
+    _check(synth.llama_decode(2, 63, dim=576, layers=2, heads=9, kv_heads=3, ffn=1536, vocab=4096,
+                              name="decoder135m_l2_decode"))
+
+
 def test_decoder135m_full_size_sampled_sequences_match_oracle():
     """Configuration 4 at its full size: the 135M GQA decoder (30 layers,
     hidden 576, 9 / 3 heads) prefilling batch 64 x 512 tokens.  Sequences

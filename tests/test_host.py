@@ -122,6 +122,16 @@ def test_plan_fuses_attention_without_a_mask():
     assert s.count("attention") == 1 and "softmax" not in s and "matmul" not in s
 
 
+def test_plan_decode_step():
+    # the KV-cache decode step: concat of past and new key/value, one query row,
+    # attention, RoPE and RMSNorm still fused; logits + 12 present tensors out
+    g = synth.llama15m_decode(1, 255)
+    s = _plan(g.mlir)
+    assert s.count("attention") == 6 and "softmax" not in s
+    assert s.count("rope") == 12 and s.count("rms_norm") == 13
+    assert len(g.out_shapes) == 13 and g.out_shapes[1] == (1, 6, 256, 48)
+
+
 def test_plan_memory_reuse():
     g = synth.resnet18(256)
     s = _plan(g.mlir)

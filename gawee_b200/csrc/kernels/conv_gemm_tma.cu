@@ -104,6 +104,11 @@ __device__ __forceinline__ void tma_load_im2col_4d(uint32_t dst, const CUtensorM
 
 }  // namespace
 
+// Poll intervals of the waits off the MMA issuer's path (nanoseconds): the A
+// warps and the TMA warp have thousands of cycles of slack per stage, the
+// accumulator warps a whole round.
+constexpr unsigned kSleepA = 64, kSleepTma = 32, kSleepAcc = 256;
+
 template <int BN, int NS, int EPI, int PASSES>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     conv_gemm_tma_kernel(const __grid_constant__ ConvGemmParams p, const __grid_constant__ CUtensorMap tm_a,
@@ -202,7 +207,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         const int nk = round_kbs(r_lo + (r_rotation(m0, nr) + rr) % nr);
         for (int j = 0; j < nk; ++j, ++g) {
           const uint32_t st = g % NS;
-          if (!mbar_wait(smem_u32(&full[st]), (g / NS) & 1, abort_flag, p.status)) {
+          if (!mbar_wait_relaxed(smem_u32(&full[st]), (g / NS) & 1, abort_flag, p.status, kSleepA)) {
             alive = false;
             break;
           }
@@ -239,7 +244,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           // waits on the accumulator warps itself (every wait it makes is
           // idle tensor time: the tensor core queues only a few MMAs).
           if (j == 0 &&
-              !__all_sync(0xffffffffu, mbar_wait(smem_u32(&acce[ar & 1]), ((ar >> 1) & 1) ^ 1, abort_flag, p.status))) {
+              !__all_sync(0xffffffffu, mbar_wait_relaxed(smem_u32(&acce[ar & 1]), ((ar >> 1) & 1) ^ 1, abort_flag,
+                                                         p.status, kSleepA))) {
             alive = false;
             break;
           }
@@ -274,7 +280,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           const int nk = round_kbs(r);
           for (int j = 0; j < nk; ++j, ++g) {
             const uint32_t st = g % NS;
-            if (!mbar_wait(smem_u32(&empty[st]), ((g / NS) & 1) ^ 1, abort_flag, p.status)) {
+            if (!mbar_wait_relaxed(smem_u32(&empty[st]), ((g / NS) & 1) ^ 1, abort_flag, p.status, kSleepTma)) {
               alive = false;
               break;
             }
@@ -398,7 +404,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       for (int j = 0; j < HB; ++j) acc[j] = 0.0f;
       for (int r = 0; r < nr; ++r, ++ar) {
         const uint32_t buf = ar & 1;
-        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&accf[buf]), (ar >> 1) & 1, abort_flag, p.status))) {
+        if (!__all_sync(0xffffffffu,
+                        mbar_wait_relaxed(smem_u32(&accf[buf]), (ar >> 1) & 1, abort_flag, p.status, kSleepAcc))) {
           ok = false;
           break;
         }

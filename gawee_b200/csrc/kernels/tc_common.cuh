@@ -78,6 +78,25 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 }
 
 
+// The same bounded wait for warps off the critical path: between polls the
+// thread sleeps `sleep_ns`, so a dozen waiting warps do not keep the
+// shared-memory barrier unit busy while the MMA issuer polls its own barrier.
+__device__ __forceinline__ bool mbar_wait_relaxed(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                                  unsigned sleep_ns) {
+  if (mbar_try(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  while (true) {
+    __nanosleep(sleep_ns);
+    if (mbar_try(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_ns() - t0 > kWaitNs) {
+      *abort_flag = 1;
+      if (status) atomicCAS(status, 0, (int)ST_BARRIER_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // 16-byte global -> shared copy that bypasses registers; `bytes` 0 writes zeros.
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");

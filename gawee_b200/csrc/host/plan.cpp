@@ -105,7 +105,7 @@ std::string Plan::summary() const {
   for (auto& op : ops) live += !op.dead;
   o << "ops=" << live << " prologue=" << prologue.size() << " pack=" << pack.size() << " main=" << main.size()
     << " arena_bytes=" << arena_bytes << " persist_bytes=" << persist_bytes << "\n";
-  for (int i : main) o << "  " << ops[i].name << "\n";
+  for (int i : main) o << "  " << ops[i].name << execution_note(ops[i]) << "\n";
   return o.str();
 }
 

@@ -120,12 +120,18 @@ struct Plan {
   std::vector<View> result_view; // per result (dense row-major)
   std::vector<int> prologue, pack, main;  // op indices per phase, in order
   size_t arena_bytes = 0, persist_bytes = 0;
-  std::string summary() const;
+  std::string summary() const;  // one line per main op: its name and execution_note
 };
 
 // Build the plan (throws std::runtime_error with a message on unsupported input).
 // Buffer offsets are assigned: persistent buffers packed one after another,
 // per-forward buffers placed in the arena by live interval over `main`.
 std::unique_ptr<Plan> build_plan(Graph g);
+
+// " [interp]" when the op's scalar program runs on the device interpreter
+// (dynamically indexed registers: the slow path) -- an elementwise program
+// with no specialised form, a generic reduction, or a GEMM epilogue program
+// that is not one of the recognised forms; "" otherwise (runtime.cpp).
+std::string execution_note(const Op& op);
 
 }  // namespace gawee

@@ -416,6 +416,24 @@ static void match_fast_ew(const EProgram& p, kern::EwParams& e) {
   e.fast = fast;
 }
 
+std::string execution_note(const Op& op) {
+  if (op.kind == OpKind::GREDUCE) return " [interp]";
+  if (op.kind == OpKind::TC) {
+    float c = 0.0f;
+    return op.tc.epi == kern::EPI_PROGRAM && match_fast_epilogue(op.tc.prog, &c) == kern::FAST_NONE
+               ? " [interp epilogue]"
+               : "";
+  }
+  if (op.kind != OpKind::EW) return "";
+  bool all_f32 = op.out.dt == DType::F32;
+  for (const auto& v : op.ins) all_f32 = all_f32 && v.dt == DType::F32;
+  kern::EwParams p{};
+  p.fast = kern::EW_INTERP;
+  p.n_in = (int)std::min<size_t>(op.ins.size(), kern::kMaxIn);
+  if (all_f32) match_fast_ew(op.prog, p);
+  return p.fast == kern::EW_INTERP ? " [interp]" : "";
+}
+
 static void launch_ew(Runtime& rt, const Op& op, cudaStream_t s) {
   const View& out = op.out;
   int r = out.rank();

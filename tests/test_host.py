@@ -122,6 +122,14 @@ def test_plan_fuses_attention_without_a_mask():
     assert s.count("attention") == 1 and "softmax" not in s and "matmul" not in s
 
 
+def test_plan_flags_interpreter_fallbacks():
+    # scalar programs without a specialised form are marked in the plan summary
+    assert "[interp" not in _plan(synth.resnet18(1).mlir)
+    assert "[interp" not in _plan(synth.llama15m().mlir)
+    s = _plan(synth.bert_tiny().mlir)
+    assert "[interp epilogue]" in s  # the GELU chain and the bias + residual epilogues of BERT's GEMMs
+
+
 def test_plan_decode_step():
     # the KV-cache decode step: concat of past and new key/value, one query row,
     # attention, RoPE and RMSNorm still fused; logits + 12 present tensors out

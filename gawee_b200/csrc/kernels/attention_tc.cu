@@ -161,6 +161,12 @@ __global__ void __launch_bounds__(256) attn_skip_kernel(const __grid_constant__ 
   if (threadIdx.x == 0) flags[blockIdx.x] = (uint8_t)(all_neg_inf ? 1 : all_zero ? 2 : 0);
 }
 
+// Poll intervals (nanoseconds) of the waits outside the softmax warps.  The
+// softmax warps are bound by instruction issue, and the TMA, MMA and split
+// warps share their sub-partitions: polling those barriers in a tight loop
+// took the issue slots the softmax needs.
+constexpr unsigned kSleepTma = 64, kSleepMma = 32, kSleepSplit = 64;
+
 template <int DV>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_tc_kernel(const __grid_constant__ AttnParams p, const __grid_constant__ CUtensorMap tq,
@@ -237,6 +243,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
     bool ok = true;
     const bool mvec = mrow && p.m_st[3] == 1 && (reinterpret_cast<uintptr_t>(mrow) & 15) == 0;
+    const float scale = p.scale;
     auto correct = [&](int u, float alpha) -> bool {  // O = O * alpha_u + (P_u . V_u), this half's columns
       if (!__all_sync(0xffffffffu, mbar_wait(bar(BAR_PV_F), u & 1, abort_flag, p.status))) return false;
       tc_fence_after();
@@ -286,16 +293,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
         tmem_ld16(trow + scol + c0, x);
+        // the scale's form is chosen once per chunk, outside the element loop:
+        // with the choice inside, the IEEE division ran for every element
+        // (the compiler evaluated both arms), about 150 cycles per score
+        const int valid = min(16, p.Skv - (j0 + c0));
+        if (p.scale_mul) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float sc = -INFINITY;
-          if (j0 + c0 + e < p.Skv) {
-            const float acc = __uint_as_float(x[e]);
-            sc = p.scale_mul ? __fmul_rn(acc, p.scale) : __fdiv_rn(acc, p.scale);
+          for (int e = 0; e < 16; ++e) {
+            float sc = __fmul_rn(__uint_as_float(x[e]), scale);
             if (use_mask) sc = __fadd_rn(sc, mk[e]);
+            if (e >= valid) sc = -INFINITY;
+            tmax = maxnan(tmax, sc);
+            x[e] = __float_as_uint(sc);
           }
-          tmax = maxnan(tmax, sc);
-          x[e] = __float_as_uint(sc);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            float sc = __fdiv_rn(__uint_as_float(x[e]), scale);
+            if (use_mask) sc = __fadd_rn(sc, mk[e]);
+            if (e >= valid) sc = -INFINITY;
+            tmax = maxnan(tmax, sc);
+            x[e] = __float_as_uint(sc);
+          }
         }
         tmem_st16(trow + scol + c0, x);
       }
@@ -374,13 +393,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int kb = t & 1;
         const int j0 = (tiles[t] & 0xffff) * kKeys;
         // K into its buffer once QK of tile t - 2 has completed
-        if (!mbar_wait(bar(kb ? BAR_KE1 : BAR_KE0), ((t >> 1) & 1) ^ 1, abort_flag, p.status)) break;
+        if (!mbar_wait_relaxed(bar(kb ? BAR_KE1 : BAR_KE0), ((t >> 1) & 1) ^ 1, abort_flag, p.status, kSleepTma)) break;
         const uint32_t kf = bar(kb ? BAR_KF1 : BAR_KF0);
         mbar_arrive_tx(kf, 2 * kTile);
         for (int hd = 0; hd < 2; ++hd)
           tma_load_attn(smem_u32(smem + kOffK + (2 * kb + hd) * kTile), &tk, kf, p.cpos[1], hd * 32, j0, hkv, b);
         // V once the split warps have transposed tile t - 1
-        if (!mbar_wait(bar(BAR_VE), (t & 1) ^ 1, abort_flag, p.status)) break;
+        if (!mbar_wait_relaxed(bar(BAR_VE), (t & 1) ^ 1, abort_flag, p.status, kSleepTma)) break;
         mbar_arrive_tx(bar(BAR_VF), 2 * kTile);
         for (int hd = 0; hd < 2; ++hd)
           tma_load_attn(smem_u32(smem + kOffV + hd * kTile), &tv, bar(BAR_VF), p.cpos[2], hd * 32, j0, hkv, b);
@@ -398,13 +417,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const uint32_t id_s = idesc_tf32(kKeys);  // S: N = 128 keys
       const uint32_t id_o = idesc_tf32(DV);     // O: N = head dim
       const uint32_t aq = smem_u32(smem + kOffQ);
-      bool alive = mbar_wait(bar(BAR_Q), 0, abort_flag, p.status) && mbar_wait(bar(BAR_QLO), 0, abort_flag, p.status);
+      bool alive = mbar_wait_relaxed(bar(BAR_Q), 0, abort_flag, p.status, kSleepMma) &&
+                   mbar_wait_relaxed(bar(BAR_QLO), 0, abort_flag, p.status, kSleepMma);
       tc_fence_after();
       auto pv = [&](int u) -> bool {
         const int sb = u & 1;
-        if (!mbar_wait(bar(BAR_P_R), u & 1, abort_flag, p.status)) return false;
-        if (!mbar_wait(bar(BAR_VT_R), u & 1, abort_flag, p.status)) return false;
-        if (!mbar_wait(bar(BAR_PV_E), (u & 1) ^ 1, abort_flag, p.status)) return false;
+        if (!mbar_wait_relaxed(bar(BAR_P_R), u & 1, abort_flag, p.status, kSleepMma)) return false;
+        if (!mbar_wait_relaxed(bar(BAR_VT_R), u & 1, abort_flag, p.status, kSleepMma)) return false;
+        if (!mbar_wait_relaxed(bar(BAR_PV_E), (u & 1) ^ 1, abort_flag, p.status, kSleepMma)) return false;
         tc_fence_after();
         const uint32_t praw = tmem + (sb ? kColS1 : kColS0), plo = tmem + kColPlo, dpv = tmem + kColPV;
         const uint32_t vt = smem_u32(smem + kOffVt), vtl = smem_u32(smem + kOffVtlo);
@@ -433,9 +453,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       };
       for (int t = 0; t < T && alive; ++t) {
         const int kb = t & 1;
-        alive = mbar_wait(bar(kb ? BAR_KF1 : BAR_KF0), (t >> 1) & 1, abort_flag, p.status) &&
-                mbar_wait(bar(BAR_KLO_R), t & 1, abort_flag, p.status) &&
-                mbar_wait(bar(kb ? BAR_SE1 : BAR_SE0), ((t >> 1) & 1) ^ 1, abort_flag, p.status);
+        alive = mbar_wait_relaxed(bar(kb ? BAR_KF1 : BAR_KF0), (t >> 1) & 1, abort_flag, p.status, kSleepMma) &&
+                mbar_wait_relaxed(bar(BAR_KLO_R), t & 1, abort_flag, p.status, kSleepMma) &&
+                mbar_wait_relaxed(bar(kb ? BAR_SE1 : BAR_SE0), ((t >> 1) & 1) ^ 1, abort_flag, p.status, kSleepMma);
         if (!alive) break;
         tc_fence_after();
         const uint32_t ds = tmem + (kb ? kColS1 : kColS0);
@@ -471,7 +491,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int q4 = warp & 3;                 // tensor-memory lane quarter of this warp
     const int row = q4 * 32 + lane;          // Q row for Q lo
     const int tid = (warp - 10) * 32 + lane;  // 0..127 for the K / V tiles
-    bool alive = mbar_wait(bar(BAR_Q), 0, abort_flag, p.status);
+    bool alive = mbar_wait_relaxed(bar(BAR_Q), 0, abort_flag, p.status, kSleepSplit);
     if (alive) {
       const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
       for (int hd = 0; hd < 2; ++hd) {
@@ -540,13 +560,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     };
     for (int t = 0; t < T && alive; ++t) {
       const int kb = t & 1;
-      alive = mbar_wait(bar(kb ? BAR_KF1 : BAR_KF0), (t >> 1) & 1, abort_flag, p.status) &&
-              mbar_wait(bar(BAR_KLO_F), (t & 1) ^ 1, abort_flag, p.status);
+      alive = mbar_wait_relaxed(bar(kb ? BAR_KF1 : BAR_KF0), (t >> 1) & 1, abort_flag, p.status, kSleepSplit) &&
+              mbar_wait_relaxed(bar(BAR_KLO_F), (t & 1) ^ 1, abort_flag, p.status, kSleepSplit);
       if (!alive) break;
       split_tile(smem_u32(smem + kOffK + 2 * kb * kTile), smem_u32(smem + kOffKlo));
       if (lane == 0) mbar_arrive(bar(BAR_KLO_R));
-      alive = mbar_wait(bar(BAR_VF), t & 1, abort_flag, p.status) &&
-              mbar_wait(bar(BAR_VT_F), (t & 1) ^ 1, abort_flag, p.status);
+      alive = mbar_wait_relaxed(bar(BAR_VF), t & 1, abort_flag, p.status, kSleepSplit) &&
+              mbar_wait_relaxed(bar(BAR_VT_F), (t & 1) ^ 1, abort_flag, p.status, kSleepSplit);
       if (!alive) break;
       transpose_v();
       if (lane == 0) {

@@ -326,12 +326,19 @@ __device__ __forceinline__ void tile_epilogue(const ConvGemmParams& p, float (&a
           // computed in place: this chunk's accumulators are not needed
           // afterwards, and the aux registers are free for the next chunk,
           // whose loads are then in flight while this one is stored
+          // one loop per form: a form chosen per element let the compiler
+          // evaluate the IEEE division for every element of every form
+          if (p.fast == FAST_ADD) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float x = acc[c0 + j];
-            if (p.fast == FAST_ADD) acc[c0 + j] = __fadd_rn(x, a[j]);
-            else if (p.fast == FAST_DIVC_ADD) acc[c0 + j] = __fadd_rn(__fdiv_rn(x, p.fast_c), a[j]);
-            else acc[c0 + j] = __fadd_rn(__fmul_rn(x, p.fast_c), a[j]);
+            for (int j = 0; j < 16; ++j) acc[c0 + j] = __fadd_rn(acc[c0 + j], a[j]);
+          } else if (p.fast == FAST_DIVC_ADD) {
+            const float c = p.fast_c;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc[c0 + j] = __fadd_rn(__fdiv_rn(acc[c0 + j], c), a[j]);
+          } else {
+            const float c = p.fast_c;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc[c0 + j] = __fadd_rn(__fmul_rn(acc[c0 + j], c), a[j]);
           }
           if (c0 + 16 < HB) {
 #pragma unroll
@@ -424,19 +431,29 @@ __device__ __forceinline__ void tile_epilogue(const ConvGemmParams& p, float (&a
             a1[j] = (in && p.fast == FAST_SIGMOID_MUL) ? __ldg(p.aux[1] + aux_row[1] + n * p.aux_sn[1]) : 0.f;
           }
         }
+        float xs[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int64_t n = nb0 + c0 + j;
-          const float x = p.bias ? __fadd_rn(acc[c0 + j], n < p.N ? __ldg(p.bias + n) : 0.f) : acc[c0 + j];
-          if (p.fast == FAST_ADD) {
-            o[j] = __fadd_rn(x, a0[j]);
-          } else if (p.fast == FAST_DIVC_ADD) {
-            o[j] = __fadd_rn(__fdiv_rn(x, p.fast_c), a0[j]);
-          } else if (p.fast == FAST_MULC_ADD) {
-            o[j] = __fadd_rn(__fmul_rn(x, p.fast_c), a0[j]);
-          } else {
+          xs[j] = p.bias ? __fadd_rn(acc[c0 + j], n < p.N ? __ldg(p.bias + n) : 0.f) : acc[c0 + j];
+        }
+        // one loop per form (see the coalesced path)
+        if (p.fast == FAST_ADD) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = __fadd_rn(xs[j], a0[j]);
+        } else if (p.fast == FAST_DIVC_ADD) {
+          const float c = p.fast_c;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = __fadd_rn(__fdiv_rn(xs[j], c), a0[j]);
+        } else if (p.fast == FAST_MULC_ADD) {
+          const float c = p.fast_c;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = __fadd_rn(__fmul_rn(xs[j], c), a0[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
             const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-a1[j])));
-            o[j] = __fmul_rn(__fmul_rn(a0[j], sg), x);
+            o[j] = __fmul_rn(__fmul_rn(a0[j], sg), xs[j]);
           }
         }
         store8(c0, o);

@@ -558,13 +558,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       fence_async_smem();  // generic-proxy writes, read by the tensor core
       __syncwarp();
     };
-    for (int t = 0; t < T && alive; ++t) {
-      const int kb = t & 1;
-      alive = mbar_wait_relaxed(bar(kb ? BAR_KF1 : BAR_KF0), (t >> 1) & 1, abort_flag, p.status, kSleepSplit) &&
-              mbar_wait_relaxed(bar(BAR_KLO_F), (t & 1) ^ 1, abort_flag, p.status, kSleepSplit);
-      if (!alive) break;
+    // K lo of tile u once K(u) has landed and QK(u - 1) has read K lo(u - 1)
+    auto k_lo = [&](int u) -> bool {
+      const int kb = u & 1;
+      if (!(mbar_wait_relaxed(bar(kb ? BAR_KF1 : BAR_KF0), (u >> 1) & 1, abort_flag, p.status, kSleepSplit) &&
+            mbar_wait_relaxed(bar(BAR_KLO_F), (u & 1) ^ 1, abort_flag, p.status, kSleepSplit)))
+        return false;
       split_tile(smem_u32(smem + kOffK + 2 * kb * kTile), smem_u32(smem + kOffKlo));
       if (lane == 0) mbar_arrive(bar(BAR_KLO_R));
+      return true;
+    };
+    // K lo(t + 1) goes before the transpose of V(t): the transpose waits for
+    // P.V(t - 1), and QK(t + 1) should not wait behind it
+    if (T > 0) alive = k_lo(0);
+    for (int t = 0; t < T && alive; ++t) {
+      if (t + 1 < T && !k_lo(t + 1)) {
+        alive = false;
+        break;
+      }
       alive = mbar_wait_relaxed(bar(BAR_VF), t & 1, abort_flag, p.status, kSleepSplit) &&
               mbar_wait_relaxed(bar(BAR_VT_F), (t & 1) ^ 1, abort_flag, p.status, kSleepSplit);
       if (!alive) break;

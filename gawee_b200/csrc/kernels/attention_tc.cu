@@ -190,27 +190,45 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int hkv = h / (p.H / p.Hkv);
   const int q0 = qt * kRowsQ;
 
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < NUM_BARS; ++i) {
-      uint32_t count = 1;
-      if (i == BAR_QLO || i == BAR_KLO_R || i == BAR_VT_R || i == BAR_VE) count = 4;
-      if (i == BAR_P_R || i == BAR_PV_E) count = 8;
-      mbar_init(bar(i), count);
-    }
-    *abort_flag = 0;
-    int n = 0;
-    const uint8_t* fl = p.skip ? p.skip + ((int64_t)((p.mb > 1 ? b : 0) * p.mh + (p.mh > 1 ? h : 0)) * p.QT + qt) * p.KT
-                               : nullptr;
-    for (int kt = 0; kt < p.KT; ++kt)
-      if (!fl || fl[kt] != 1) tiles[n++] = kt | ((fl && fl[kt] == 2) ? 0x10000 : 0);
-    *ntiles = n;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
   if (warp == 8) {
+    // the TMA warp sets up the barriers and issues Q at once: its latency
+    // overlaps the tile list and the tensor-memory allocation
+    if (lane == 0) {
+      for (int i = 0; i < NUM_BARS; ++i) {
+        uint32_t count = 1;
+        if (i == BAR_QLO || i == BAR_KLO_R || i == BAR_VT_R || i == BAR_VE) count = 4;
+        if (i == BAR_P_R || i == BAR_PV_E) count = 8;
+        mbar_init(bar(i), count);
+      }
+      *abort_flag = 0;
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tq)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tk)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tv)) : "memory");
+      mbar_arrive_tx(bar(BAR_Q), 2 * kTile);
+      for (int hd = 0; hd < 2; ++hd)
+        tma_load_attn(smem_u32(smem + kOffQ + hd * kTile), &tq, bar(BAR_Q), p.cpos[0], hd * 32, q0, h, b);
+    }
+    __syncwarp();
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(512u)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  } else if (warp == 0) {
+    // the key tiles this query tile visits, ascending: one flag per lane
+    // (all reads in flight together), compacted with ballots
+    const uint8_t* fl = p.skip ? p.skip + ((int64_t)((p.mb > 1 ? b : 0) * p.mh + (p.mh > 1 ? h : 0)) * p.QT + qt) * p.KT
+                               : nullptr;
+    int n = 0;
+    for (int base = 0; base < p.KT; base += 32) {
+      const int kt = base + lane;
+      const int f = (fl && kt < p.KT) ? (int)fl[kt] : 0;
+      const bool keep = kt < p.KT && f != 1;
+      const unsigned m = __ballot_sync(0xffffffffu, keep);
+      if (keep) tiles[n + __popc(m & ((1u << lane) - 1u))] = kt | (f == 2 ? 0x10000 : 0);
+      n += __popc(m);
+    }
+    if (lane == 0) *ntiles = n;
   }
   tc_fence_before();
   __syncthreads();
@@ -383,13 +401,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else if (warp == 8) {
     // ------------------------------------------------------------------ TMA
     if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tq)) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tk)) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tv)) : "memory");
-      mbar_arrive_tx(bar(BAR_Q), 2 * kTile);
-      for (int hd = 0; hd < 2; ++hd)
-        tma_load_attn(smem_u32(smem + kOffQ + hd * kTile), &tq, bar(BAR_Q), p.cpos[0], hd * 32, q0, h, b);
-      for (int t = 0; t < T; ++t) {
+      for (int t = 0; t < T; ++t) {  // (Q was issued before the block-wide barrier)
         const int kb = t & 1;
         const int j0 = (tiles[t] & 0xffff) * kKeys;
         // K into its buffer once QK of tile t - 2 has completed

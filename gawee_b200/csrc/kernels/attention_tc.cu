@@ -429,8 +429,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const uint32_t id_s = idesc_tf32(kKeys);  // S: N = 128 keys
       const uint32_t id_o = idesc_tf32(DV);     // O: N = head dim
       const uint32_t aq = smem_u32(smem + kOffQ);
-      bool alive = mbar_wait_relaxed(bar(BAR_Q), 0, abort_flag, p.status, kSleepMma) &&
-                   mbar_wait_relaxed(bar(BAR_QLO), 0, abort_flag, p.status, kSleepMma);
+      // Q lo is waited for just before the first lo products (tile 0)
+      bool alive = mbar_wait_relaxed(bar(BAR_Q), 0, abort_flag, p.status, kSleepMma);
       tc_fence_after();
       auto pv = [&](int u) -> bool {
         const int sb = u & 1;
@@ -465,28 +465,39 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       };
       for (int t = 0; t < T && alive; ++t) {
         const int kb = t & 1;
+        // the raw products need only K and a free score buffer; K lo (and,
+        // for tile 0, Q lo) are waited for after them, so the split of K
+        // overlaps the first eight MMAs
         alive = mbar_wait_relaxed(bar(kb ? BAR_KF1 : BAR_KF0), (t >> 1) & 1, abort_flag, p.status, kSleepMma) &&
-                mbar_wait_relaxed(bar(BAR_KLO_R), t & 1, abort_flag, p.status, kSleepMma) &&
                 mbar_wait_relaxed(bar(kb ? BAR_SE1 : BAR_SE0), ((t >> 1) & 1) ^ 1, abort_flag, p.status, kSleepMma);
         if (!alive) break;
         tc_fence_after();
         const uint32_t ds = tmem + (kb ? kColS1 : kColS0);
+        const uint32_t k_raw = smem_u32(smem + kOffK + 2 * kb * kTile);
+#pragma unroll
         for (int hd = 0; hd < 2; ++hd) {  // K = 64: two 32-wide halves of the head dim
           const uint64_t dq = umma_desc_sw128(aq + hd * kTile);
-          const uint64_t dk = umma_desc_sw128(smem_u32(smem + kOffK + (2 * kb + hd) * kTile));
-          const uint64_t dkl = umma_desc_sw128(smem_u32(smem + kOffKlo + hd * kTile));
-          const uint32_t qlo = tmem + kColQlo + 32 * hd;
-          if (three) {
+          const uint64_t dk = umma_desc_sw128(k_raw + hd * kTile);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) umma_ss(ds, dq + 2 * kk, dk + 2 * kk, id_s, (hd | kk) != 0);
+        }
+        alive = mbar_wait_relaxed(bar(BAR_KLO_R), t & 1, abort_flag, p.status, kSleepMma) &&
+                (t > 0 || mbar_wait_relaxed(bar(BAR_QLO), 0, abort_flag, p.status, kSleepMma));
+        if (!alive) break;
+        tc_fence_after();
+        if (three) {
+#pragma unroll
+          for (int hd = 0; hd < 2; ++hd) {
+            const uint64_t dq = umma_desc_sw128(aq + hd * kTile);
+            const uint64_t dk = umma_desc_sw128(k_raw + hd * kTile);
+            const uint64_t dkl = umma_desc_sw128(smem_u32(smem + kOffKlo + hd * kTile));
+            const uint32_t qlo = tmem + kColQlo + 32 * hd;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               const uint64_t o = (uint64_t)(2 * kk);
-              umma_ss(ds, dq + o, dk + o, id_s, (hd | kk) != 0);
               umma_ss(ds, dq + o, dkl + o, id_s, 1);
               umma_tf32_ts(ds, qlo + 8 * kk, dk + o, id_s, 1);
             }
-          } else {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) umma_ss(ds, dq + 2 * kk, dk + 2 * kk, id_s, (hd | kk) != 0);
           }
         }
         umma_commit(bar(kb ? BAR_SF1 : BAR_SF0));

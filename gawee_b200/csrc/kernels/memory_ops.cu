@@ -1022,16 +1022,20 @@ __global__ void __launch_bounds__(kThreads) rope_kernel(const __grid_constant__ 
   }
 }
 
-// Four consecutive outputs of one row per thread (d and d / 2 multiples of
-// 4, so the four sit on one side of the half), 32-bit coordinates, float4
-// loads of x, cos and sin where their last stride is 1 and rows are aligned.
+// Four consecutive columns of one row and their partners half a row away
+// per thread (d / 2 a multiple of 4): out[c] = x[c] cos[c] + (-x[c + h]) sin[c]
+// and out[c + h] = x[c + h] cos[c + h] + x[c] sin[c + h] read x[c] and
+// x[c + h] once for both; 32-bit coordinates found once per eight outputs;
+// float4 loads of x, cos and sin where their last stride is 1 and rows are
+// aligned.
 __global__ void __launch_bounds__(kThreads) rope4_kernel(const __grid_constant__ RopeParams p, unsigned vec_mask) {
   const int r = p.rank;
-  const uint32_t d = (uint32_t)p.shape[r - 1], q4 = d / 4, half = (uint32_t)p.half;
-  const uint32_t total = (uint32_t)(p.numel / 4);
+  const uint32_t d = (uint32_t)p.shape[r - 1], half = (uint32_t)p.half, h4 = half / 4;
+  const uint32_t total = (uint32_t)(p.numel / 8);
   for (uint32_t u = blockIdx.x * blockDim.x + threadIdx.x; u < total; u += gridDim.x * blockDim.x) {
-    uint32_t rem = u / q4;
-    const uint32_t col = (u - rem * q4) * 4;
+    uint32_t rem = u / h4;
+    const uint32_t col = (u - rem * h4) * 4;
+    const uint32_t row = rem;
     int64_t xo = 0, co = 0, so = 0;
     for (int k = r - 2; k >= 0; --k) {
       const uint32_t sh = (uint32_t)p.shape[k];
@@ -1042,8 +1046,7 @@ __global__ void __launch_bounds__(kThreads) rope4_kernel(const __grid_constant__
       co += c * p.c_st[k];
       so += c * p.s_st[k];
     }
-    const uint32_t rcol = col < half ? col + half : col - half;
-    float xv[4], rv[4], cv[4], sv[4];
+    float a[4], b[4], ca[4], cb[4], sa[4], sb[4];
     auto load4 = [&](const float* base, int64_t st, bool v, float (&o)[4]) {
       if (v) {
         const float4 t = __ldg(reinterpret_cast<const float4*>(base));
@@ -1054,16 +1057,21 @@ __global__ void __launch_bounds__(kThreads) rope4_kernel(const __grid_constant__
       }
     };
     const int64_t xl = p.x_st[r - 1], cl = p.c_st[r - 1], sl = p.s_st[r - 1];
-    load4(p.x + xo + col * xl, xl, vec_mask & 1, xv);
-    load4(p.x + xo + rcol * xl, xl, vec_mask & 1, rv);
-    load4(p.cs + co + col * cl, cl, vec_mask & 2, cv);
-    load4(p.sn + so + col * sl, sl, vec_mask & 4, sv);
-    const bool neg = col < half;
-    float o[4];
+    load4(p.x + xo + col * xl, xl, vec_mask & 1, a);
+    load4(p.x + xo + (col + half) * xl, xl, vec_mask & 1, b);
+    load4(p.cs + co + col * cl, cl, vec_mask & 2, ca);
+    load4(p.cs + co + (col + half) * cl, cl, vec_mask & 2, cb);
+    load4(p.sn + so + col * sl, sl, vec_mask & 4, sa);
+    load4(p.sn + so + (col + half) * sl, sl, vec_mask & 4, sb);
+    float lo[4], hi[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e)
-      o[e] = __fadd_rn(__fmul_rn(xv[e], cv[e]), __fmul_rn(neg ? -rv[e] : rv[e], sv[e]));
-    *reinterpret_cast<float4*>(p.out + (int64_t)u * 4) = make_float4(o[0], o[1], o[2], o[3]);
+    for (int e = 0; e < 4; ++e) {
+      lo[e] = __fadd_rn(__fmul_rn(a[e], ca[e]), __fmul_rn(-b[e], sa[e]));
+      hi[e] = __fadd_rn(__fmul_rn(b[e], cb[e]), __fmul_rn(a[e], sb[e]));
+    }
+    float* orow = p.out + (int64_t)row * d;
+    *reinterpret_cast<float4*>(orow + col) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+    *reinterpret_cast<float4*>(orow + col + half) = make_float4(hi[0], hi[1], hi[2], hi[3]);
   }
 }
 
@@ -1077,10 +1085,11 @@ void launch_rope(const RopeParams& p, cudaStream_t s) {
       if (st[k] % 4) return false;
     return true;
   };
-  if (d % 8 == 0 && p.numel / 4 < (int64_t(1) << 31) && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0) {
+  if (d % 8 == 0 && 2 * p.half == d && p.numel / 4 < (int64_t(1) << 31) &&
+      (reinterpret_cast<uintptr_t>(p.out) & 15) == 0) {
     const unsigned mask = (rows_aligned(p.x, p.x_st) ? 1u : 0u) | (rows_aligned(p.cs, p.c_st) ? 2u : 0u) |
                           (rows_aligned(p.sn, p.s_st) ? 4u : 0u);
-    rope4_kernel<<<resident_grid<rope4_kernel>(p.numel / 4), kThreads, 0, s>>>(p, mask);
+    rope4_kernel<<<resident_grid<rope4_kernel>(p.numel / 8), kThreads, 0, s>>>(p, mask);
     return;
   }
   rope_kernel<<<resident_grid<rope_kernel>(p.numel), kThreads, 0, s>>>(p);

@@ -927,9 +927,68 @@ void launch_topk(const TopKParams& p, cudaStream_t s) {
 }
 
 // ---------------------------------------------------------------------------
-// Row normalisation: one warp per row.  The row is read twice (the second
-// read hits L1), written once; the sums are per-lane then a shuffle tree.
+// Row normalisation: one warp per row.  Rows of at most kRowRegCols columns
+// (float4-aligned) are loaded once into registers, all loads in flight
+// together; longer or unaligned rows are read again per pass (the repeat
+// reads hit L1).  Either way each lane adds its own elements in ascending
+// column order and a shuffle tree adds the lanes, so both forms give the
+// same bits.
 // ---------------------------------------------------------------------------
+constexpr int kRowRegVecs = 8;                  // float4 per lane
+constexpr int kRowRegCols = kRowRegVecs * 128;  // 1024 columns
+
+__device__ __forceinline__ void rownorm_row_regs(const RowNormParams& p, const float* x, float* y, int lane,
+                                                 float count) {
+  auto warp_sum = [](float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+  };
+  float4 v[kRowRegVecs];
+#pragma unroll
+  for (int j = 0; j < kRowRegVecs; ++j) {
+    const int64_t c = lane * 4 + 128 * j;
+    v[j] = c < p.cols ? *reinterpret_cast<const float4*>(x + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float mu = 0.f;
+  if (p.centered) {
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < kRowRegVecs; ++j)
+      if (lane * 4 + 128 * j < p.cols) s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v[j].x), v[j].y), v[j].z), v[j].w);
+    mu = __fdiv_rn(warp_sum(s), count);
+  }
+  float s2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < kRowRegVecs; ++j) {
+    if (lane * 4 + 128 * j < p.cols) {
+      const float a = __fsub_rn(v[j].x, mu), b = __fsub_rn(v[j].y, mu), d = __fsub_rn(v[j].z, mu),
+                  e = __fsub_rn(v[j].w, mu);
+      s2 = __fadd_rn(s2, __fmul_rn(a, a));
+      s2 = __fadd_rn(s2, __fmul_rn(b, b));
+      s2 = __fadd_rn(s2, __fmul_rn(d, d));
+      s2 = __fadd_rn(s2, __fmul_rn(e, e));
+    }
+  }
+  const float r = __fsqrt_rn(__fadd_rn(__fdiv_rn(warp_sum(s2), count), p.eps));
+#pragma unroll
+  for (int j = 0; j < kRowRegVecs; ++j) {
+    const int64_t c = lane * 4 + 128 * j;
+    if (c < p.cols) {
+      const float4 w = __ldg(reinterpret_cast<const float4*>(p.w + c));
+      float4 o = make_float4(__fmul_rn(__fdiv_rn(__fsub_rn(v[j].x, mu), r), w.x),
+                             __fmul_rn(__fdiv_rn(__fsub_rn(v[j].y, mu), r), w.y),
+                             __fmul_rn(__fdiv_rn(__fsub_rn(v[j].z, mu), r), w.z),
+                             __fmul_rn(__fdiv_rn(__fsub_rn(v[j].w, mu), r), w.w));
+      if (p.b) {
+        const float4 bb = __ldg(reinterpret_cast<const float4*>(p.b + c));
+        o = make_float4(__fadd_rn(o.x, bb.x), __fadd_rn(o.y, bb.y), __fadd_rn(o.z, bb.z), __fadd_rn(o.w, bb.w));
+      }
+      *reinterpret_cast<float4*>(y + c) = o;
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kThreads) rownorm_kernel(const __grid_constant__ RowNormParams p) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
@@ -946,6 +1005,10 @@ __global__ void __launch_bounds__(kThreads) rownorm_kernel(const __grid_constant
   for (int64_t row = blockIdx.x * (int64_t)(blockDim.x / 32) + threadIdx.x / 32; row < p.rows; row += warps) {
     const float* x = p.x + row * p.x_rs;
     float* y = p.out + row * p.cols;
+    if (vec && p.cols <= kRowRegCols) {
+      rownorm_row_regs(p, x, y, lane, count);
+      continue;
+    }
     float mu = 0.f;
     if (p.centered) {
       float s = 0.f;

@@ -343,17 +343,22 @@ def test_fused_rms_and_layer_norm():
     """RMSNorm and LayerNorm chains as the emitter decomposes them (Pow /
     ReduceMean / Add / Sqrt / Div / Mul [/ Add], centering by Sub of a mean)
     run as one row kernel each, on a dense and on a strided (transposed)
-    input, within fp32 rounding of the oracle's sequential sums."""
+    input, within fp32 rounding of the oracle's sequential sums.  Rows of up
+    to 1024 aligned columns are held in registers, longer ones are streamed:
+    576 and 1536 columns cover one of each."""
     from gawee_b200.synth import _layer_norm, _rms_norm
 
     def g_(g):
         x = rand_input(g, (2, 5, 96), 91, scale=3.0)
         xt = g.transpose(rand_input(g, (5, 2, 96), 92), [1, 0, 2])  # rows with two strides
         y = rand_input(g, (3, 7, 100), 93)                           # cols not a multiple of 4
-        return [_rms_norm(g, x, 1e-5), _rms_norm(g, xt, 1e-6), _layer_norm(g, y, 1e-12), _layer_norm(g, x, 1e-5)]
+        z = rand_input(g, (3, 4, 576), 94, scale=2.0)                # lanes hold 4 or 5 float4
+        u = rand_input(g, (2, 3, 1536), 98)                          # longer than the register row
+        return [_rms_norm(g, x, 1e-5), _rms_norm(g, xt, 1e-6), _layer_norm(g, y, 1e-12), _layer_norm(g, x, 1e-5),
+                _rms_norm(g, z, 1e-5), _layer_norm(g, z, 1e-5), _rms_norm(g, u, 1e-6), _layer_norm(g, u, 1e-5)]
     mlir, args = build(g_)
     s = _names(mlir)
-    assert s.count("rms_norm") == 2 and s.count("layer_norm") == 2, s
+    assert s.count("rms_norm") == 4 and s.count("layer_norm") == 4, s
     parity(mlir, args, atol=2e-6, rtol=2e-6)
 
 

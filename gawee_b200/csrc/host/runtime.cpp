@@ -110,6 +110,7 @@ struct Runtime {
   int tma_rk = kern::kRK;                  // TMA kernel: k-blocks per promotion round
   int passes = 3;                          // tensor-core passes per product (precision mode: 3 fp32, 1 tf32)
   std::vector<int> ksplit;                 // per op (TC only): k splits, 1 = none
+  std::vector<char> aux_tma;               // per op (TC only): epilogue operand staged by TMA (TMA kernel)
   std::vector<uint8_t*> attn_skip;         // per op (ATTN only): skip flags of the mask tiles
   std::vector<std::array<std::array<int8_t, 3>, 3>> attn_cpos;  // per op (ATTN): tensor-map dim order
   float* splitk_ws = nullptr;              // partial sums of split contractions (ops run in order: shared)
@@ -216,14 +217,22 @@ static GemmRows merged_rows(const Op& op) {
   return g;
 }
 
+kern::ConvGemmParams tc_params(Runtime& rt, int o, const Op& op);
+
 void Runtime::build_tensor_maps() {
   Plan& P = *plan;
   tmaps.assign(P.ops.size(), {});
   ksplit.assign(P.ops.size(), 1);
+  aux_tma.assign(P.ops.size(), 0);
   a_tma.assign(P.ops.size(), kern::A_TMA_NONE);
   // GAWEE_TC_TMA=0 keeps every contraction on the warp-gather kernel
   bool use_tma = true;
   if (const char* e = std::getenv("GAWEE_TC_TMA")) use_tma = std::atoi(e) != 0;
+  // GAWEE_TC_TMA_AUX=1 has the TMA kernel stage its epilogue's residual or
+  // fast-epilogue operand in shared memory by TMA; 0 reads it from global
+  // memory in the epilogue
+  bool use_aux = false;
+  if (const char* e = std::getenv("GAWEE_TC_TMA_AUX")) use_aux = std::atoi(e) != 0;
   int sms = 0;
   GCHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
   // GAWEE_MAX_KSPLIT caps the k splits of small contractions (1 disables them)
@@ -295,6 +304,8 @@ void Runtime::build_tensor_maps() {
                                                     a_tma[o] != kern::A_TMA_NONE ? tma_rk : kern::kRK));
     ksplit[o] = k;
     if (k > 1) ws_floats = std::max(ws_floats, (size_t)k * (size_t)gr.M * (size_t)t.N);
+    if (use_aux && a_tma[o] != kern::A_TMA_NONE && k == 1)
+      aux_tma[o] = kern::conv_gemm_tma_aux_ok(tc_params(*this, (int)o, op)) ? 1 : 0;
   }
   if (ws_floats) {
     if (cudaMalloc(&splitk_ws, ws_floats * sizeof(float)) != cudaSuccess)
@@ -492,7 +503,9 @@ static void launch_ew(Runtime& rt, const Op& op, cudaStream_t s) {
   kern::launch_elementwise(p, s);
 }
 
-static void launch_tc(Runtime& rt, int o, const Op& op, cudaStream_t s) {
+// The contraction's launch parameters, from the op and the runtime's
+// per-op choices (A source, k splits, aux staging).
+kern::ConvGemmParams tc_params(Runtime& rt, int o, const Op& op) {
   const auto& t = op.tc;
   kern::ConvGemmParams p{};
   p.x = reinterpret_cast<const float*>(rt.ptr(t.x));
@@ -553,10 +566,19 @@ static void launch_tc(Runtime& rt, int o, const Op& op, cudaStream_t s) {
     p.ksplit = rt.ksplit[o];
     p.ws = rt.splitk_ws;
   }
-  bool launched;
   if (rt.a_tma[o] != kern::A_TMA_NONE) {
     p.a_tma = rt.a_tma[o];
     p.rk = rt.tma_rk;
+    p.aux_tma = o < (int)rt.aux_tma.size() ? rt.aux_tma[o] : 0;
+  }
+  return p;
+}
+
+static void launch_tc(Runtime& rt, int o, const Op& op, cudaStream_t s) {
+  const auto& t = op.tc;
+  const kern::ConvGemmParams p = tc_params(rt, o, op);
+  bool launched;
+  if (rt.a_tma[o] != kern::A_TMA_NONE) {
     launched = kern::launch_conv_gemm_tma(p, rt.tmaps[o][2].b, rt.tmaps[o][0].b, rt.tmaps[o][1].b, t.block_n, s);
   } else {
     launched = kern::launch_conv_gemm_tc(p, rt.tmaps[o][0].b, rt.tmaps[o][1].b, t.block_n, s);
@@ -1183,6 +1205,8 @@ gawee_status gawee_op_info(const gawee_ctx* ctx, int i, char* name, size_t n, in
                                                                   : " [tma]";
     if (op.kind == gawee::OpKind::TC && o < (int)ctx->rt.ksplit.size() && ctx->rt.ksplit[o] > 1)
       nm += " [split-k " + std::to_string(ctx->rt.ksplit[o]) + "]";
+    if (op.kind == gawee::OpKind::TC && o < (int)ctx->rt.aux_tma.size() && ctx->rt.aux_tma[o])
+      nm += " [aux smem]";
     std::strncpy(name, nm.c_str(), n - 1);
     name[n - 1] = 0;
   }

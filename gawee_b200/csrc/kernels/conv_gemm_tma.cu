@@ -49,29 +49,37 @@ namespace kern {
 namespace {
 
 // Stages per tile width: 4 x 48 KB (BN 128) or 4 x 32 KB (BN 64) of shared
-// memory plus 20 KB of epilogue staging; tensor memory holds 4 A stages of
-// 64 columns (raw, remainder) beside the two round accumulators.
+// memory plus 20 KB of epilogue staging; tensor memory holds NS A stages of
+// 64 columns (raw, remainder) beside the two round accumulators.  With the
+// epilogue's aux operand staged by TMA (AUX), the [128][BN] aux tile takes
+// the staging's place and BN 128 keeps 3 stages (3 x 48 + 64 KB).
 template <int BN>
 struct TmaConfig;
 template <>
 struct TmaConfig<64> {
   static constexpr int NS = 4;
+  static constexpr int NS_AUX = 4;
 };
 template <>
 struct TmaConfig<128> {
   static constexpr int NS = 4;
+  static constexpr int NS_AUX = 3;
 };
 
-template <int BN, int NS>
+template <int BN, int NS, int AUX = 0>
 struct TmaSmem {
   static constexpr int kATile = kBM * kBK * 4;          // 16 KB: raw A of one k-block
   static constexpr int kBTile = BN * kBK * 4;           // one B plane of one k-block
   static constexpr int kStage = kATile + 2 * kBTile;    // A, B hi, B lo (a multiple of 1024)
-  static constexpr int kStageOff = NS * kStage;         // epilogue staging
-  static constexpr int kBarOff = kStageOff + 8 * kStageWarpFloats * 4;
+  static constexpr int kStageOff = NS * kStage;         // epilogue staging, or the aux tile
+  // the aux tile: BN / 32 boxes of [128 rows][32 columns], 16 KB each, 128-byte swizzled
+  static constexpr int kAuxBox = kBM * kBK * 4;
+  static constexpr int kAuxBytes = AUX ? (BN / kBK) * kAuxBox : 0;
+  static constexpr int kBarOff = kStageOff + (AUX ? kAuxBytes : 8 * kStageWarpFloats * 4);
   static constexpr int kNAcc = 2;                       // round accumulators in tensor memory
-  // full, remainders-ready, empty per stage; full, empty per accumulator; all MMAs done
-  static constexpr int kNumBars = 3 * NS + 2 * kNAcc + 1;
+  // full, remainders-ready, empty per stage; full, empty per accumulator; all
+  // MMAs done; with AUX the aux tile's full and empty
+  static constexpr int kNumBars = 3 * NS + 2 * kNAcc + 1 + (AUX ? 2 : 0);
   static constexpr int kBytes = kBarOff + 8 * kNumBars + 16 + 1024;  // + alignment slack
   // BN 64 folds hi*hi and hi*lo into one N = 128 MMA (B stage: hi rows then lo rows)
   static constexpr bool kFold = BN == 64;
@@ -109,11 +117,18 @@ __device__ __forceinline__ void tma_load_im2col_4d(uint32_t dst, const CUtensorM
 // accumulator warps a whole round.
 constexpr unsigned kSleepA = 64, kSleepTma = 32, kSleepAcc = 256;
 
-template <int BN, int NS, int EPI, int PASSES>
+// AUX: the epilogue's aux operand (the residual of EPI_BIAS_ADD_RELU, or
+// aux 0 of EPI_FAST) is loaded per tile by the TMA warp through tm_x into
+// shared memory, 2 * NS k-blocks before the tile's last, instead of being
+// read from global memory by the accumulator warps after the tile's last
+// round (which held the MMA issuer up once it ran out of drained
+// accumulators).  Only unsplit launches (ksplit 1) use it.
+template <int BN, int NS, int EPI, int PASSES, int AUX>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     conv_gemm_tma_kernel(const __grid_constant__ ConvGemmParams p, const __grid_constant__ CUtensorMap tm_a,
-                         const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo) {
-  using L = TmaSmem<BN, NS>;
+                         const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo,
+                         const __grid_constant__ CUtensorMap tm_x) {
+  using L = TmaSmem<BN, NS, AUX>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
@@ -124,6 +139,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint64_t* accf = bars + 3 * NS;      // round accumulator complete (one commit)
   uint64_t* acce = accf + L::kNAcc;    // round accumulator drained (8 accumulator warps)
   uint64_t* done = acce + L::kNAcc;    // every MMA of this CTA completed
+  uint64_t* aux_full = done + 1;       // AUX: the tile's aux operand landed (TMA transaction bytes)
+  uint64_t* aux_empty = done + 2;      // AUX: the aux tile's epilogue is done with it (8 accumulator warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -171,6 +188,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       mbar_init(smem_u32(&acce[b]), 8);
     }
     mbar_init(smem_u32(done), 1);
+    if (AUX) {
+      mbar_init(smem_u32(aux_full), 1);
+      mbar_init(smem_u32(aux_empty), 8);
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -261,9 +282,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_a)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_hi)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_lo)) : "memory");
+      if (AUX) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_x)) : "memory");
       const int C = (int)p.C, S = p.S;
       const uint32_t PQ = (uint32_t)(p.P * p.Q), Q = (uint32_t)p.Q;
+      // AUX: the unit-local k-block after whose loads the aux tile is loaded
+      // (an unsplit unit covers all num_kb k-blocks)
+      const int aux_at = max(0, num_kb - 2 * NS);
       uint32_t g = 0;
+      uint32_t ua = 0;  // aux tiles loaded
       bool alive = true;
       for (int64_t u = blockIdx.x; u < num_units && alive; u += gridDim.x) {
         int64_t m0;
@@ -275,10 +301,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         const uint32_t pp = pq / Q, qq = pq - pp * Q;
         const int w0 = (int)(qq * p.sw) - p.pw, h0 = (int)(pp * p.sh) - p.ph;
         const int rot = r_rotation(m0, nr);
+        int jj = 0;  // unit-local k-block
         for (int rr = 0; rr < nr && alive; ++rr) {
           const int r = r_lo + (rot + rr) % nr;
           const int nk = round_kbs(r);
-          for (int j = 0; j < nk; ++j, ++g) {
+          for (int j = 0; j < nk; ++j, ++g, ++jj) {
             const uint32_t st = g % NS;
             if (!mbar_wait_relaxed(smem_u32(&empty[st]), ((g / NS) & 1) ^ 1, abort_flag, p.status, kSleepTma)) {
               alive = false;
@@ -308,6 +335,20 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             }
             tma_load_3d(sa + L::kATile, &tm_hi, bar, k0, n0, 0);
             if (three) tma_load_3d(sa + L::kATile + L::kBTile, &tm_lo, bar, k0, n0, 0);
+            if (AUX && jj == aux_at) {
+              // the previous tile's epilogue has released the aux tile
+              if (!mbar_wait_relaxed(smem_u32(aux_empty), (ua & 1) ^ 1, abort_flag, p.status, kSleepTma)) {
+                alive = false;
+                break;
+              }
+              const uint32_t xb = smem_u32(aux_full);
+              mbar_arrive_tx(xb, (uint32_t)L::kAuxBytes);
+              const uint32_t sx = smem_u32(smem + L::kStageOff);
+#pragma unroll
+              for (int b = 0; b < BN / kBK; ++b)
+                tma_load_2d(sx + (uint32_t)(b * L::kAuxBox), &tm_x, xb, n0 + b * kBK, (int)m0);
+              ++ua;
+            }
           }
         }
       }
@@ -393,6 +434,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     const int cbase = half * HB;
     const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
     uint32_t ar = 0;
+    uint32_t ua = 0;  // AUX: aux tiles consumed
     bool ok = true;
     for (int64_t u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
       int64_t m0;
@@ -430,8 +472,18 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         if (lane == 0) mbar_arrive(smem_u32(&acce[buf]));
       }
       ok = __all_sync(0xffffffffu, ok && !*abort_flag);
-      tile_epilogue<BN, EPI>(p, acc, m0, n0, 0, c_off, warp, lane,
-                             reinterpret_cast<float*>(smem + L::kStageOff), ok);
+      if constexpr (AUX != 0) {
+        if (ok)
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait_relaxed(smem_u32(aux_full), ua & 1, abort_flag, p.status, kSleepAcc));
+        if (ok) tile_epilogue_aux<BN, EPI>(p, acc, m0, n0, warp, lane, smem_u32(smem + L::kStageOff));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(aux_empty));
+        ++ua;
+      } else {
+        tile_epilogue<BN, EPI>(p, acc, m0, n0, 0, c_off, warp, lane,
+                               reinterpret_cast<float*>(smem + L::kStageOff), ok);
+      }
     }
   }
 
@@ -479,11 +531,12 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_tiled() {
   return fn;
 }
 
-template <int BN, int EPI, int PASSES>
-bool launch_t(const ConvGemmParams& p, const void* tma, const void* tmh, const void* tml, cudaStream_t s) {
-  constexpr int NS = TmaConfig<BN>::NS;
-  auto kern = conv_gemm_tma_kernel<BN, NS, EPI, PASSES>;
-  constexpr int smem = TmaSmem<BN, NS>::kBytes;
+template <int BN, int EPI, int PASSES, int AUX>
+bool launch_t(const ConvGemmParams& p, const void* tma, const void* tmh, const void* tml, const void* tmx,
+              cudaStream_t s) {
+  constexpr int NS = AUX ? TmaConfig<BN>::NS_AUX : TmaConfig<BN>::NS;
+  auto kern = conv_gemm_tma_kernel<BN, NS, EPI, PASSES, AUX>;
+  constexpr int smem = TmaSmem<BN, NS, AUX>::kBytes;
   static_assert(smem <= 232448, "shared memory per CTA");
   static std::mutex mu;
   static uint64_t attr_devices = 0;
@@ -502,29 +555,67 @@ bool launch_t(const ConvGemmParams& p, const void* tma, const void* tmh, const v
   const int64_t units = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN) * std::max(1, p.ksplit);
   dim3 grid((unsigned)std::min<int64_t>(units, sms), 1, 1);
   kern<<<grid, kThreadsTC, smem, s>>>(p, *static_cast<const CUtensorMap*>(tma), *static_cast<const CUtensorMap*>(tmh),
-                                      *static_cast<const CUtensorMap*>(tml));
+                                      *static_cast<const CUtensorMap*>(tml), *static_cast<const CUtensorMap*>(tmx));
   return true;
 }
 
+// tmx: the aux operand's tensor map, or nullptr (the epilogue reads it from
+// global memory; the kernel's tm_x is then a copy of tm_a it never reads)
 template <int BN, int PASSES>
-bool launch_epi_p(const ConvGemmParams& p, const void* tma, const void* tmh, const void* tml, cudaStream_t s) {
+bool launch_epi_p(const ConvGemmParams& p, const void* tma, const void* tmh, const void* tml, const void* tmx,
+                  cudaStream_t s) {
   switch (p.epi) {
-    case EPI_NONE: return launch_t<BN, EPI_NONE, PASSES>(p, tma, tmh, tml, s);
-    case EPI_BIAS: return launch_t<BN, EPI_BIAS, PASSES>(p, tma, tmh, tml, s);
-    case EPI_BIAS_RELU: return launch_t<BN, EPI_BIAS_RELU, PASSES>(p, tma, tmh, tml, s);
-    case EPI_BIAS_ADD_RELU: return launch_t<BN, EPI_BIAS_ADD_RELU, PASSES>(p, tma, tmh, tml, s);
-    case EPI_PROGRAM: return launch_t<BN, EPI_PROGRAM, PASSES>(p, tma, tmh, tml, s);
-    case EPI_FAST: return launch_t<BN, EPI_FAST, PASSES>(p, tma, tmh, tml, s);
+    case EPI_NONE: return launch_t<BN, EPI_NONE, PASSES, 0>(p, tma, tmh, tml, tma, s);
+    case EPI_BIAS: return launch_t<BN, EPI_BIAS, PASSES, 0>(p, tma, tmh, tml, tma, s);
+    case EPI_BIAS_RELU: return launch_t<BN, EPI_BIAS_RELU, PASSES, 0>(p, tma, tmh, tml, tma, s);
+    case EPI_BIAS_ADD_RELU:
+      return tmx ? launch_t<BN, EPI_BIAS_ADD_RELU, PASSES, 1>(p, tma, tmh, tml, tmx, s)
+                 : launch_t<BN, EPI_BIAS_ADD_RELU, PASSES, 0>(p, tma, tmh, tml, tma, s);
+    case EPI_PROGRAM: return launch_t<BN, EPI_PROGRAM, PASSES, 0>(p, tma, tmh, tml, tma, s);
+    case EPI_FAST:
+      return tmx ? launch_t<BN, EPI_FAST, PASSES, 1>(p, tma, tmh, tml, tmx, s)
+                 : launch_t<BN, EPI_FAST, PASSES, 0>(p, tma, tmh, tml, tma, s);
     default: return false;
   }
 }
 
 template <int BN>
-bool launch_epi(const ConvGemmParams& p, const void* tma, const void* tmh, const void* tml, cudaStream_t s) {
-  return p.passes == 1 ? launch_epi_p<BN, 1>(p, tma, tmh, tml, s) : launch_epi_p<BN, 3>(p, tma, tmh, tml, s);
+bool launch_epi(const ConvGemmParams& p, const void* tma, const void* tmh, const void* tml, const void* tmx,
+                cudaStream_t s) {
+  return p.passes == 1 ? launch_epi_p<BN, 1>(p, tma, tmh, tml, tmx, s) : launch_epi_p<BN, 3>(p, tma, tmh, tml, tmx, s);
+}
+
+// The aux operand of an unsplit launch as a tiled map over [M][N] (row
+// stride ld), when the epilogue can take it from shared memory: the
+// residual of EPI_BIAS_ADD_RELU, or the single aux tensor of an EPI_FAST
+// form (FAST_SIGMOID_MUL when both of its operands are the same tensor);
+// rows 16-byte aligned, unit column stride, and an output the epilogue
+// stores in float4 rows.
+bool make_aux_tensor_map(const ConvGemmParams& p, CUtensorMap* out) {
+  if (p.ksplit > 1 || p.nb != 1 || p.ldc_n != 1 || p.ldc % 4 != 0 || (reinterpret_cast<uintptr_t>(p.out) & 15))
+    return false;
+  const float* src = nullptr;
+  int64_t ld = 0;
+  if (p.epi == EPI_BIAS_ADD_RELU && p.bias && p.res) {
+    src = p.res;
+    ld = p.ldc;
+  } else if (p.epi == EPI_FAST && !p.bias && p.n_aux >= 1 && p.aux_sn[0] == 1 &&
+             (p.fast == FAST_ADD || p.fast == FAST_DIVC_ADD || p.fast == FAST_MULC_ADD ||
+              (p.fast == FAST_SIGMOID_MUL && p.n_aux >= 2 && p.aux[1] == p.aux[0] && p.aux_sm[1] == p.aux_sm[0] &&
+               p.aux_sn[1] == 1))) {
+    src = p.aux[0];
+    ld = p.aux_sm[0];
+  }
+  if (!src || ld < p.N) return false;
+  return make_a_tensor_map_2d(src, p.M, p.N, ld, out);
 }
 
 }  // namespace
+
+bool conv_gemm_tma_aux_ok(const ConvGemmParams& p) {
+  CUtensorMap m;
+  return make_aux_tensor_map(p, &m);
+}
 
 int conv_gemm_tma_smem_bytes(int block_n) {
   return block_n == 64 ? TmaSmem<64, TmaConfig<64>::NS>::kBytes : TmaSmem<128, TmaConfig<128>::NS>::kBytes;
@@ -600,9 +691,11 @@ bool launch_conv_gemm_tma(const ConvGemmParams& p_in, const void* tmap_a, const 
   }
   const int64_t units = ((p.M + kBM - 1) / kBM) * ((p.N + block_n - 1) / block_n) * p.ksplit;
   if (p.M >= (int64_t(1) << 31) || units >= (int64_t(1) << 31) || p.P * p.Q >= (int64_t(1) << 31)) return false;
+  CUtensorMap xmap;
+  const void* tmap_x = p.aux_tma && make_aux_tensor_map(p, &xmap) ? &xmap : nullptr;
   bool ok = false;
-  if (block_n == 64) ok = launch_epi<64>(p, tmap_a, tmap_hi, tmap_lo, s);
-  else if (block_n == 128) ok = launch_epi<128>(p, tmap_a, tmap_hi, tmap_lo, s);
+  if (block_n == 64) ok = launch_epi<64>(p, tmap_a, tmap_hi, tmap_lo, tmap_x, s);
+  else if (block_n == 128) ok = launch_epi<128>(p, tmap_a, tmap_hi, tmap_lo, tmap_x, s);
   if (!ok) return false;
   if (p.ksplit > 1) launch_splitk_reduce(p_in, p.split_stride, s);
   return true;

@@ -325,6 +325,11 @@ struct ConvGemmParams {
   // hi*hi + hi*lo + lo*hi; the default, also for 0) or 1 (one TF32 product
   // of the truncated operands: the single-pass TF32 precision mode).
   int passes;
+  // launch_conv_gemm_tma only: nonzero lets the epilogue's aux operand (the
+  // residual, or an EPI_FAST operand) come per tile through shared memory by
+  // TMA when conv_gemm_tma_aux_ok accepts the launch; 0 reads it from global
+  // memory in the epilogue.  Same results either way.
+  int aux_tma;
 };
 
 enum ATma : int {
@@ -406,6 +411,11 @@ bool make_a_tensor_map_im2col(const float* x, int64_t images, int64_t H, int64_t
                               int dw, void* tmap_out, int* mode);
 bool make_a_tensor_map_2d(const float* x, int64_t M, int64_t K, int64_t ld, void* tmap_out);
 int conv_gemm_tma_smem_bytes(int block_n);
+// Whether launch_conv_gemm_tma can stage this launch's epilogue operand in
+// shared memory: an unsplit launch, EPI_BIAS_ADD_RELU (the residual) or an
+// EPI_FAST form with one distinct aux tensor, that operand a row-major
+// [M][N] view with 16-byte aligned rows, and the output in float4 rows.
+bool conv_gemm_tma_aux_ok(const ConvGemmParams& p);
 
 // Build the TMA descriptors for packed B planes [batch][N][ldk] (fp32).
 bool make_b_tensor_maps(const float* hi, const float* lo, int64_t batch, int64_t N, int64_t ldk, int block_n,

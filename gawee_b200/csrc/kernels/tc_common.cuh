@@ -520,6 +520,97 @@ __device__ __forceinline__ void tile_epilogue(const ConvGemmParams& p, float (&a
   }
 }
 
+__device__ __forceinline__ void sts128(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+
+// Epilogue of one unsplit output tile whose aux operand is already in shared
+// memory (`tile`: the residual of EPI_BIAS_ADD_RELU, or aux 0 of EPI_FAST,
+// loaded by TMA as BN / 32 boxes of [128 rows][32 columns], box b 16 KB at
+// b * 16 KB, 128-byte swizzled: 16-byte chunk c of row r at chunk c ^ (r & 7),
+// zero past M and N).  Same warps, operations and order as tile_epilogue;
+// each thread reads its row's aux values, writes its results over them, and
+// the warp stores its 32 rows 8 at a time (4 lanes x 16 bytes per row) --
+// both shared-memory patterns cover the 8 chunk positions of a 128-byte row
+// evenly, so neither has bank conflicts.  Columns past N and rows past M are
+// computed but not stored.
+template <int BN, int EPI>
+__device__ __forceinline__ void tile_epilogue_aux(const ConvGemmParams& p, float (&acc)[BN / 2], int64_t m0, int n0,
+                                                  int warp, int lane, uint32_t tile) {
+  static_assert(EPI == EPI_FAST || EPI == EPI_BIAS_ADD_RELU, "aux epilogue forms");
+  constexpr int HB = BN / 2;
+  const int q = warp & 3;
+  const int cbase = ((warp - 6) / 4) * HB;
+  const int row = q * 32 + lane;
+  // shared-memory address of 16-byte chunk `ch` (4 columns, 0 .. BN / 4 - 1) of tile row r
+  auto chunk = [tile](int r, int ch) -> uint32_t {
+    return tile + (uint32_t)((ch >> 3) * (kBM * kBK * 4) + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
+  };
+  const int c4 = lane & 3;
+#pragma unroll
+  for (int c0 = 0; c0 < HB; c0 += 16) {
+    const int ch0 = (cbase + c0) >> 2;
+    float a[16];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 v = lds128(chunk(row, ch0 + j));
+      a[4 * j] = v.x; a[4 * j + 1] = v.y; a[4 * j + 2] = v.z; a[4 * j + 3] = v.w;
+    }
+    float o[16];
+    // one loop per form: a form chosen per element would have the compiler
+    // evaluate the IEEE division for every element of every form
+    if (EPI == EPI_BIAS_ADD_RELU) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int n = n0 + cbase + c0 + j;
+        const float x = __fadd_rn(__fadd_rn(acc[c0 + j], n < p.N ? __ldg(p.bias + n) : 0.f), a[j]);
+        o[j] = maximumf_(x, 0.0f);
+      }
+    } else if (p.fast == FAST_ADD) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) o[j] = __fadd_rn(acc[c0 + j], a[j]);
+    } else if (p.fast == FAST_DIVC_ADD) {
+      const float c = p.fast_c;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) o[j] = __fadd_rn(__fdiv_rn(acc[c0 + j], c), a[j]);
+    } else if (p.fast == FAST_MULC_ADD) {
+      const float c = p.fast_c;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) o[j] = __fadd_rn(__fmul_rn(acc[c0 + j], c), a[j]);
+    } else {  // FAST_SIGMOID_MUL with both operands the aux tile
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-a[j])));
+        o[j] = __fmul_rn(__fmul_rn(a[j], sg), acc[c0 + j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) sts128(chunk(row, ch0 + j), o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+    __syncwarp();
+    const int n = n0 + cbase + c0 + c4 * 4;
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int r = q * 32 + it * 8 + (lane >> 2);
+      const int64_t m = m0 + r;
+      const float4 v = lds128(chunk(r, ch0 + c4));
+      if (m < p.M && n < p.N) {
+        float* cp = p.out + m * p.ldc + n;
+        if (n + 3 < p.N) {
+          *reinterpret_cast<float4*>(cp) = v;
+        } else {
+          const float x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (n + e < p.N) cp[e] = x[e];
+        }
+      }
+    }
+  }
+  // the tile was written through the generic proxy; the next TMA load into
+  // it comes through the async proxy
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 }  // namespace
 }  // namespace kern
 }  // namespace gawee

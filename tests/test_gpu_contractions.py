@@ -298,3 +298,70 @@ def test_batched_lhs_rows_merge_into_one_gemm():
     for o in outs:
         for k in range(2):
             compare(o[k], want[k], 2e-4, 1e-4, f"output{k}")
+
+
+AUX_GEMMS = [
+    # (m, k, n, epilogue): the TMA kernel stages the epilogue's operand tile in shared memory
+    (300, 576, 200, "add"),       # partial M and N tiles; the tile loaded mid-unit (18 k-blocks)
+    (9000, 64, 576, "add"),       # 2 k-blocks: loaded with the unit's first; 2-3 tiles per CTA
+    (12800, 576, 512, "swiglu"),  # (gate * sigmoid(gate)) * up, one operand tile; 2-3 tiles per CTA
+    (517, 320, 64, "divc"),       # BN 64; (acc / 6.93) + r, the IEEE division
+    (260, 96, 40, "mulc"),        # BN 64, partial N; (acc / 8) + r as an exact multiply
+]
+
+
+@pytest.mark.parametrize("m,k,n,epi", AUX_GEMMS)
+def test_gemm_aux_staged_epilogue_matches_oracle_and_global_reads(m, k, n, epi):
+    """The residual / fast-epilogue operand through a TMA-staged shared-memory
+    tile (GAWEE_TC_TMA_AUX=1): the oracle's values, and bit for bit the
+    epilogue that reads the operand from global memory (GAWEE_TC_TMA_AUX=0)."""
+    import oracle
+
+    def g_(g):
+        a = rand_input(g, (m, k), 71)
+        y = g.matmul(a, rand_input(g, (k, n), 72))
+        if epi == "swiglu":
+            gate = g.matmul(a, rand_input(g, (k, n), 73))
+            return [g.mul(g.mul(gate, g.sigmoid(gate)), y)]
+        r = rand_input(g, (m, n), 74)
+        if epi == "divc":
+            y = g.div(y, g.const(6.928203230275509, F))
+        elif epi == "mulc":
+            y = g.div(y, g.const(8.0, F))
+        return [g.add(y, r)]
+    mlir, args = build(g_)
+    want = oracle.run(mlir, args)[0]
+    names, outs = _run_env(mlir, args, {"GAWEE_MAX_KSPLIT": 1, "GAWEE_TC_TMA_AUX": 1})
+    names_g, outs_g = _run_env(mlir, args, {"GAWEE_MAX_KSPLIT": 1, "GAWEE_TC_TMA_AUX": 0})
+    assert any("[tma]" in nm and "[aux smem]" in nm for nm in names), names
+    assert not any("[aux smem]" in nm for nm in names_g), names_g
+    for o in outs:
+        compare(o[0], want, 2e-4 * max(1.0, math.sqrt(k) / 8), 1e-4, epi)
+        np.testing.assert_array_equal(o[0], outs_g[0][0])
+
+
+@pytest.mark.parametrize("f", [64, 128])
+def test_conv_residual_aux_staged_matches_oracle_and_global_reads(f):
+    """A residual block on the im2col TMA kernel (BN 64 and 128): the
+    residual tile staged in shared memory gives the oracle's values and the
+    same bits as the epilogue's global reads."""
+    import oracle
+
+    def g_(g):
+        x = g.relu(rand_input(g, (3, f, 17, 15), 81))
+        att = {"strides": _arr([1, 1]), "padding": _arr([1, 1]), "dilation": _arr([1, 1])}
+        w1 = rand_input(g, (f, f, 3, 3), 82, scale=float(np.sqrt(2.0 / (9 * f))))
+        w2 = rand_input(g, (f, f, 3, 3), 83, scale=float(np.sqrt(2.0 / (9 * f))))
+        b1, b2 = rand_input(g, (f,), 84, scale=0.1), rand_input(g, (f,), 85, scale=0.1)
+        y = g.relu(g.op("conv", [x, w1, b1], att, F, (3, f, 17, 15)))
+        y = g.op("conv", [y, w2, b2], att, F, (3, f, 17, 15))
+        return [g.relu(g.add(y, x))]
+    mlir, args = build(g_)
+    want = oracle.run(mlir, args)[0]
+    names, outs = _run_env(mlir, args, {"GAWEE_MAX_KSPLIT": 1, "GAWEE_TC_TMA_AUX": 1})
+    names_g, outs_g = _run_env(mlir, args, {"GAWEE_MAX_KSPLIT": 1, "GAWEE_TC_TMA_AUX": 0})
+    assert any("conv+add+relu [tma im2col] [aux smem]" in nm for nm in names), names
+    assert not any("[aux smem]" in nm for nm in names_g), names_g
+    for o in outs:
+        compare(o[0], want, 1e-4, 1e-4, "residual block")
+        np.testing.assert_array_equal(o[0], outs_g[0][0])

@@ -228,10 +228,10 @@ void Runtime::build_tensor_maps() {
   // GAWEE_TC_TMA=0 keeps every contraction on the warp-gather kernel
   bool use_tma = true;
   if (const char* e = std::getenv("GAWEE_TC_TMA")) use_tma = std::atoi(e) != 0;
-  // GAWEE_TC_TMA_AUX=1 has the TMA kernel stage its epilogue's residual or
-  // fast-epilogue operand in shared memory by TMA; 0 reads it from global
-  // memory in the epilogue
-  bool use_aux = false;
+  // The TMA kernel stages its epilogue's residual or fast-epilogue operand in
+  // shared memory by TMA where the layout allows; GAWEE_TC_TMA_AUX=0 has the
+  // epilogue read it from global memory instead (the same bits, slower)
+  bool use_aux = true;
   if (const char* e = std::getenv("GAWEE_TC_TMA_AUX")) use_aux = std::atoi(e) != 0;
   int sms = 0;
   GCHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));

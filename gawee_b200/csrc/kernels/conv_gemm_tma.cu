@@ -119,10 +119,12 @@ constexpr unsigned kSleepA = 64, kSleepTma = 32, kSleepAcc = 256;
 
 // AUX: the epilogue's aux operand (the residual of EPI_BIAS_ADD_RELU, or
 // aux 0 of EPI_FAST) is loaded per tile by the TMA warp through tm_x into
-// shared memory, 2 * NS k-blocks before the tile's last, instead of being
-// read from global memory by the accumulator warps after the tile's last
-// round (which held the MMA issuer up once it ran out of drained
-// accumulators).  Only unsplit launches (ksplit 1) use it.
+// shared memory while the tile's rounds run, instead of being read from
+// global memory by the accumulator warps after the tile's last round (which
+// held the MMA issuer up once it ran out of drained accumulators); for
+// FAST_SIGMOID_MUL the accumulator warps also form aux * sigmoid(aux) in
+// place between the last round drains.  Only unsplit launches (ksplit 1)
+// use it.
 template <int BN, int NS, int EPI, int PASSES, int AUX>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     conv_gemm_tma_kernel(const __grid_constant__ ConvGemmParams p, const __grid_constant__ CUtensorMap tm_a,
@@ -286,8 +288,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       const int C = (int)p.C, S = p.S;
       const uint32_t PQ = (uint32_t)(p.P * p.Q), Q = (uint32_t)p.Q;
       // AUX: the unit-local k-block after whose loads the aux tile is loaded
-      // (an unsplit unit covers all num_kb k-blocks)
-      const int aux_at = max(0, num_kb - 2 * NS);
+      // (an unsplit unit covers all num_kb k-blocks): late enough that the
+      // previous tile's epilogue has released it, early enough that it lands
+      // while the tile's last rounds are still to come
+      const int aux_at = max(0, min(num_kb - 2 * NS, 3 * NS));
       uint32_t g = 0;
       uint32_t ua = 0;  // aux tiles loaded
       bool alive = true;
@@ -444,6 +448,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       float acc[HB];
 #pragma unroll
       for (int j = 0; j < HB; ++j) acc[j] = 0.0f;
+      int pre = 0;  // FAST_SIGMOID_MUL: 16-column chunks of the aux row already aux * sigmoid(aux)
       for (int r = 0; r < nr; ++r, ++ar) {
         const uint32_t buf = ar & 1;
         if (!__all_sync(0xffffffffu,
@@ -470,13 +475,23 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&acce[buf]));
+        if constexpr (AUX != 0 && EPI == EPI_FAST) {
+          // one chunk after each of the last rounds but the final one, once
+          // the aux tile has landed (tested without waiting): the tensor core
+          // has two rounds of work queued meanwhile
+          if (p.fast == FAST_SIGMOID_MUL && r + 1 < nr && r + 1 + (HB / 16) >= nr && pre < HB / 16 &&
+              __all_sync(0xffffffffu, mbar_test(smem_u32(aux_full), ua & 1))) {
+            aux_sigmoid_chunk<BN>(smem_u32(smem + L::kStageOff), warp, lane, pre);
+            ++pre;
+          }
+        }
       }
       ok = __all_sync(0xffffffffu, ok && !*abort_flag);
       if constexpr (AUX != 0) {
         if (ok)
           ok = __all_sync(0xffffffffu,
                           mbar_wait_relaxed(smem_u32(aux_full), ua & 1, abort_flag, p.status, kSleepAcc));
-        if (ok) tile_epilogue_aux<BN, EPI>(p, acc, m0, n0, warp, lane, smem_u32(smem + L::kStageOff));
+        if (ok) tile_epilogue_aux<BN, EPI>(p, acc, m0, n0, warp, lane, smem_u32(smem + L::kStageOff), pre);
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(aux_empty));
         ++ua;

@@ -62,6 +62,19 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of a phase (test_wait never suspends the thread).
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait: returns false if the CTA is aborting or the wait timed out.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status) {
   if (mbar_try(bar, parity)) return true;
@@ -524,11 +537,41 @@ __device__ __forceinline__ void sts128(uint32_t addr, float a, float b, float c,
   asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }
 
+// Shared-memory address of 16-byte chunk `ch` (4 columns, 0 .. BN / 4 - 1) of
+// row r of a staged aux tile: BN / 32 boxes of [128 rows][32 columns], box b
+// 16 KB at b * 16 KB, 128-byte swizzled (chunk c of row r at c ^ (r & 7)).
+__device__ __forceinline__ uint32_t aux_chunk(uint32_t tile, int r, int ch) {
+  return tile + (uint32_t)((ch >> 3) * (kBM * kBK * 4) + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
+}
+
+// FAST_SIGMOID_MUL, ahead of the epilogue: 16-column chunk i of this
+// thread's half row of the staged aux tile becomes aux * (1 / (1 + exp(-aux)))
+// in place -- the epilogue's first product, which does not involve the
+// accumulator -- so the epilogue that follows only multiplies by it.  The
+// accumulator warps call it between round drains, while the tensor core
+// works on the tile's remaining rounds.
+template <int BN>
+__device__ __forceinline__ void aux_sigmoid_chunk(uint32_t tile, int warp, int lane, int i) {
+  constexpr int HB = BN / 2;
+  const int row = (warp & 3) * 32 + lane;
+  const int ch0 = (((warp - 6) / 4) * HB + i * 16) >> 2;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t addr = aux_chunk(tile, row, ch0 + j);
+    const float4 v = lds128(addr);
+    const float a[4] = {v.x, v.y, v.z, v.w};
+    float t[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) t[e] = __fmul_rn(a[e], __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-a[e]))));
+    sts128(addr, t[0], t[1], t[2], t[3]);
+  }
+}
+
 // Epilogue of one unsplit output tile whose aux operand is already in shared
 // memory (`tile`: the residual of EPI_BIAS_ADD_RELU, or aux 0 of EPI_FAST,
-// loaded by TMA as BN / 32 boxes of [128 rows][32 columns], box b 16 KB at
-// b * 16 KB, 128-byte swizzled: 16-byte chunk c of row r at chunk c ^ (r & 7),
-// zero past M and N).  Same warps, operations and order as tile_epilogue;
+// laid out as aux_chunk describes, zero past M and N; for FAST_SIGMOID_MUL
+// this thread's first `pre` 16-column chunks already hold aux * sigmoid(aux),
+// from aux_sigmoid_chunk).  Same warps, operations and order as tile_epilogue;
 // each thread reads its row's aux values, writes its results over them, and
 // the warp stores its 32 rows 8 at a time (4 lanes x 16 bytes per row) --
 // both shared-memory patterns cover the 8 chunk positions of a 128-byte row
@@ -536,16 +579,13 @@ __device__ __forceinline__ void sts128(uint32_t addr, float a, float b, float c,
 // computed but not stored.
 template <int BN, int EPI>
 __device__ __forceinline__ void tile_epilogue_aux(const ConvGemmParams& p, float (&acc)[BN / 2], int64_t m0, int n0,
-                                                  int warp, int lane, uint32_t tile) {
+                                                  int warp, int lane, uint32_t tile, int pre) {
   static_assert(EPI == EPI_FAST || EPI == EPI_BIAS_ADD_RELU, "aux epilogue forms");
   constexpr int HB = BN / 2;
   const int q = warp & 3;
   const int cbase = ((warp - 6) / 4) * HB;
   const int row = q * 32 + lane;
-  // shared-memory address of 16-byte chunk `ch` (4 columns, 0 .. BN / 4 - 1) of tile row r
-  auto chunk = [tile](int r, int ch) -> uint32_t {
-    return tile + (uint32_t)((ch >> 3) * (kBM * kBK * 4) + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
-  };
+  auto chunk = [tile](int r, int ch) -> uint32_t { return aux_chunk(tile, r, ch); };
   const int c4 = lane & 3;
 #pragma unroll
   for (int c0 = 0; c0 < HB; c0 += 16) {
@@ -577,6 +617,9 @@ __device__ __forceinline__ void tile_epilogue_aux(const ConvGemmParams& p, float
       const float c = p.fast_c;
 #pragma unroll
       for (int j = 0; j < 16; ++j) o[j] = __fadd_rn(__fmul_rn(acc[c0 + j], c), a[j]);
+    } else if (c0 / 16 < pre) {  // FAST_SIGMOID_MUL, the chunk already aux * sigmoid(aux)
+#pragma unroll
+      for (int j = 0; j < 16; ++j) o[j] = __fmul_rn(a[j], acc[c0 + j]);
     } else {  // FAST_SIGMOID_MUL with both operands the aux tile
 #pragma unroll
       for (int j = 0; j < 16; ++j) {

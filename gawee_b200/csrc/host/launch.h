@@ -17,6 +17,7 @@ struct PackSpec {
   View src;
   int64_t batch = 1, K = 0, N = 0;
   int64_t sn = 0;
+  int64_t row_off = 0;  // first plane row written (several operands packed into one pair of planes)
   std::vector<int64_t> k_shape, k_st, k_valid;
   std::vector<int64_t> batch_shape, batch_st;
 };

@@ -3,6 +3,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <limits>
 #include <map>
@@ -131,6 +132,7 @@ class Planner {
     find_attention_clusters();
     find_norm_clusters();
     find_rope_clusters();
+    find_merged_matmuls();
     for (size_t n = 0; n < g.nodes.size(); ++n) {
       if (skip_node_.count((int)n)) continue;  // folded into a fused op
       try {
@@ -147,6 +149,11 @@ class Planner {
         auto rt = rope_at_.find((int)n);
         if (rt != rope_at_.end()) {
           plan_rope(rt->second);
+          continue;
+        }
+        auto mt = merge_at_.find((int)n);
+        if (mt != merge_at_.end()) {
+          plan_matmul_merged(mt->second);
           continue;
         }
         plan_node(g.nodes[n]);
@@ -1473,6 +1480,141 @@ class Planner {
     op.writes = {out};
     add_op(std::move(op));
     set_view(n.outs[0], out);
+  }
+
+  // ---------------------------------------------------------------- merged contractions
+  // Matmuls that share their left operand (the same value) and whose right
+  // operands are 2-D arguments or constants -- the Q, K and V projections of
+  // an attention block -- run as one GEMM over the concatenated weights: A is
+  // read once and the N = 192 projections of a GQA block stop wasting half a
+  // 128-wide tile.  Each result is a column slice of the shared output, so
+  // only results that feed views (reshape, transpose) are merged: a result
+  // feeding an elementwise op keeps its own GEMM and the fused epilogue.
+  // GAWEE_MERGE_GEMMS=0 turns the merge off.
+  std::map<int, std::vector<int>> merge_at_;  // first matmul node -> the group's nodes, in order
+
+  void find_merged_matmuls() {
+    if (const char* e = std::getenv("GAWEE_MERGE_GEMMS"))
+      if (std::atoi(e) == 0) return;
+    Graph& g = plan_->g;
+    std::vector<std::vector<int>> consumers(g.values.size());
+    for (size_t k = 0; k < g.nodes.size(); ++k)
+      for (int v : g.nodes[k].ins) consumers[v].push_back((int)k);
+    std::set<int> results(g.results.begin(), g.results.end());
+    std::map<int, std::vector<int>> by_lhs;  // lhs value -> candidate nodes
+    for (size_t k = 0; k < g.nodes.size(); ++k) {
+      const Node& n = g.nodes[k];
+      if (n.op != "gawee.matmul" || n.ins.size() != 2 || n.outs.size() != 1) continue;
+      if (skip_node_.count((int)k) || attn_at_.count((int)k) || norm_at_.count((int)k) || rope_at_.count((int)k))
+        continue;
+      const Value& a = val(n.ins[0]);
+      const Value& b = val(n.ins[1]);
+      const Value& o = val(n.outs[0]);
+      if (!a.type.is_tensor || !b.type.is_tensor || b.type.shape.size() != 2 || a.type.shape.size() < 2) continue;
+      if (b.def_node >= 0) continue;  // weights: function arguments or constants
+      if (o.type.dtype != DType::F32 || a.type.dtype != DType::F32 || b.type.dtype != DType::F32) continue;
+      if (b.type.shape[1] % 4 != 0 || results.count(n.outs[0])) continue;
+      bool views_only = !consumers[n.outs[0]].empty();
+      for (int c : consumers[n.outs[0]])
+        if (g.nodes[c].op != "gawee.reshape" && g.nodes[c].op != "gawee.transpose") views_only = false;
+      if (!views_only) continue;
+      by_lhs[n.ins[0]].push_back((int)k);
+    }
+    for (auto& [lhs, nodes] : by_lhs) {
+      (void)lhs;
+      if (nodes.size() < 2) continue;
+      merge_at_[nodes[0]] = nodes;
+      for (size_t i = 1; i < nodes.size(); ++i) skip_node_.insert(nodes[i]);
+    }
+  }
+
+  void plan_matmul_merged(const std::vector<int>& nodes) {  // GaweeToLinalg.cpp:959-1112, per member
+    Graph& g = plan_->g;
+    const Node& n0 = g.nodes[nodes[0]];
+    View lhs = value_view(n0.ins[0]);
+    const int ra = lhs.rank();
+    const int64_t M = lhs.shape[ra - 2], K = lhs.shape[ra - 1];
+    std::vector<int64_t> widths;
+    int64_t Ntot = 0;
+    for (int k : nodes) {
+      const View rhs = value_view(g.nodes[k].ins[1]);
+      if (rhs.rank() != 2 || rhs.shape[0] != K) unsupported("merged matmul operands");
+      widths.push_back(rhs.shape[1]);
+      Ntot += rhs.shape[1];
+    }
+    const int64_t ldk = round_up(K, 4);
+    const int hi = new_buf(DType::F32, Ntot * ldk);
+    const int lo = new_buf(DType::F32, Ntot * ldk);
+    int64_t row = 0;
+    for (size_t i = 0; i < nodes.size(); ++i) {
+      const View rhs = value_view(g.nodes[nodes[i]].ins[1]);
+      PackSpec ps;
+      ps.src = rhs;
+      ps.K = K;
+      ps.N = widths[i];
+      ps.sn = rhs.st[1];
+      ps.k_shape = {K};
+      ps.k_st = {rhs.st[0]};
+      ps.k_valid = {K};
+      ps.batch = 1;
+      ps.row_off = row;
+      row += widths[i];
+      Op op;
+      op.kind = OpKind::PACK;
+      op.name = "pack_matmul_b";
+      op.reads = {rhs};
+      op.writes = {dense_view(hi, DType::F32, {Ntot * ldk}), dense_view(lo, DType::F32, {Ntot * ldk})};
+      op.launch = launch::pack(ps, ldk, hi, lo);
+      add_op(std::move(op));
+    }
+    const Value& o0 = val(n0.outs[0]);
+    std::vector<int64_t> oshape = o0.type.shape;
+    oshape.back() = Ntot;
+    const int br = (int)oshape.size() - 2;
+    if (br > 4) unsupported("matmul with more than 4 batch dims");
+    View a = gemm_operand_a(lhs);
+    std::vector<int64_t> a_bst(br, 0), b_bst(br, 0);
+    const int la = br - (ra - 2);
+    for (int d = 0; d < br; ++d) {
+      const int ia = d - la;
+      if (ia >= 0 && a.shape[ia] != 1) a_bst[d] = a.st[ia];
+    }
+    View out = alloc(DType::F32, oshape);
+    Op op;
+    op.kind = OpKind::TC;
+    op.name = "matmul" + std::to_string(nodes.size());
+    auto& t = op.tc;
+    t.x = a;
+    t.out = out;
+    t.hi = hi;
+    t.lo = lo;
+    t.b_batch = 1;
+    t.ldk = ldk;
+    t.H = M; t.W = 1; t.C = round_up(K, 4); t.P = M; t.Q = 1;
+    t.M = M; t.N = Ntot; t.K = K;
+    t.block_n = pick_block_n(Ntot);
+    t.epi = kern::EPI_NONE;
+    t.batch_rank = br;
+    t.batch_shape.assign(oshape.begin(), oshape.begin() + br);
+    t.a_bst = a_bst;
+    t.b_bst = b_bst;
+    {
+      double nbt = 1;
+      for (auto d : t.batch_shape) nbt *= (double)d;
+      t.flops = 2.0 * nbt * (double)M * (double)Ntot * (double)K;
+    }
+    op.reads = {a, dense_view(hi, DType::F32, {1}), dense_view(lo, DType::F32, {1})};
+    op.writes = {out};
+    add_op(std::move(op));
+    // each member's result: its column slice of the shared output
+    int64_t col = 0;
+    for (size_t i = 0; i < nodes.size(); ++i) {
+      View v = out;
+      v.shape.back() = widths[i];
+      v.off += col;
+      col += widths[i];
+      set_view(g.nodes[nodes[i]].outs[0], v);
+    }
   }
 
   // ---------------------------------------------------------------- reductions / pools

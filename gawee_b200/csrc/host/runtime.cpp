@@ -920,10 +920,11 @@ Fn pack(const PackSpec& ps, int64_t ldk, int hi, int lo) {
     pp.batch_st[d] = ps.batch_st[d];
   }
   View src = ps.src;
-  return [pp, src, hi, lo](Runtime& rt, void* s) mutable {
+  const int64_t off = ps.row_off * ldk;
+  return [pp, src, hi, lo, off](Runtime& rt, void* s) mutable {
     pp.src = reinterpret_cast<const float*>(rt.ptr(src));
-    pp.hi = static_cast<float*>(rt.plan->bufs[hi].ptr);
-    pp.lo = static_cast<float*>(rt.plan->bufs[lo].ptr);
+    pp.hi = static_cast<float*>(rt.plan->bufs[hi].ptr) + off;
+    pp.lo = static_cast<float*>(rt.plan->bufs[lo].ptr) + off;
     kern::launch_pack_b(pp, static_cast<cudaStream_t>(s));
   };
 }

@@ -79,6 +79,24 @@ def test_gqa_decoder_reduced():
     _check(synth.llama(2, 64, dim=576, layers=2, heads=9, kv_heads=3, ffn=1536, vocab=4096, name="decoder135m_l2"))
 
 
+@pytest.mark.parametrize("decode", [False, True])
+def test_merged_qkv_projection_matches_oracle_merged_and_not(decode, monkeypatch):
+    """The Q, K and V projections of each layer as one GEMM over the
+    concatenated weights (6 query and 2 key/value heads of 16: N = 96 + 32 +
+    32 = 160, a ragged second tile; K and V read as column slices by RoPE,
+    the KV-cache concat and attention): the oracle's values with the merge
+    and without it (GAWEE_MERGE_GEMMS=0)."""
+    kw = dict(dim=96, layers=2, heads=6, kv_heads=2, ffn=128, vocab=300)
+    g = synth.llama_decode(2, 37, name="gqa_small_decode", **kw) if decode else \
+        synth.llama(2, 40, name="gqa_small", **kw)
+    from gawee_b200.runtime import plan_text
+    assert plan_text(g.mlir).count("matmul3") == 2
+    _check(g)
+    monkeypatch.setenv("GAWEE_MERGE_GEMMS", "0")
+    assert "matmul3" not in plan_text(g.mlir)
+    _check(g)
+
+
 @pytest.mark.parametrize("past", [1, 255])
 def test_llama15m_decode_step(past):
     """A KV-cache decode step with the reference tinyllama binding's inputs

@@ -140,6 +140,31 @@ def test_plan_decode_step():
     assert len(g.out_shapes) == 13 and g.out_shapes[1] == (1, 6, 256, 48)
 
 
+def test_plan_merges_projections_that_share_their_input(monkeypatch):
+    # Q, K and V projections of one input (weights are arguments, results feed
+    # reshapes) run as one GEMM; a projection feeding an elementwise op keeps
+    # its own GEMM so the op stays fused into its epilogue; GAWEE_MERGE_GEMMS=0
+    # keeps every projection separate
+    from tests.helpers import build, rand_input
+
+    def g_(g):
+        x = rand_input(g, (2, 37, 64), 1)
+        q, k, v = (g.matmul(x, rand_input(g, (64, n), 2 + i)) for i, n in enumerate((96, 32, 32)))
+        outs = [g.transpose(g.reshape(t, (2, 37, t.shape[-1] // 16, 16)), [0, 2, 1, 3]) for t in (q, k, v)]
+        gate = g.matmul(x, rand_input(g, (64, 48), 6))
+        up = g.matmul(x, rand_input(g, (64, 48), 7))
+        return outs + [g.mul(g.mul(gate, g.sigmoid(gate)), up)]
+    mlir = build(g_)[0]
+    s = _plan(mlir)
+    assert s.count("matmul3") == 1 and "reshape_copy" not in s, s
+    assert s.count("matmul+sigmoid+mul+mul") == 1, s  # gate and up stay apart: the product is fused
+    assert "matmul3" in _plan(synth.llama15m().mlir) and "matmul3" in _plan(synth.llama15m_decode(1, 1).mlir)
+    assert "matmul3" not in _plan(synth.bert_tiny().mlir)  # its projections' bias adds are epilogues
+    monkeypatch.setenv("GAWEE_MERGE_GEMMS", "0")
+    s = _plan(mlir)
+    assert "matmul3" not in s and s.count("matmul\n") >= 4, s
+
+
 def test_plan_memory_reuse():
     g = synth.resnet18(256)
     s = _plan(g.mlir)

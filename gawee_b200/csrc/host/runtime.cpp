@@ -109,6 +109,13 @@ struct Runtime {
   std::vector<int> a_tma;                  // per op (TC only): kern::ATma, A_TMA_NONE = warp gather
   int tma_rk = kern::kRK;                  // TMA kernel: k-blocks per promotion round
   int passes = 3;                          // tensor-core passes per product (precision mode: 3 fp32, 1 tf32)
+  // BF16 mode: TMA-kernel contractions in bf16 from a bf16 copy of their B
+  // planes (the other tensor-core kernels run single-pass TF32, passes 1)
+  bool bf16 = false;
+  std::vector<void*> bf16_plane;           // per op (TMA-kernel TC ops): [b_batch * N][bf16_ldk] bf16
+  std::vector<TMap> bf16_map;              // per op: its tensor map
+  std::vector<int64_t> bf16_ldk;           // per op: row pitch, a multiple of 8
+  std::vector<char> bf16_fresh;            // per op: the plane matches the packed planes
   std::vector<int> ksplit;                 // per op (TC only): k splits, 1 = none
   std::vector<char> aux_tma;               // per op (TC only): epilogue operand staged by TMA (TMA kernel)
   std::vector<uint8_t*> attn_skip;         // per op (ATTN only): skip flags of the mask tiles
@@ -138,11 +145,14 @@ struct Runtime {
     if (splitk_ws) cudaFree(splitk_ws);
     for (uint8_t* f : attn_skip)
       if (f) cudaFree(f);
+    for (void* b : bf16_plane)
+      if (b) cudaFree(b);
     if (own_stream) cudaStreamDestroy(own_stream);
   }
 
   void allocate();
   void build_tensor_maps();
+  void enable_bf16();
   void run_op(int o, cudaStream_t s);
   void run_list(const std::vector<int>& ops, cudaStream_t s, bool check);
   void forward(cudaStream_t s);
@@ -245,8 +255,9 @@ void Runtime::build_tensor_maps() {
   if (const char* e = std::getenv("GAWEE_PRECISION")) {
     const std::string m(e);
     if (m == "tf32") passes = 1;
+    else if (m == "bf16") passes = 1, bf16 = true;
     else if (m == "fp32" || m.empty()) passes = 3;
-    else throw StatusError(GAWEE_ERR_INVALID, "GAWEE_PRECISION must be fp32 or tf32, not " + m);
+    else throw StatusError(GAWEE_ERR_INVALID, "GAWEE_PRECISION must be fp32, tf32 or bf16, not " + m);
   }
   size_t ws_floats = 0;
   attn_skip.assign(P.ops.size(), nullptr);
@@ -310,6 +321,34 @@ void Runtime::build_tensor_maps() {
   if (ws_floats) {
     if (cudaMalloc(&splitk_ws, ws_floats * sizeof(float)) != cudaSuccess)
       throw StatusError(GAWEE_ERR_OOM, "cudaMalloc of the split-K workspace failed");
+  }
+  if (bf16) enable_bf16();
+}
+
+// The BF16 mode's per-op state: a bf16 B plane and its tensor map for every
+// contraction on the TMA kernel (allocated once, on the first switch to the
+// mode); an op whose plane cannot be mapped keeps single-pass TF32.  Planes
+// are filled from the packed planes before the next forward's main phase.
+void Runtime::enable_bf16() {
+  Plan& P = *plan;
+  bf16_plane.resize(P.ops.size(), nullptr);
+  bf16_map.resize(P.ops.size());
+  bf16_ldk.resize(P.ops.size(), 0);
+  bf16_fresh.assign(P.ops.size(), 0);
+  for (size_t o = 0; o < P.ops.size(); ++o) {
+    const Op& op = P.ops[o];
+    if (op.dead || op.kind != OpKind::TC || a_tma[o] == kern::A_TMA_NONE || bf16_plane[o]) continue;
+    const auto& t = op.tc;
+    const int64_t ldk16 = (t.ldk + 7) / 8 * 8;
+    void* b = nullptr;
+    if (cudaMalloc(&b, (size_t)(t.b_batch * t.N * ldk16) * 2) != cudaSuccess)
+      throw StatusError(GAWEE_ERR_OOM, "cudaMalloc of a bf16 B plane failed");
+    if (!kern::make_b_tensor_map_bf16(b, t.b_batch, t.N, ldk16, t.block_n, bf16_map[o].b)) {
+      cudaFree(b);
+      continue;
+    }
+    bf16_plane[o] = b;
+    bf16_ldk[o] = ldk16;
   }
 }
 
@@ -562,6 +601,7 @@ kern::ConvGemmParams tc_params(Runtime& rt, int o, const Op& op) {
   }
   p.status = rt.status();
   p.passes = rt.passes;
+  if (rt.bf16 && o < (int)rt.bf16_plane.size() && rt.bf16_plane[o]) p.passes = 2;
   if (rt.ksplit[o] > 1 && p.epi <= kern::EPI_BIAS_ADD_RELU) {
     p.ksplit = rt.ksplit[o];
     p.ws = rt.splitk_ws;
@@ -579,7 +619,8 @@ static void launch_tc(Runtime& rt, int o, const Op& op, cudaStream_t s) {
   const kern::ConvGemmParams p = tc_params(rt, o, op);
   bool launched;
   if (rt.a_tma[o] != kern::A_TMA_NONE) {
-    launched = kern::launch_conv_gemm_tma(p, rt.tmaps[o][2].b, rt.tmaps[o][0].b, rt.tmaps[o][1].b, t.block_n, s);
+    const void* b_map = p.passes == 2 ? static_cast<const void*>(rt.bf16_map[o].b) : rt.tmaps[o][0].b;
+    launched = kern::launch_conv_gemm_tma(p, rt.tmaps[o][2].b, b_map, rt.tmaps[o][1].b, t.block_n, s);
   } else {
     launched = kern::launch_conv_gemm_tc(p, rt.tmaps[o][0].b, rt.tmaps[o][1].b, t.block_n, s);
   }
@@ -641,6 +682,7 @@ void Runtime::forward(cudaStream_t s) {
     run_list(plan->prologue, s, true);
     prologue_done = true;
   }
+  bool repacked = false;
   for (int o : plan->pack) {
     const Op& op = plan->ops[o];
     bool need = !pack_done[o];
@@ -649,6 +691,19 @@ void Runtime::forward(cudaStream_t s) {
       run_op(o, s);
       GCHECK(cudaGetLastError());
       pack_done[o] = 1;
+      repacked = true;
+    }
+  }
+  if (repacked) std::fill(bf16_fresh.begin(), bf16_fresh.end(), 0);
+  if (bf16) {
+    for (size_t o = 0; o < bf16_plane.size(); ++o) {
+      if (!bf16_plane[o] || bf16_fresh[o]) continue;
+      const auto& t = plan->ops[o].tc;
+      kern::launch_planes_to_bf16(static_cast<const float*>(plan->bufs[t.hi].ptr),
+                                  static_cast<const float*>(plan->bufs[t.lo].ptr), bf16_plane[o], t.b_batch * t.N,
+                                  t.ldk, bf16_ldk[o], s);
+      GCHECK(cudaGetLastError());
+      bf16_fresh[o] = 1;
     }
   }
   // First forward runs eagerly (it also sets kernel attributes); later ones
@@ -1155,10 +1210,17 @@ gawee_status gawee_set_graph_mode(gawee_ctx* ctx, int enabled) {
 }
 
 gawee_status gawee_set_precision(gawee_ctx* ctx, int mode) {
-  if (!ctx || (mode != GAWEE_PRECISION_FP32 && mode != GAWEE_PRECISION_TF32)) return GAWEE_ERR_INVALID;
-  const int passes = mode == GAWEE_PRECISION_TF32 ? 1 : 3;
-  if (passes == ctx->rt.passes) return GAWEE_OK;
+  if (!ctx || (mode != GAWEE_PRECISION_FP32 && mode != GAWEE_PRECISION_TF32 && mode != GAWEE_PRECISION_BF16))
+    return GAWEE_ERR_INVALID;
+  const int passes = mode == GAWEE_PRECISION_FP32 ? 3 : 1;
+  const bool bf16 = mode == GAWEE_PRECISION_BF16;
+  if (passes == ctx->rt.passes && bf16 == ctx->rt.bf16) return GAWEE_OK;
   cudaSetDevice(ctx->rt.device);
+  if (bf16) {
+    const gawee_status st = guard(ctx, [&] { ctx->rt.enable_bf16(); });
+    if (st != GAWEE_OK) return st;
+  }
+  ctx->rt.bf16 = bf16;
   // the captured graph holds the old kernel parameters: capture again
   if (ctx->rt.gexec) cudaGraphExecDestroy(ctx->rt.gexec);
   if (ctx->rt.graph) cudaGraphDestroy(ctx->rt.graph);
@@ -1170,6 +1232,7 @@ gawee_status gawee_set_precision(gawee_ctx* ctx, int mode) {
 
 int gawee_precision(const gawee_ctx* ctx) {
   if (!ctx) return -1;
+  if (ctx->rt.bf16) return GAWEE_PRECISION_BF16;
   return ctx->rt.passes == 1 ? GAWEE_PRECISION_TF32 : GAWEE_PRECISION_FP32;
 }
 
@@ -1208,6 +1271,7 @@ gawee_status gawee_op_info(const gawee_ctx* ctx, int i, char* name, size_t n, in
       nm += " [split-k " + std::to_string(ctx->rt.ksplit[o]) + "]";
     if (op.kind == gawee::OpKind::TC && o < (int)ctx->rt.aux_tma.size() && ctx->rt.aux_tma[o])
       nm += " [aux smem]";
+    if (ctx->rt.bf16 && o < (int)ctx->rt.bf16_plane.size() && ctx->rt.bf16_plane[o]) nm += " [bf16]";
     std::strncpy(name, nm.c_str(), n - 1);
     name[n - 1] = 0;
   }

@@ -688,6 +688,21 @@ bool make_b_tensor_maps(const float* hi, const float* lo, int64_t batch, int64_t
   return true;
 }
 
+bool make_b_tensor_map_bf16(const void* plane, int64_t batch, int64_t N, int64_t ldk16, int block_n,
+                            void* tmap_out) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  if (ldk16 % 8 != 0 || (reinterpret_cast<uintptr_t>(plane) & 15)) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)ldk16, (cuuint64_t)N, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(ldk16 * 2), (cuuint64_t)(N * ldk16 * 2)};
+  cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)block_n, 1};  // 32 bf16: one 64-byte swizzled row
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(static_cast<CUtensorMap*>(tmap_out), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(plane),
+                   dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 int choose_ksplit(int64_t M, int64_t N, int64_t K, int nb, int block_n, int epi, int sms, int rk) {
   if (nb != 1 || epi > EPI_BIAS_ADD_RELU || M <= 0 || N <= 0 || K <= 0 || sms <= 0 || rk <= 0) return 1;
   const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + block_n - 1) / block_n);

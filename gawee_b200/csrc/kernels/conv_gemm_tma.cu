@@ -66,11 +66,14 @@ struct TmaConfig<128> {
   static constexpr int NS_AUX = 3;
 };
 
-template <int BN, int NS, int AUX = 0>
+template <int BN, int NS, int AUX = 0, int PASSES = 3>
 struct TmaSmem {
+  // PASSES 2: the BF16 mode -- one B plane of bf16 values (64-byte rows,
+  // 64-byte swizzled) and A as bf16 pairs in tensor memory
+  static constexpr bool kBf16 = PASSES == 2;
   static constexpr int kATile = kBM * kBK * 4;          // 16 KB: raw A of one k-block
-  static constexpr int kBTile = BN * kBK * 4;           // one B plane of one k-block
-  static constexpr int kStage = kATile + 2 * kBTile;    // A, B hi, B lo (a multiple of 1024)
+  static constexpr int kBTile = BN * kBK * (kBf16 ? 2 : 4);  // one B plane of one k-block
+  static constexpr int kStage = kATile + (kBf16 ? 1 : 2) * kBTile;  // A, B hi[, B lo] (a multiple of 1024)
   static constexpr int kStageOff = NS * kStage;         // epilogue staging, or the aux tile
   // the aux tile: BN / 32 boxes of [128 rows][32 columns], 16 KB each, 128-byte swizzled
   static constexpr int kAuxBox = kBM * kBK * 4;
@@ -82,10 +85,12 @@ struct TmaSmem {
   static constexpr int kNumBars = 3 * NS + 2 * kNAcc + 1 + (AUX ? 2 : 0);
   static constexpr int kBytes = kBarOff + 8 * kNumBars + 16 + 1024;  // + alignment slack
   // BN 64 folds hi*hi and hi*lo into one N = 128 MMA (B stage: hi rows then lo rows)
-  static constexpr bool kFold = BN == 64;
+  static constexpr bool kFold = BN == 64 && !kBf16;
   static constexpr int kAccCols = kFold ? 2 * BN : BN;
   static constexpr int kACol = kNAcc * kAccCols;          // first A column
-  static constexpr int kUsedCols = kACol + NS * 2 * kBK;  // per stage 32 raw and 32 remainder columns
+  // per stage 32 raw and 32 remainder columns, or 16 columns of bf16 pairs
+  static constexpr int kAStageCols = kBf16 ? kBK / 2 : 2 * kBK;
+  static constexpr int kUsedCols = kACol + NS * kAStageCols;
   static constexpr int kTmemCols = kUsedCols <= 256 ? 256 : 512;
   static_assert(kStage % 1024 == 0, "stages must keep the 1024-byte swizzle alignment");
   static_assert(kUsedCols <= 512, "tensor memory columns");
@@ -110,6 +115,51 @@ __device__ __forceinline__ void tma_load_im2col_4d(uint32_t dst, const CUtensorM
       : "memory");
 }
 
+// Shared-memory descriptor for the BF16 mode's B tile: K-major, 64-byte
+// swizzle (rows of 32 bf16), 8-row groups 512 B apart.
+__device__ __forceinline__ uint64_t umma_desc_sw64(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr & 0x3FFFFu) >> 4);  // start address
+  d |= (uint64_t)1 << 16;                   // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(512 >> 4) << 32;          // stride byte offset
+  d |= (uint64_t)1 << 46;                   // descriptor version (sm_100)
+  d |= (uint64_t)4 << 61;                   // SWIZZLE_64B
+  return d;
+}
+
+// Instruction descriptor: kind::f16 with bf16 A and B, fp32 accumulate, K-major, M = 128.
+template <int BN>
+__device__ __forceinline__ uint32_t umma_idesc_bf16() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+}
+
+// D (tensor memory) += A (tensor memory, bf16 pairs: two k per column) . B (shared memory, bf16)
+__device__ __forceinline__ void umma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st16_a(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// Two fp32 values rounded to bf16 (round to nearest even), the first in the low half.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
 }  // namespace
 
 // Poll intervals of the waits off the MMA issuer's path (nanoseconds): the A
@@ -125,12 +175,15 @@ constexpr unsigned kSleepA = 64, kSleepTma = 32, kSleepAcc = 256;
 // FAST_SIGMOID_MUL the accumulator warps also form aux * sigmoid(aux) in
 // place between the last round drains.  Only unsplit launches (ksplit 1)
 // use it.
+// PASSES: 3 (fp32 from three TF32 products), 1 (one TF32 product) or 2 (the
+// BF16 mode: one kind::f16 product of bf16 operands, B from a bf16 plane
+// through tm_hi, A rounded to bf16 by the A warps).
 template <int BN, int NS, int EPI, int PASSES, int AUX>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     conv_gemm_tma_kernel(const __grid_constant__ ConvGemmParams p, const __grid_constant__ CUtensorMap tm_a,
                          const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo,
                          const __grid_constant__ CUtensorMap tm_x) {
-  using L = TmaSmem<BN, NS, AUX>;
+  using L = TmaSmem<BN, NS, AUX, PASSES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
@@ -151,6 +204,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   // fp32 from three TF32 products, or one (the single-pass TF32 mode): a
   // template parameter, so the three-pass kernel carries no test of it
   constexpr bool three = PASSES == 3;
+  constexpr bool bf16 = PASSES == 2;
   const int num_kb = (int)((p.K + kBK - 1) / kBK);
   const int rk = p.rk;  // k-blocks per promotion round (the launcher fills it)
   const int num_rounds = (num_kb + rk - 1) / rk;
@@ -250,8 +304,15 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             x[4 * c + 2] = __float_as_uint(v.z);
             x[4 * c + 3] = __float_as_uint(v.w);
           }
-          const uint32_t acol = tmem_rows + (uint32_t)(L::kACol + st * 2 * kBK);
-          tmem_st32(acol, x);
+          const uint32_t acol = tmem_rows + (uint32_t)(L::kACol + st * L::kAStageCols);
+          if constexpr (bf16) {
+            uint32_t h[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) h[e] = pack_bf16x2(__uint_as_float(x[2 * e]), __uint_as_float(x[2 * e + 1]));
+            tmem_st16_a(acol, h);
+          } else {
+            tmem_st32(acol, x);
+          }
           if (three) {
             uint32_t y[32];
 #pragma unroll
@@ -366,9 +427,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     }
   } else if (warp == 5) {
     // ------------------------------------------------------------------ MMA issuer
-    const uint32_t idesc = umma_idesc_tf32<BN>();
+    const uint32_t idesc = bf16 ? umma_idesc_bf16<BN>() : umma_idesc_tf32<BN>();
     const uint32_t idesc2 = umma_idesc_tf32<2 * BN>();  // B's hi and lo planes as one operand
-    const uint64_t desc0 = umma_desc_sw128(smem_u32(smem));
+    const uint64_t desc0 = bf16 ? umma_desc_sw64(smem_u32(smem)) : umma_desc_sw128(smem_u32(smem));
     constexpr uint64_t kStageDesc = (uint64_t)(L::kStage >> 4);  // descriptor start-address units
     constexpr uint64_t kATileDesc = (uint64_t)(L::kATile >> 4);
     constexpr uint64_t kBTileDesc = (uint64_t)(L::kBTile >> 4);
@@ -394,13 +455,18 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           if (lane == 0) {
             const uint64_t dbh = desc0 + (uint64_t)st * kStageDesc + kATileDesc;
             const uint64_t dbl = dbh + kBTileDesc;
-            const uint32_t a_raw = tmem_base + (uint32_t)(L::kACol + st * 2 * kBK);
+            const uint32_t a_raw = tmem_base + (uint32_t)(L::kACol + st * L::kAStageCols);
             const uint32_t a_rem = a_raw + kBK;
             // a K-major SW128 descriptor advances 32 bytes (2 units) per
             // 8-wide k-step; an A column holds one k
             // the pass count is tested once per k-block, outside the issue
             // loop: the issuing thread is the kernel's critical path
-            if (three) {
+            if constexpr (bf16) {
+              // two 16-wide k-steps: 32 bytes of each 64-byte B row and 8 A columns (two k each) apart
+#pragma unroll
+              for (int kk = 0; kk < kBK / 16; ++kk)
+                umma_bf16_ts(tmem_d, a_raw + 8 * kk, dbh + 2 * kk, idesc, (j | kk) != 0);
+            } else if (three) {
 #pragma unroll
               for (int kk = 0; kk < kBK / 8; ++kk) {
                 const uint64_t o = (uint64_t)(2 * kk);
@@ -551,7 +617,7 @@ bool launch_t(const ConvGemmParams& p, const void* tma, const void* tmh, const v
               cudaStream_t s) {
   constexpr int NS = AUX ? TmaConfig<BN>::NS_AUX : TmaConfig<BN>::NS;
   auto kern = conv_gemm_tma_kernel<BN, NS, EPI, PASSES, AUX>;
-  constexpr int smem = TmaSmem<BN, NS, AUX>::kBytes;
+  constexpr int smem = TmaSmem<BN, NS, AUX, PASSES>::kBytes;
   static_assert(smem <= 232448, "shared memory per CTA");
   static std::mutex mu;
   static uint64_t attr_devices = 0;
@@ -597,7 +663,9 @@ bool launch_epi_p(const ConvGemmParams& p, const void* tma, const void* tmh, con
 template <int BN>
 bool launch_epi(const ConvGemmParams& p, const void* tma, const void* tmh, const void* tml, const void* tmx,
                 cudaStream_t s) {
-  return p.passes == 1 ? launch_epi_p<BN, 1>(p, tma, tmh, tml, tmx, s) : launch_epi_p<BN, 3>(p, tma, tmh, tml, tmx, s);
+  if (p.passes == 1) return launch_epi_p<BN, 1>(p, tma, tmh, tml, tmx, s);
+  if (p.passes == 2) return launch_epi_p<BN, 2>(p, tma, tmh, tml, tmx, s);
+  return launch_epi_p<BN, 3>(p, tma, tmh, tml, tmx, s);
 }
 
 // The aux operand of an unsplit launch as a tiled map over [M][N] (row
@@ -687,7 +755,7 @@ bool launch_conv_gemm_tma(const ConvGemmParams& p_in, const void* tmap_a, const 
   if (p.rk <= 0) p.rk = kRK;
   if (p.rk > 16) return false;
   if (p.passes == 0) p.passes = 3;
-  if (p.passes != 1 && p.passes != 3) return false;
+  if (p.passes < 1 || p.passes > 3) return false;
   if (p.K <= 0 || p.nb != 1 || (p.a_tma != A_TMA_2D && p.a_tma != A_TMA_IM2COL && p.a_tma != A_TMA_IM2COL_TAPS))
     return false;
   if (p.a_tma == A_TMA_IM2COL && p.C % kBK != 0) return false;

@@ -256,6 +256,10 @@ struct PackBParams {
   int64_t batch_shape[4], batch_st[4];
 };
 void launch_pack_b(const PackBParams& p, cudaStream_t s);
+// The BF16 mode's B plane ([rows][ldk16] bf16, ldk16 a multiple of 8 >= ldk)
+// from packed hi / lo planes ([rows][ldk] fp32): bf16(hi + lo), zero past ldk.
+void launch_planes_to_bf16(const float* hi, const float* lo, void* out, int64_t rows, int64_t ldk, int64_t ldk16,
+                           cudaStream_t s);
 
 // ---------------------------------------------------------------------------
 // Tensor-core contraction: implicit-GEMM convolution / (batched) GEMM.
@@ -323,7 +327,9 @@ struct ConvGemmParams {
   int rk;
   // Tensor-core passes per product: 3 (fp32 from three TF32 products,
   // hi*hi + hi*lo + lo*hi; the default, also for 0) or 1 (one TF32 product
-  // of the truncated operands: the single-pass TF32 precision mode).
+  // of the truncated operands: the single-pass TF32 precision mode); 2 is
+  // the BF16 mode of launch_conv_gemm_tma only (one kind::f16 product of
+  // bf16-rounded operands, B from the bf16 plane's map passed as tmap_hi).
   int passes;
   // launch_conv_gemm_tma only: nonzero lets the epilogue's aux operand (the
   // residual, or an EPI_FAST operand) come per tile through shared memory by
@@ -418,6 +424,10 @@ int conv_gemm_tma_smem_bytes(int block_n);
 bool conv_gemm_tma_aux_ok(const ConvGemmParams& p);
 
 // Build the TMA descriptors for packed B planes [batch][N][ldk] (fp32).
+// The BF16 mode's B operand for launch_conv_gemm_tma (passes 2, as its tmap_hi):
+// a tiled map over the bf16 plane, boxes of 32 k x block_n rows, 64-byte swizzle.
+bool make_b_tensor_map_bf16(const void* plane, int64_t batch, int64_t N, int64_t ldk16, int block_n,
+                            void* tmap_out);
 bool make_b_tensor_maps(const float* hi, const float* lo, int64_t batch, int64_t N, int64_t ldk, int block_n,
                         void* tmap_hi_out, void* tmap_lo_out);
 

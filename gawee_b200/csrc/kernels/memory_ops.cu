@@ -2,6 +2,8 @@
 // reductions, softmax, gather, index remaps, pooling, top-k and the packing of
 // tensor-core B operands.  Grids are sized as multiples of the SM count and
 // use grid-stride loops.
+#include <cuda_bf16.h>
+
 #include <algorithm>
 #include <cfloat>
 #include <cstdio>
@@ -1295,6 +1297,29 @@ __global__ void __launch_bounds__(256) pack_b_kn_kernel(const __grid_constant__ 
     }
     __syncthreads();
   }
+}
+
+// The BF16 mode's B plane from the packed TF32 planes: hi + lo is the
+// packed fp32 value exactly (lo = x - hi, exact), rounded to bf16 (nearest
+// even); rows of ldk16 >= ldk values, zero past ldk.
+__global__ void __launch_bounds__(kThreads) planes_to_bf16_kernel(const float* __restrict__ hi,
+                                                                  const float* __restrict__ lo,
+                                                                  __nv_bfloat16* __restrict__ out, int64_t rows,
+                                                                  int64_t ldk, int64_t ldk16) {
+  const int64_t total = rows * ldk16;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / ldk16, k = i - r * ldk16;
+    float x = 0.f;
+    if (k < ldk) x = __fadd_rn(hi[r * ldk + k], lo[r * ldk + k]);
+    out[i] = __float2bfloat16_rn(x);
+  }
+}
+
+void launch_planes_to_bf16(const float* hi, const float* lo, void* out, int64_t rows, int64_t ldk, int64_t ldk16,
+                           cudaStream_t s) {
+  if (rows <= 0 || ldk16 <= 0) return;
+  planes_to_bf16_kernel<<<grid_for(rows * ldk16), kThreads, 0, s>>>(hi, lo, static_cast<__nv_bfloat16*>(out), rows,
+                                                                    ldk, ldk16);
 }
 
 void launch_pack_b(const PackBParams& p, cudaStream_t s) {

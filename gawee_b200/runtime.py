@@ -110,7 +110,7 @@ def _stream_ptr(stream) -> Optional[int]:
 class Model:
     """A gawee `forward` function compiled for one B200."""
 
-    PRECISIONS = {"fp32": 0, "tf32": 1}
+    PRECISIONS = {"fp32": 0, "tf32": 1, "bf16": 2}
 
     def __init__(self, mlir: str, device: int = 0, entry: str = "forward", graph_mode: bool = True,
                  precision: Optional[str] = None):
@@ -137,8 +137,9 @@ class Model:
 
     def set_precision(self, precision: str):
         """Tensor-core arithmetic: "fp32" (three TF32 passes, the default and the
-        parity mode) or "tf32" (one pass; see gawee_set_precision in
-        include/gawee_cuda.h for its error bound)."""
+        parity mode), "tf32" (one pass) or "bf16" (one bf16 pass on the TMA
+        contraction kernel, single-pass TF32 elsewhere); gawee_set_precision in
+        include/gawee_cuda.h states each mode's error bound."""
         if precision not in self.PRECISIONS:
             raise ValueError(f"precision must be one of {sorted(self.PRECISIONS)}, not {precision!r}")
         self._check(self._lib.gawee_set_precision(self._h, self.PRECISIONS[precision]))

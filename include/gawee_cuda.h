@@ -118,10 +118,18 @@ gawee_status gawee_set_graph_mode(gawee_ctx* ctx, int enabled);
  *   GAWEE_PRECISION_TF32: one TF32 product of the truncated operands (10
  *     explicit mantissa bits each), same accumulation: |error| <= 2^-9 *
  *     sum |a_k * b_k| per output plus the accumulation term; not a parity mode.
- * GAWEE_PRECISION=tf32 in the environment selects TF32 at gawee_create.
- * Changing the mode drops the captured CUDA graph (it is captured again on
- * the next forward); call it between forwards, with no forward in flight. */
-enum { GAWEE_PRECISION_FP32 = 0, GAWEE_PRECISION_TF32 = 1 };
+ *   GAWEE_PRECISION_BF16: contractions on the TMA kernel take one bf16
+ *     product (both operands rounded to nearest bf16, 8 significant bits,
+ *     relative error <= 2^-9 each), same fp32 accumulation: |error| <=
+ *     2^-8 * sum |a_k * b_k| plus the accumulation term; the other
+ *     tensor-core kernels (the gather kernel, fused attention) run single-pass
+ *     TF32.  The first switch to it allocates a bf16 copy of those
+ *     contractions' B operands (half the size of one packed plane).
+ * GAWEE_PRECISION=tf32 or bf16 in the environment selects the mode at
+ * gawee_create.  Changing the mode drops the captured CUDA graph (it is
+ * captured again on the next forward); call it between forwards, with no
+ * forward in flight. */
+enum { GAWEE_PRECISION_FP32 = 0, GAWEE_PRECISION_TF32 = 1, GAWEE_PRECISION_BF16 = 2 };
 gawee_status gawee_set_precision(gawee_ctx* ctx, int mode);
 int gawee_precision(const gawee_ctx* ctx); /* the current mode, -1 for NULL */
 

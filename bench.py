@@ -32,7 +32,9 @@ One JSON line on rank 0:
               ResNet-18, BERT-tiny and Llama-15M (configurations 0-2; Llama-15M
               both as the reference binding's KV-cache decode step and as a
               256-token prefill) -- each with its own e2e, roofline and CPU
-              baseline
+              baseline; and `precision_modes`: the ResNet-18 b256 and
+              decoder-135M b64 forwards again in the single-pass TF32 and
+              BF16 modes (reduced precision, not the headline)
 `--impl reference` times that CPU implementation alone (the reference's own
 MLIR/LLVM toolchain is not available, so its AOT binary cannot be built).
 """
@@ -345,6 +347,33 @@ def latency_entry(name, g, metric, published_ms, published_src, peaks, local, st
             "reference_published_ms": published_ms, "reference_published_source": published_src}
 
 
+def precision_modes(m, stream, steps, units):
+    """Device time of `steps` forwards of an already warmed model in each
+    reduced-precision mode (single-pass TF32, BF16), as units per second;
+    the model is left in fp32.  Neither is a parity mode: their error bounds
+    are stated with gawee_set_precision in include/gawee_cuda.h."""
+    import torch
+    sp = stream.cuda_stream
+    out = {}
+    try:
+        for mode in ("tf32", "bf16"):
+            m.set_precision(mode)
+            for _ in range(3):
+                m.forward(sp)
+            m.synchronize(sp)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(steps):
+                m.forward(sp)
+            e1.record(stream)
+            m.synchronize(sp)
+            ms = e0.elapsed_time(e1) / steps
+            out[mode] = {"value": units / ms * 1e3, "ms_per_step": ms}
+    finally:
+        m.set_precision("fp32")
+    return out
+
+
 def decoder_entry(peaks, local, steps):
     """Config 4 at N=1: decoder-135M prefill, batch 64 x 512, tokens/s."""
     import torch
@@ -382,6 +411,7 @@ def decoder_entry(peaks, local, steps):
         ms_e2e = e0.elapsed_time(e1) / steps
         roof, kern, prof = tc_roofline(m, sp, peaks)
         n_launch = m.num_launches()
+        modes = precision_modes(m, stream, steps, 64 * 512)
     finally:
         m.close()
     tokens = 64 * 512
@@ -392,12 +422,19 @@ def decoder_entry(peaks, local, steps):
             "e2e": {"value": tokens / ms_e2e * 1e3, "unit": "tokens/s", "h2d_bytes_per_step": int(args[0].nbytes),
                     "d2h_bytes_per_step": out_bytes,
                     "note": "serial: upload, forward and the 6.4 GB logits download in one stream"},
-            "gpu_launches_per_step": n_launch, "roofline": roof, "cpu_baseline": cpu}
+            "gpu_launches_per_step": n_launch, "roofline": roof, "cpu_baseline": cpu,
+            "precision_modes": modes}
 
 
-def run_extra(peaks, local):
+def run_extra(peaks, local, resnet_modes=None):
     from gawee_b200 import synth
     out = {"decoder135m_prefill": decoder_entry(peaks, local, steps=5)}
+    out["precision_modes"] = {
+        "note": "the same workloads in the reduced-precision modes (not parity modes; bounds with "
+                "gawee_set_precision in include/gawee_cuda.h): single-pass TF32 everywhere, or BF16 "
+                "products on the TMA contraction kernel with single-pass TF32 elsewhere",
+        "resnet18_b256": dict(resnet_modes or {}, unit="images/s"),
+        "decoder135m_b64x512": dict(out["decoder135m_prefill"].pop("precision_modes"), unit="tokens/s")}
     cfgs = [("resnet18_b1_latency", synth.resnet18(1), "ResNet-18 fp32 batch-1 latency (1x3x224x224)", 6814.2),
             ("bert_tiny_s128_latency", synth.bert_tiny(), "BERT-tiny fp32 encoder latency (batch 1, seq 128)", 354.0),
             ("llama15m_decode_step_latency", synth.llama15m_decode(1, 1),
@@ -604,9 +641,11 @@ def main():
         line["e2e"]["h2d_bytes_per_step"] = int(t.item())
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(a.workload)
+    extra_on = rank == 0 and world == 1 and not a.no_extra and a.workload == "resnet18" and not a.batch
+    resnet_modes = precision_modes(m, stream, a.steps, global_batch * items) if extra_on else None
     m.close()
-    if rank == 0 and world == 1 and not a.no_extra and a.workload == "resnet18" and not a.batch:
-        line["extra"] = run_extra(peaks, local)
+    if extra_on:
+        line["extra"] = run_extra(peaks, local, resnet_modes)
     if rank == 0:
         sys.stderr.write("per-kernel ms (one eager forward):\n")
         for (n, tc, f), t in sorted(zip(kern, prof), key=lambda x: -x[1])[:12]:

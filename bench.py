@@ -474,7 +474,9 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep NCCL's banner off stdout, where the JSON line goes
+    # NCCL_DEBUG is left as the caller set it: at any level from VERSION up
+    # NCCL prints its version banner on stdout, where the JSON line goes
+    # (unset, it prints nothing)
     if world != a.gpus:
         raise SystemExit(f"--gpus {a.gpus} but WORLD_SIZE={world}")
     torch.cuda.set_device(local)

@@ -230,3 +230,34 @@ def test_bf16_resnet_logits_close_and_fp32_restored():
     rel = float(np.max(np.abs(b1 - want))) / float(np.max(np.abs(want)))
     print(f"resnet18 b2 64x64 bf16: max |err| / max |logit| = {rel:.2e}")
     assert 1e-5 < rel < 5e-2
+
+
+def test_bf16_gqa_decoder_close():
+    """A GQA decoder in the BF16 mode: merged Q/K/V GEMM, residual and SwiGLU
+    epilogues with the staged operand in bf16, attention in single-pass TF32.
+    A closeness figure against the oracle, and the fp32 bits after switching
+    back."""
+    import oracle
+    from gawee_b200 import synth
+    from gawee_b200.runtime import Model
+    g = synth.llama(2, 64, dim=576, layers=2, heads=9, kv_heads=3, ffn=1536, vocab=4096, name="decoder_l2_bf16")
+    args = g.make_args()
+    want = oracle.run(g.mlir, args)[0]
+    m = Model(g.mlir)
+    try:
+        fp32_a = m.run(args)[0]
+        m.set_precision("bf16")
+        names = [n for n, _, _ in m.kernels()]
+        b1 = m.run(args)[0]
+        b2 = m.run(args)[0]
+        m.set_precision("fp32")
+        fp32_b = m.run(args)[0]
+    finally:
+        m.close()
+    assert any(n.startswith("matmul3") and "[bf16]" in n for n in names), names
+    assert any("sigmoid" in n and "[aux smem]" in n and "[bf16]" in n for n in names), names
+    np.testing.assert_array_equal(fp32_b, fp32_a)
+    np.testing.assert_array_equal(b1, b2)
+    rel = float(np.max(np.abs(b1 - want))) / float(np.max(np.abs(want)))
+    print(f"decoder 2 layers b2 s64 bf16: max |err| / max |logit| = {rel:.2e}")
+    assert 1e-5 < rel < 5e-2

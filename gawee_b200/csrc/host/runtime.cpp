@@ -119,6 +119,9 @@ struct Runtime {
   std::vector<int> ksplit;                 // per op (TC only): k splits, 1 = none
   std::vector<char> aux_tma;               // per op (TC only): epilogue operand staged by TMA (TMA kernel)
   std::vector<uint8_t*> attn_skip;         // per op (ATTN only): skip flags of the mask tiles
+  // per op (ATTN only): 1 when the mask is a constant or a prologue result
+  // (fixed once the prologue has run), 2 once its flags have been filled
+  std::vector<char> attn_skip_static;
   std::vector<std::array<std::array<int8_t, 3>, 3>> attn_cpos;  // per op (ATTN): tensor-map dim order
   float* splitk_ws = nullptr;              // partial sums of split contractions (ops run in order: shared)
   ncclComm_t comm = nullptr;
@@ -261,6 +264,7 @@ void Runtime::build_tensor_maps() {
   }
   size_t ws_floats = 0;
   attn_skip.assign(P.ops.size(), nullptr);
+  attn_skip_static.assign(P.ops.size(), 0);
   attn_cpos.assign(P.ops.size(), {});
   for (size_t o = 0; o < P.ops.size(); ++o) {
     const Op& op = P.ops[o];
@@ -278,6 +282,17 @@ void Runtime::build_tensor_maps() {
         const int64_t n = mb * mh * ((a.S + 127) / 128) * ((a.Skv + 127) / 128);
         if (cudaMalloc(&attn_skip[o], (size_t)n) != cudaSuccess)
           throw StatusError(GAWEE_ERR_OOM, "cudaMalloc of attention skip flags failed");
+        // a constant mask, or a persistent one written only by prologue ops
+        // (the causal mask): its flags, once filled, hold for every forward
+        const Buf& mbuf = P.bufs[a.mask.buf];
+        bool fixed = mbuf.kind == BufKind::CONST;
+        if (mbuf.kind == BufKind::PERSIST) {
+          fixed = true;
+          for (const Op& w : P.ops)
+            for (const View& v : w.writes)
+              if (!w.dead && v.buf == a.mask.buf && w.phase != Phase::PROLOGUE) fixed = false;
+        }
+        attn_skip_static[o] = fixed ? 1 : 0;
       }
       continue;
     }
@@ -655,8 +670,11 @@ static void launch_attn(Runtime& rt, int o, const Op& op, cudaStream_t s) {
     for (int i = 0; i < 3; ++i) p.cpos[w][i] = rt.attn_cpos[o][w][i];
   p.status = rt.status();
   p.passes = rt.passes;
-  if (!kern::launch_attention(p, rt.tmaps[o][0].b, rt.tmaps[o][1].b, rt.tmaps[o][2].b, rt.attn_skip[o], s))
+  char& fixed = rt.attn_skip_static[o];
+  if (!kern::launch_attention(p, rt.tmaps[o][0].b, rt.tmaps[o][1].b, rt.tmaps[o][2].b, rt.attn_skip[o], fixed == 2,
+                              s))
     throw StatusError(GAWEE_ERR_UNSUPPORTED, "attention launch rejected the shape of op " + op.name);
+  if (fixed == 1) fixed = 2;  // filled by this launch, valid for every later forward
 }
 
 void Runtime::run_op(int o, cudaStream_t s) {
@@ -1244,7 +1262,10 @@ int gawee_num_launches(const gawee_ctx* ctx) {
   for (int o : ctx->rt.plan->main) {
     const auto& op = ctx->rt.plan->ops[o];
     n += 1 + (o < (int)ctx->rt.ksplit.size() && ctx->rt.ksplit[o] > 1 ? 1 : 0);
-    if (op.kind == gawee::OpKind::ATTN && op.attn.has_mask) ++n;  // the skip-flag pass
+    // the skip-flag pass, unless the mask is fixed and its flags are filled
+    if (op.kind == gawee::OpKind::ATTN && op.attn.has_mask &&
+        !(o < (int)ctx->rt.attn_skip_static.size() && ctx->rt.attn_skip_static[o] == 2))
+      ++n;
   }
   return n;
 }

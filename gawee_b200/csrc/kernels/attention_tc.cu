@@ -701,15 +701,17 @@ bool attn_supported(int64_t D, int64_t Skv, int64_t H, int64_t Hkv) {
 }
 
 bool launch_attention(const AttnParams& p, const void* tq, const void* tk, const void* tv, uint8_t* skip_flags,
-                      cudaStream_t s) {
+                      bool flags_current, cudaStream_t s) {
   if (!attn_supported(p.D, p.Skv, p.H, p.Hkv) || p.B <= 0 || p.S <= 0) return false;
   if (p.passes != 0 && p.passes != 1 && p.passes != 3) return false;
   AttnParams q = p;
   if (q.passes == 0) q.passes = 3;
   q.skip = nullptr;
   if (p.mask && skip_flags) {
-    const int blocks = p.mb * p.mh * p.QT * p.KT;
-    attn_skip_kernel<<<blocks, 256, 0, s>>>(p, skip_flags);
+    if (!flags_current) {
+      const int blocks = p.mb * p.mh * p.QT * p.KT;
+      attn_skip_kernel<<<blocks, 256, 0, s>>>(p, skip_flags);
+    }
     q.skip = skip_flags;
   }
   switch ((p.D + 15) / 16 * 16) {

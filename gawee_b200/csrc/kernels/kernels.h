@@ -384,8 +384,12 @@ bool attn_supported(int64_t D, int64_t Skv, int64_t H, int64_t Hkv);
 bool make_attn_tensor_map(const float* base, int64_t batch, int64_t heads, int64_t seq, int64_t dim, int64_t st_b,
                           int64_t st_h, int64_t st_s, void* tmap_out, int8_t* cpos);
 // skip_flags: mb * mh * QT * KT bytes of device scratch (used when p.mask is set).
+// skip_flags: per (mask block, query tile, key tile) flags that
+// attn_skip_kernel fills before the attention kernel runs, unless
+// flags_current says they already hold this mask's flags (a mask that never
+// changes after the forward that first filled them).
 bool launch_attention(const AttnParams& p, const void* tq, const void* tk, const void* tv, uint8_t* skip_flags,
-                      cudaStream_t s);
+                      bool flags_current, cudaStream_t s);
 
 // Returns false (and launches nothing) when the shape is not supported.
 bool launch_conv_gemm_tc(const ConvGemmParams& p, const void* tmap_hi, const void* tmap_lo, int block_n,

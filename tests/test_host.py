@@ -165,6 +165,36 @@ def test_plan_merges_projections_that_share_their_input(monkeypatch):
     assert "matmul3" not in s and s.count("matmul\n") >= 4, s
 
 
+def test_plan_keeps_projections_apart_when_a_merge_would_not_hold():
+    # a result returned as is needs its own dense buffer; computed weights are
+    # not packed once; different left operands share nothing
+    from tests.helpers import build, rand_input
+
+    def returned(g):
+        x = rand_input(g, (2, 37, 64), 1)
+        q = g.matmul(x, rand_input(g, (64, 32), 2))
+        k = g.matmul(x, rand_input(g, (64, 32), 3))
+        return [q, g.reshape(k, (2, 37, 2, 16))]
+
+    def computed_weight(g):
+        x = rand_input(g, (2, 37, 64), 1)
+        w = g.add(rand_input(g, (64, 32), 2), rand_input(g, (64, 32), 4))
+        q = g.matmul(x, w)
+        k = g.matmul(x, rand_input(g, (64, 32), 3))
+        return [g.reshape(t, (2, 37, 2, 16)) for t in (q, k)]
+
+    def two_inputs(g):
+        x = rand_input(g, (2, 37, 64), 1)
+        y = rand_input(g, (2, 37, 64), 5)
+        q = g.matmul(x, rand_input(g, (64, 32), 2))
+        k = g.matmul(y, rand_input(g, (64, 32), 3))
+        return [g.reshape(t, (2, 37, 2, 16)) for t in (q, k)]
+    for f in (returned, computed_weight, two_inputs):
+        s = _plan(build(f)[0])
+        ops = [ln.strip() for ln in s.splitlines()[1:]]
+        assert ops.count("matmul") == 2 and not any(o.startswith("matmul2") for o in ops), (f.__name__, s)
+
+
 def test_plan_memory_reuse():
     g = synth.resnet18(256)
     s = _plan(g.mlir)

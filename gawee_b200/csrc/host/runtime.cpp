@@ -399,7 +399,9 @@ static kern::DProgram to_device(const EProgram& p) {
 // evaluate them without the interpreter.  Registers: r0 = accumulator,
 // r1.. = aux operands; every match checks the exact operation sequence, so
 // the fast path computes the same IEEE operations in the same order.
-static int match_fast_epilogue(const EProgram& p, float* c) {
+// *swap_aux is set when the program adds aux 1 before aux 0 (FAST_ADD_ADD):
+// the caller then swaps the two operands so the kernel's order is the program's.
+static int match_fast_epilogue(const EProgram& p, float* c, bool* swap_aux = nullptr) {
   const auto& k = p.code;
   auto f32 = [&](const EInstr& in) { return in.ty == DType::F32 && in.rty == DType::F32; };
   auto uses = [](const EInstr& in, int x, int y) { return (in.a == x && in.b == y) || (in.a == y && in.b == x); };
@@ -427,6 +429,46 @@ static int match_fast_epilogue(const EProgram& p, float* c) {
       k[5].op == EOp::MULF && uses(k[5], 1, k[4].dst) && k[6].op == EOp::MULF && uses(k[6], k[5].dst, 0) &&
       p.result == k[6].dst)
     return kern::FAST_SIGMOID_MUL;
+  // (acc + aux0) + aux1, or (acc + aux1) + aux0: a bias and a residual
+  if (p.n_args == 3 && k.size() == 2 && k[0].op == EOp::ADDF && k[1].op == EOp::ADDF && p.result == k[1].dst) {
+    if (uses(k[0], 0, 1) && uses(k[1], k[0].dst, 2)) return kern::FAST_ADD_ADD;
+    if (uses(k[0], 0, 2) && uses(k[1], k[0].dst, 1)) {
+      if (swap_aux) *swap_aux = true;
+      return kern::FAST_ADD_ADD;
+    }
+  }
+  // exact GELU after a bias: t = acc + aux0, (t * (erf(t / c) + 1)) * 0.5, the
+  // constants wherever the code holds them; traced back from the result
+  if (p.n_args == 2 && k.size() == 9) {
+    auto def = [&](int r) -> const EInstr* {
+      for (const auto& in : k)
+        if (in.dst == r) return &in;
+      return nullptr;
+    };
+    auto is_const = [&](int r, double v) {
+      const EInstr* d = def(r);
+      return d && d->op == EOp::CONST && d->fimm == v;
+    };
+    const EInstr* R = def(p.result);
+    if (!R || R->op != EOp::MULF) return kern::FAST_NONE;
+    const int w = is_const(R->b, 0.5) ? R->a : is_const(R->a, 0.5) ? R->b : -1;
+    const EInstr* W = def(w);
+    if (!W || W->op != EOp::MULF) return kern::FAST_NONE;
+    for (int side = 0; side < 2; ++side) {
+      const EInstr* T = def(side ? W->b : W->a);
+      const EInstr* V = def(side ? W->a : W->b);
+      if (!T || !V || T->op != EOp::ADDF || !uses(*T, 0, 1) || V->op != EOp::ADDF) continue;
+      const int e = is_const(V->b, 1.0) ? V->a : is_const(V->a, 1.0) ? V->b : -1;
+      const EInstr* E = def(e);
+      if (!E || E->op != EOp::ERF) continue;
+      const EInstr* U = def(E->a);
+      if (!U || U->op != EOp::DIVF || U->a != T->dst) continue;
+      const EInstr* C = def(U->b);
+      if (!C || C->op != EOp::CONST) continue;
+      *c = (float)C->fimm;
+      return kern::FAST_GELU;
+    }
+  }
   return kern::FAST_NONE;
 }
 
@@ -611,8 +653,15 @@ kern::ConvGemmParams tc_params(Runtime& rt, int o, const Op& op) {
   }
   if (t.epi == kern::EPI_PROGRAM) {
     p.prog = to_device(t.prog);
-    p.fast = match_fast_epilogue(t.prog, &p.fast_c);
+    bool swap = false;
+    p.fast = match_fast_epilogue(t.prog, &p.fast_c, &swap);
     if (p.fast != kern::FAST_NONE) p.epi = kern::EPI_FAST;
+    if (swap) {  // the form adds aux 0 first
+      std::swap(p.aux[0], p.aux[1]);
+      std::swap(p.aux_sm[0], p.aux_sm[1]);
+      std::swap(p.aux_sn[0], p.aux_sn[1]);
+      for (int d = 0; d < 4; ++d) std::swap(p.aux_sb[0][d], p.aux_sb[1][d]);
+    }
   }
   p.status = rt.status();
   p.passes = rt.passes;

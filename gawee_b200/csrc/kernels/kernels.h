@@ -353,6 +353,8 @@ enum FastEpi : int {
   FAST_DIVC_ADD = 2,     // (acc / c) + aux0
   FAST_SIGMOID_MUL = 3,  // (aux0 * (1 / (1 + exp(-aux1)))) * acc
   FAST_MULC_ADD = 4,     // (acc * c) + aux0: acc / d with d a power of two, c = 1 / d (exact)
+  FAST_ADD_ADD = 5,      // (acc + aux0) + aux1: bias and residual
+  FAST_GELU = 6,         // (t * (erf(t / c) + 1)) * 0.5 with t = acc + aux0: bias and exact GELU
 };
 
 // ---------------------------------------------------------------------------

@@ -280,7 +280,7 @@ __device__ __forceinline__ void tile_epilogue(const ConvGemmParams& p, float (&a
     // 16-column chunk ahead when there is a single aux operand), computes
     // the chunk, and the warp stores it through the shared-memory
     // transpose (8 rows x 64 bytes per store instead of 32 rows x 16 bytes).
-    const bool two = p.fast == FAST_SIGMOID_MUL;
+    const bool two = p.fast == FAST_SIGMOID_MUL || p.fast == FAST_ADD_ADD;
     int64_t abase = 0, abase1 = 0;
     {
       uint32_t rem = (uint32_t)z;
@@ -318,14 +318,25 @@ __device__ __forceinline__ void tile_epilogue(const ConvGemmParams& p, float (&a
         }
         float o[16];
         if (two) {  // this chunk's second operand now; no prefetch (registers)
+          if (p.fast == FAST_SIGMOID_MUL) {
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {  // four values of the second operand live at a time
-            const float4 t = mrow ? __ldg(reinterpret_cast<const float4*>(arow1 + c0) + j) : make_float4(0, 0, 0, 0);
-            const float b1[4] = {t.x, t.y, t.z, t.w};
+            for (int j = 0; j < 4; ++j) {  // four values of the second operand live at a time
+              const float4 t = mrow ? __ldg(reinterpret_cast<const float4*>(arow1 + c0) + j) : make_float4(0, 0, 0, 0);
+              const float b1[4] = {t.x, t.y, t.z, t.w};
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-b1[e])));
-              acc[c0 + 4 * j + e] = __fmul_rn(__fmul_rn(a[4 * j + e], sg), acc[c0 + 4 * j + e]);
+              for (int e = 0; e < 4; ++e) {
+                const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-b1[e])));
+                acc[c0 + 4 * j + e] = __fmul_rn(__fmul_rn(a[4 * j + e], sg), acc[c0 + 4 * j + e]);
+              }
+            }
+          } else {  // FAST_ADD_ADD
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float4 t = mrow ? __ldg(reinterpret_cast<const float4*>(arow1 + c0) + j) : make_float4(0, 0, 0, 0);
+              const float b1[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                acc[c0 + 4 * j + e] = __fadd_rn(__fadd_rn(acc[c0 + 4 * j + e], a[4 * j + e]), b1[e]);
             }
           }
           if (c0 + 16 < HB) {
@@ -348,10 +359,17 @@ __device__ __forceinline__ void tile_epilogue(const ConvGemmParams& p, float (&a
             const float c = p.fast_c;
 #pragma unroll
             for (int j = 0; j < 16; ++j) acc[c0 + j] = __fadd_rn(__fdiv_rn(acc[c0 + j], c), a[j]);
-          } else {
+          } else if (p.fast == FAST_MULC_ADD) {
             const float c = p.fast_c;
 #pragma unroll
             for (int j = 0; j < 16; ++j) acc[c0 + j] = __fadd_rn(__fmul_rn(acc[c0 + j], c), a[j]);
+          } else {  // FAST_GELU
+            const float c = p.fast_c;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float t = __fadd_rn(acc[c0 + j], a[j]);
+              acc[c0 + j] = __fmul_rn(__fmul_rn(t, __fadd_rn(erff(__fdiv_rn(t, c)), 1.0f)), 0.5f);
+            }
           }
           if (c0 + 16 < HB) {
 #pragma unroll
@@ -416,7 +434,8 @@ __device__ __forceinline__ void tile_epilogue(const ConvGemmParams& p, float (&a
       // a time, their operand loads all in flight before they are used.
       bool aux_vec = p.aux_sn[0] == 1 && nb0 + HB <= p.N &&
                      ((reinterpret_cast<uintptr_t>(p.aux[0] + aux_row[0] + nb0) & 15) == 0);
-      if (p.fast == FAST_SIGMOID_MUL)
+      const bool two = p.fast == FAST_SIGMOID_MUL || p.fast == FAST_ADD_ADD;
+      if (two)
         aux_vec = aux_vec && p.aux_sn[1] == 1 && ((reinterpret_cast<uintptr_t>(p.aux[1] + aux_row[1] + nb0) & 15) == 0);
 #pragma unroll
       for (int c0 = 0; c0 < HB; c0 += 8) {
@@ -426,7 +445,7 @@ __device__ __forceinline__ void tile_epilogue(const ConvGemmParams& p, float (&a
           const float4 u = __ldg(q0), v = __ldg(q0 + 1);
           a0[0] = u.x; a0[1] = u.y; a0[2] = u.z; a0[3] = u.w;
           a0[4] = v.x; a0[5] = v.y; a0[6] = v.z; a0[7] = v.w;
-          if (p.fast == FAST_SIGMOID_MUL) {
+          if (two) {
             const float4* q1 = reinterpret_cast<const float4*>(p.aux[1] + aux_row[1] + nb0 + c0);
             const float4 w = __ldg(q1), x = __ldg(q1 + 1);
             a1[0] = w.x; a1[1] = w.y; a1[2] = w.z; a1[3] = w.w;
@@ -441,7 +460,7 @@ __device__ __forceinline__ void tile_epilogue(const ConvGemmParams& p, float (&a
             const int64_t n = nb0 + c0 + j;
             const bool in = n < p.N;
             a0[j] = in ? __ldg(p.aux[0] + aux_row[0] + n * p.aux_sn[0]) : 0.f;
-            a1[j] = (in && p.fast == FAST_SIGMOID_MUL) ? __ldg(p.aux[1] + aux_row[1] + n * p.aux_sn[1]) : 0.f;
+            a1[j] = (in && two) ? __ldg(p.aux[1] + aux_row[1] + n * p.aux_sn[1]) : 0.f;
           }
         }
         float xs[8];
@@ -462,6 +481,16 @@ __device__ __forceinline__ void tile_epilogue(const ConvGemmParams& p, float (&a
           const float c = p.fast_c;
 #pragma unroll
           for (int j = 0; j < 8; ++j) o[j] = __fadd_rn(__fmul_rn(xs[j], c), a0[j]);
+        } else if (p.fast == FAST_ADD_ADD) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = __fadd_rn(__fadd_rn(xs[j], a0[j]), a1[j]);
+        } else if (p.fast == FAST_GELU) {
+          const float c = p.fast_c;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float t = __fadd_rn(xs[j], a0[j]);
+            o[j] = __fmul_rn(__fmul_rn(t, __fadd_rn(erff(__fdiv_rn(t, c)), 1.0f)), 0.5f);
+          }
         } else {
 #pragma unroll
           for (int j = 0; j < 8; ++j) {

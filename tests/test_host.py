@@ -138,6 +138,33 @@ def test_plan_flags_interpreter_fallbacks():
     assert "matmul+tanh [interp epilogue]" in _plan(build(g_)[0])
 
 
+def test_plan_matches_gelu_epilogue_exactly():
+    # bias + GELU runs as a specialised epilogue only when the program is exactly
+    # (t * (erf(t / c) + 1)) * 0.5, in any operand order of the commutative steps
+    from tests.helpers import build, rand_input
+    F = "f32"
+
+    def gelu(form):
+        def g_(g):
+            t = g.add(g.matmul(rand_input(g, (37, 64), 1), rand_input(g, (64, 48), 2)), rand_input(g, (48,), 3))
+            c = g.const(1.4142135381698608, F)
+            if form == "standard":
+                y = g.mul(g.mul(t, g.add(g.erf(g.div(t, c)), g.const(1.0, F))), g.const(0.5, F))
+            elif form == "swapped":
+                y = g.mul(g.const(0.5, F), g.mul(g.add(g.const(1.0, F), g.erf(g.div(t, c))), t))
+            elif form == "wrong_constant":
+                y = g.mul(g.mul(t, g.add(g.erf(g.div(t, c)), g.const(2.0, F))), g.const(0.5, F))
+            else:  # c / t: not GELU
+                y = g.mul(g.mul(t, g.add(g.erf(g.div(c, t)), g.const(1.0, F))), g.const(0.5, F))
+            return [y]
+        return _plan(build(g_)[0])
+    for form in ("standard", "swapped"):
+        s = gelu(form)
+        assert "erf" in s and "[interp" not in s, (form, s)
+    for form in ("wrong_constant", "divisor_swapped"):
+        assert "[interp epilogue]" in gelu(form), form
+
+
 def test_plan_decode_step():
     # the KV-cache decode step: concat of past and new key/value, one query row,
     # attention, RoPE and RMSNorm still fused; logits + 12 present tensors out
